@@ -1,0 +1,9 @@
+// bybycuda.cu - the single translation unit of libbybycuda.so (the routes share the device
+// error word, so they are compiled together).
+#include "abi.cu"
+#include "simt.cu"
+#include "gemv.cu"
+#include "tc.cu"
+#include "vm.cu"
+#include "session.cu"
+#include "shard.cu"

@@ -1,0 +1,181 @@
+// common.cuh - shared host/device helpers of libbybycuda.so: status reporting, the
+// device-side error word, and thin wrappers over the sm_100a PTX this library issues
+// (mbarrier, TMA bulk-tensor copies, globaltimer).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/bybycuda.h"
+
+namespace bybycu {
+
+// ---------------------------------------------------------------------------------------
+// Host-side status: the last failure of this host thread.
+// ---------------------------------------------------------------------------------------
+int set_error(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+void clear_error();
+
+#define BYBYCU_CUDA_TRY(expr)                                          \
+    do {                                                               \
+        cudaError_t e__ = (expr);                                      \
+        if (e__ != cudaSuccess) return ::bybycu::cuda_fail(e__, #expr); \
+    } while (0)
+
+// Launch check: catches configuration errors of the launch just issued.
+#define BYBYCU_LAUNCH_CHECK(name)                                      \
+    do {                                                               \
+        cudaError_t e__ = cudaGetLastError();                          \
+        if (e__ != cudaSuccess) return ::bybycu::cuda_fail(e__, name); \
+    } while (0)
+
+// ---------------------------------------------------------------------------------------
+// Device-side error word.  Kernels never trap: a wait that runs out of time records a code
+// here and the kernel returns; bybycu_device_error() reads and clears it.
+// ---------------------------------------------------------------------------------------
+enum DeviceErr : uint32_t {
+    kDevErrNone = 0,
+    kDevErrFullWait = 1,    // consumer waited too long for a TMA stage
+    kDevErrEmptyWait = 2,   // producer waited too long for a free stage
+    kDevErrDrainWait = 3,   // producer could not drain its copies after an error
+    kDevErrMmaWait = 4,     // tensor-core commit never arrived
+    kDevErrPeerWait = 5,    // a peer rank's signal never arrived
+    kDevErrTmemAlloc = 6,   // tensor memory allocation failed
+};
+
+__device__ uint32_t g_device_error = 0;
+
+// Wall-clock bound of every device-side wait (nanoseconds of %globaltimer).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void record_device_error(uint32_t code) {
+    atomicCAS(&g_device_error, 0u, code);
+}
+
+// ---------------------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on phase `parity`: true when the phase completed, false (error recorded)
+// when kWaitLimitNs passed first.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(err);
+            return false;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// TMA (bulk tensor copies, no multicast)
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorMap* map,
+                                                 uint64_t* bar, int32_t c0, int32_t c1,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Named barrier among `count` threads (a subset of the CTA).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// Host helpers shared by the launchers
+// ---------------------------------------------------------------------------------------
+struct DeviceInfo {
+    int device = -1;
+    int sm_count = 0;
+    int max_smem_optin = 0;
+    int cc_major = 0, cc_minor = 0;
+};
+int current_device_info(DeviceInfo* info);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+int encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                         uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                         uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle,
+                         CUtensorMapL2promotion promo);
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace bybycu

@@ -1,0 +1,198 @@
+// shard.cu - column sharding of the tile GEMM over GPUs.
+//
+// The split is distributed.nim's partition (distributed.nim:109-135): largest remainder
+// over equal weights, computed in float64 exactly as the reference does, taken over blocks
+// of `align` columns.  The exchange is device-side: each rank computes its column slice
+// and its kernels store the slice straight into every peer's output over NVLink (peer
+// pointers), then raise one counter per CTA in every rank's signal array; a one-CTA kernel
+// waits, bounded, for every rank's counters of this epoch.  No collective library is on the
+// data path and no load reads another GPU's memory.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "kernels.h"
+
+namespace bybycu {
+
+int check_tile_gemm(int fmt, int M, int K, int N, int64_t x_len, int64_t packed_len, int64_t scale_base,
+                    int64_t lut_len, int64_t lut_base, int64_t out_len);
+int choose_route(const GemmArgs& a, int requested, int* route);
+int run_gemm(const GemmArgs& a, int route);
+
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr int kExchangeCtas = 32;
+
+struct PeerSet {
+    float* out[kMaxRanks];
+    uint32_t* sig[kMaxRanks];
+};
+
+// Largest-remainder partition of `length` items over `world` equal weights
+// (distributed.nim:109-135): floor of length * (1 / world), then one more to the largest
+// remainders, first index first on ties.
+std::vector<int> partition_equal(int length, int world) {
+    std::vector<int> out(world, 0);
+    std::vector<double> rem(world, 0.0);
+    const double total = static_cast<double>(world);
+    int assigned = 0;
+    for (int i = 0; i < world; ++i) {
+        const double exact = static_cast<double>(length) * (1.0 / total);
+        out[i] = static_cast<int>(std::floor(exact));
+        rem[i] = exact - static_cast<double>(out[i]);
+        assigned += out[i];
+    }
+    while (assigned < length) {
+        int best = -1;
+        for (int i = 0; i < world; ++i)
+            if (best < 0 || rem[i] > rem[best]) best = i;
+        if (best < 0) break;
+        ++out[best];
+        rem[best] = -1.0;
+        ++assigned;
+    }
+    return out;
+}
+
+// Copies out[:, n0:n1) of this rank into every other rank's out, then signals.
+__global__ void __launch_bounds__(256) exchange_kernel(const float* __restrict__ out, int M, int N, int n0, int n1,
+                                                       PeerSet peers, int world, int rank) {
+    const int cols = n1 - n0;
+    const int64_t total = static_cast<int64_t>(M) * cols;
+    const bool vec = ((n0 | cols | N) & 3) == 0;
+    if (vec) {
+        const int cols4 = cols / 4;
+        const int64_t total4 = static_cast<int64_t>(M) * cols4;
+        for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total4;
+             i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+            const int64_t m = i / cols4;
+            const int64_t c = (i % cols4) * 4;
+            const int64_t off = m * N + n0 + c;
+            const float4 v = *reinterpret_cast<const float4*>(out + off);
+            for (int r = 0; r < world; ++r)
+                if (r != rank) *reinterpret_cast<float4*>(peers.out[r] + off) = v;
+        }
+    } else {
+        for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+             i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+            const int64_t m = i / cols;
+            const int64_t off = m * N + n0 + (i % cols);
+            const float v = out[off];
+            for (int r = 0; r < world; ++r)
+                if (r != rank) peers.out[r][off] = v;
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int r = 0; r < world; ++r) atomicAdd_system(peers.sig[r] + rank, 1u);
+}
+
+// Waits until every rank's counter in this rank's signal array reached the target of this
+// epoch.  epoch == 0: the epoch is kept on the device (sig[kMaxRanks] counts this rank's
+// completed exchanges), so the launch sequence can be captured in a CUDA graph and replayed.
+__global__ void wait_kernel(uint32_t* sig, int world, uint32_t epoch, uint32_t per_epoch) {
+    __shared__ uint32_t s_epoch;
+    if (threadIdx.x == 0) s_epoch = epoch ? epoch : sig[kMaxRanks] + 1;
+    __syncthreads();
+    const uint32_t target = s_epoch * per_epoch;
+    const int r = threadIdx.x;
+    if (r < world) {
+        const uint64_t t0 = globaltimer_ns();
+        for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(sig + r) : "memory");
+            if (static_cast<int32_t>(v - target) >= 0) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                record_device_error(kDevErrPeerWait);
+                break;
+            }
+            __nanosleep(128);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && epoch == 0) sig[kMaxRanks] = s_epoch;
+}
+
+}  // namespace
+}  // namespace bybycu
+
+using namespace bybycu;
+
+extern "C" {
+
+int bybycu_ipc_handle(const void* dptr, uint8_t handle[64]) {
+    if (!dptr || !handle) return set_error(BYBYCU_ERR_ARGS, "ipc handle: bad arguments");
+    cudaIpcMemHandle_t h;
+    BYBYCU_CUDA_TRY(cudaIpcGetMemHandle(&h, const_cast<void*>(dptr)));
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    memcpy(handle, &h, 64);
+    return BYBYCU_OK;
+}
+
+int bybycu_ipc_open(const uint8_t handle[64], void** dptr) {
+    if (!dptr || !handle) return set_error(BYBYCU_ERR_ARGS, "ipc open: bad arguments");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, 64);
+    BYBYCU_CUDA_TRY(cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess));
+    return BYBYCU_OK;
+}
+
+int bybycu_ipc_close(void* dptr) {
+    if (dptr) BYBYCU_CUDA_TRY(cudaIpcCloseMemHandle(dptr));
+    return BYBYCU_OK;
+}
+
+int bybycu_shard_range(int N, int world, int rank, int align, int* n0, int* n1) {
+    if (!n0 || !n1 || N < 0 || world < 1 || rank < 0 || rank >= world || align < 1)
+        return set_error(BYBYCU_ERR_ARGS, "shard range: bad arguments");
+    const int blocks = static_cast<int>(ceil_div(N, align));
+    const std::vector<int> parts = partition_equal(blocks, world);
+    int start = 0;
+    for (int r = 0; r < rank; ++r) start += parts[r];
+    *n0 = std::min(N, start * align);
+    *n1 = std::min(N, (start + parts[rank]) * align);
+    return BYBYCU_OK;
+}
+
+int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1, const void* x, int x_dtype,
+                               const void* packed, int64_t packed_len, int64_t scale_base, const float* lut,
+                               int64_t lut_len, int64_t lut_base, void* out, void* const* peer_out,
+                               uint32_t* const* peer_signal, int world, int rank, uint32_t epoch, void* stream) {
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_out || !peer_signal || !out || !x ||
+        !packed)
+        return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: bad arguments");
+    if (n0 < 0 || n1 > N || n0 > n1) return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: bad column range");
+    PeerSet peers{};
+    for (int r = 0; r < world; ++r) {
+        if (!peer_out[r] || !peer_signal[r]) return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: peer %d missing", r);
+        peers.out[r] = static_cast<float*>(peer_out[r]);
+        peers.sig[r] = peer_signal[r];
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int cols = n1 - n0;
+    if (cols > 0) {
+        if (int rc = check_tile_gemm(fmt, M, K, cols, static_cast<int64_t>(M) * K, packed_len, scale_base, lut_len,
+                                     lut_base, static_cast<int64_t>(M) * cols))
+            return rc;
+        GemmArgs a;
+        a.fmt = fmt; a.M = M; a.K = K; a.N = cols;
+        a.x = x; a.x_dtype = x_dtype;
+        a.packed = static_cast<const uint8_t*>(packed); a.packed_len = packed_len; a.scale_base = scale_base;
+        a.lut = lut ? lut + lut_base : nullptr;
+        a.out = out; a.out_dtype = BYBYCU_DT_F32; a.out_ld = N; a.out_col0 = n0;
+        a.stream = s;
+        int route = 0;
+        if (int rc = choose_route(a, BYBYCU_ROUTE_AUTO, &route)) return rc;
+        if (int rc = run_gemm(a, route)) return rc;
+    }
+    exchange_kernel<<<kExchangeCtas, 256, 0, s>>>(static_cast<const float*>(out), M, N, n0, n1, peers, world, rank);
+    BYBYCU_LAUNCH_CHECK("exchange_kernel");
+    wait_kernel<<<1, 32, 0, s>>>(peer_signal[rank], world, epoch, static_cast<uint32_t>(kExchangeCtas));
+    BYBYCU_LAUNCH_CHECK("wait_kernel");
+    return BYBYCU_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,346 @@
+"""The `cuda` GpuBackend of BybyLang's operator API for the tile-GEMM path (gpubackend.nim),
+implemented over libbybycuda.so.
+
+What changes against the reference: ``parseBackend("cuda")`` returns a real ``gbCuda`` (the
+reference remaps it to Vulkan, gpubackend.nim:107-121), the cuda path forces
+``gForbidCpuFallback`` on, and every session op of this path runs hand-written sm_100a
+kernels.  There is no Vulkan, Metal or CPU dispatch here: a failure raises (the
+``handleGpuFailure`` policy with fallback forbidden, gpubackend.nim:80-105).
+
+Besides the session API, two tensor-level entry points serve Python callers:
+``tile_gemm`` (device tensors in, device tensor out, asynchronous on the current stream)
+and ``Q4B32Weights`` (weights resident on the device, the residentUploadQ4 role).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import os
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _lib
+from ._lib import BybyCudaError, call, check, load
+from .session_vm import (TileFormatF16, TileFormatFp4Km, TileFormatQ4B32, VmProgram,
+                         tileWeightBytes)
+
+
+class GpuBackend(enum.IntEnum):
+    """gpubackend.nim:55-57."""
+    gbAuto = 0
+    gbCpu = 1
+    gbCuda = 2
+    gbMetal = 3
+    gbVulkan = 4
+
+    def __str__(self) -> str:
+        return {0: "auto", 1: "cpu", 2: "cuda", 3: "metal", 4: "vulkan"}[int(self)]
+
+
+gForbidCpuFallback = False
+
+
+def setForbidCpuFallback(forbid: bool) -> None:
+    """gpubackend.nim:75-76.  The cuda path turns it on by itself and keeps it on."""
+    global gForbidCpuFallback
+    gForbidCpuFallback = bool(forbid)
+
+
+def parseBackend(s: str) -> GpuBackend:
+    """gpubackend.nim:107-114, with `cuda` a real backend."""
+    v = s.strip().lower()
+    table = {"cuda": GpuBackend.gbCuda, "metal": GpuBackend.gbMetal, "cpu": GpuBackend.gbCpu,
+             "vulkan": GpuBackend.gbVulkan, "auto": GpuBackend.gbAuto}
+    if v not in table:
+        raise ValueError(f"unknown BybyLang backend: {s}")
+    return table[v]
+
+
+def normalizeBackend(b: GpuBackend) -> GpuBackend:
+    """gpubackend.nim:116-121 without the cuda -> vulkan remap."""
+    return b
+
+
+def detectBackend() -> GpuBackend:
+    """gbCuda when an sm_100 device is present; this package provides no other backend."""
+    n = C.c_int(0)
+    call("bybycu_device_count", C.byref(n))
+    if n.value == 0:
+        raise BybyCudaError(_lib.ERR_NODEV, "no CUDA device: this package has no CPU, Vulkan or Metal path")
+    return GpuBackend.gbCuda
+
+
+def _chosen(backend: GpuBackend) -> GpuBackend:
+    b = detectBackend() if backend == GpuBackend.gbAuto else backend
+    if b != GpuBackend.gbCuda:
+        raise BybyCudaError(_lib.ERR_ARGS, f"backend '{b}' is not provided by bybylang_b200 (only 'cuda')")
+    return b
+
+
+_initialised: set = set()
+
+
+def ensureGpuInit(backend: GpuBackend = GpuBackend.gbCuda, device: int | None = None) -> bool:
+    """Selects the device (BYBY_CUDA_DEVICE, default 0) and forbids CPU fallback."""
+    _chosen(backend)
+    dev = int(os.environ.get("BYBY_CUDA_DEVICE", "0")) if device is None else device
+    call("bybycu_init", dev)
+    _initialised.add(dev)
+    setForbidCpuFallback(True)
+    return True
+
+
+def handleGpuFailure(backend: GpuBackend, opName: str, e: Exception):
+    """gpubackend.nim:80-105 with fallback forbidden on this path: always raises."""
+    msg = f"[GPU] backend '{backend}' failed during '{opName}' ({e})"
+    raise BybyCudaError(getattr(e, "code", _lib.ERR_CUDA),
+                        msg + ". CPU fallback is forbidden (gForbidCpuFallback=true).") from e
+
+
+# --------------------------------------------------------------------------------------
+# Session API (gpubackend.nim:1042-2722)
+# --------------------------------------------------------------------------------------
+
+@dataclass
+class CudaResidentTensor:
+    """gpubackend.nim:23-27: a device pointer and its size (here in bytes)."""
+    dptr: int = 0
+    n: int = 0
+
+
+@dataclass
+class SessionHandle:
+    kind: GpuBackend = GpuBackend.gbCuda
+    cudaHandle: CudaResidentTensor = field(default_factory=CudaResidentTensor)
+
+    @property
+    def ptr(self) -> int:
+        return self.cudaHandle.dptr
+
+
+def sessionBegin(backend: GpuBackend) -> bool:
+    _chosen(backend)
+    if not _initialised:
+        ensureGpuInit(backend)
+    try:
+        call("bybycu_session_begin")
+    except BybyCudaError as e:
+        handleGpuFailure(backend, "sessionBegin", e)
+    return True
+
+
+def sessionEnd(backend: GpuBackend) -> bool:
+    _chosen(backend)
+    try:
+        call("bybycu_session_end")
+    except BybyCudaError as e:
+        handleGpuFailure(backend, "sessionEnd", e)
+    return True
+
+
+def sessionUpload(backend: GpuBackend, data) -> SessionHandle:
+    """gpubackend.nim:1133: the bytes of `data` (float32 words or any array) on the device."""
+    _chosen(backend)
+    a = np.ascontiguousarray(data)
+    h = C.c_void_p()
+    call("bybycu_session_upload", a.ctypes.data_as(C.c_void_p), a.nbytes, C.byref(h))
+    return SessionHandle(GpuBackend.gbCuda, CudaResidentTensor(h.value, a.nbytes))
+
+
+def sessionAllocScratch(backend: GpuBackend, n: int) -> SessionHandle:
+    _chosen(backend)
+    h = C.c_void_p()
+    call("bybycu_session_alloc_scratch", int(n), C.byref(h))
+    return SessionHandle(GpuBackend.gbCuda, CudaResidentTensor(h.value, int(n) * 4))
+
+
+def sessionRead(backend: GpuBackend, h: SessionHandle, n: int) -> np.ndarray:
+    _chosen(backend)
+    out = np.zeros(int(n), np.float32)
+    call("bybycu_session_read", C.c_void_p(h.ptr), out.ctypes.data_as(C.c_void_p), int(n))
+    return out
+
+
+def sessionFree(backend: GpuBackend, h: SessionHandle) -> None:
+    _chosen(backend)
+    if h.ptr:
+        call("bybycu_session_free", C.c_void_p(h.ptr))
+    h.cudaHandle = CudaResidentTensor()
+
+
+def _gemm(name: str, backend: GpuBackend, args, c: SessionHandle, M: int, N: int) -> bool:
+    _chosen(backend)
+    if not c.ptr:
+        c.cudaHandle = sessionAllocScratch(backend, M * N).cudaHandle
+    try:
+        call(name, *args)
+    except BybyCudaError as e:
+        handleGpuFailure(backend, name, e)
+    return True
+
+
+def sessionFp4GemmTensorCore(backend, a: SessionHandle, w: SessionHandle, lut: SessionHandle,
+                             c: SessionHandle, M: int, K: int, N: int) -> bool:
+    """gpubackend.nim:1442-1449: FP4-KM tile GEMM on the tensor-core routes."""
+    if not c.ptr:
+        c.cudaHandle = sessionAllocScratch(backend, M * N).cudaHandle
+    return _gemm("bybycu_session_fp4_gemm", backend,
+                 (C.c_void_p(a.ptr), C.c_void_p(w.ptr), C.c_void_p(lut.ptr), C.c_void_p(c.ptr), M, K, N, 1),
+                 c, M, N)
+
+
+def sessionFp4GemmTiledEnc(backend, a: SessionHandle, w: SessionHandle, lut: SessionHandle,
+                           c: SessionHandle, M: int, K: int, N: int) -> bool:
+    """gpubackend.nim:1465-1473: the FP32 register-tile route."""
+    if not c.ptr:
+        c.cudaHandle = sessionAllocScratch(backend, M * N).cudaHandle
+    return _gemm("bybycu_session_fp4_gemm", backend,
+                 (C.c_void_p(a.ptr), C.c_void_p(w.ptr), C.c_void_p(lut.ptr), C.c_void_p(c.ptr), M, K, N, 0),
+                 c, M, N)
+
+
+def sessionF16GemmTile(backend, a: SessionHandle, w: SessionHandle, c: SessionHandle, M: int, K: int,
+                       N: int, tensorCore: bool) -> bool:
+    """gpubackend.nim:1475-1482."""
+    if not c.ptr:
+        c.cudaHandle = sessionAllocScratch(backend, M * N).cudaHandle
+    return _gemm("bybycu_session_f16_gemm", backend,
+                 (C.c_void_p(a.ptr), C.c_void_p(w.ptr), C.c_void_p(c.ptr), M, K, N, int(bool(tensorCore))),
+                 c, M, N)
+
+
+def sessionQ4B32Gemm(backend, a: SessionHandle, w: SessionHandle, c: SessionHandle, M: int, K: int,
+                     N: int, tensorCore: bool = True) -> bool:
+    """Format 2 (Q4B32) through the same session encoder shape."""
+    if not c.ptr:
+        c.cudaHandle = sessionAllocScratch(backend, M * N).cudaHandle
+    return _gemm("bybycu_session_q4b32_gemm", backend,
+                 (C.c_void_p(a.ptr), C.c_void_p(w.ptr), C.c_void_p(c.ptr), M, K, N, int(bool(tensorCore))),
+                 c, M, N)
+
+
+def sessionTileGemmReady(backend, f16: bool, tensorCore: bool, fmt: int | None = None) -> bool:
+    """gpubackend.nim:1484-1488: the exact-data parity gate, once per process."""
+    _chosen(backend)
+    if not _initialised:
+        ensureGpuInit(backend)
+    f = fmt if fmt is not None else (TileFormatF16 if f16 else TileFormatFp4Km)
+    r = C.c_int(0)
+    call("bybycu_tile_gemm_ready", f, int(bool(tensorCore)), C.byref(r))
+    return bool(r.value)
+
+
+def sessionMicroVmEnc(backend, code, mem: SessionHandle, nThreads: int, tgFloats: int, tgSize: int,
+                      packed: SessionHandle | None = None, lut: SessionHandle | None = None,
+                      inp: SessionHandle | None = None) -> bool:
+    """gpubackend.nim:1065-1081 for tile-GEMM / shape-op programs.  With only `mem` the slots
+    alias it as in nimf_cpu_vm_run (cpu_vm.c:822-828); the optional slots bind u8, lut and
+    input separately as nimf_cpu_vm_run_slots does."""
+    _chosen(backend)
+    words = np.ascontiguousarray(code.words if isinstance(code, VmProgram) else code, np.uint32)
+    pk = packed if packed is not None else mem
+    lt = lut if lut is not None else mem
+    err = C.create_string_buffer(256)
+    rc = load().bybycu_vm_run_slots(
+        words.ctypes.data_as(C.POINTER(C.c_uint32)), len(words), C.c_void_p(mem.ptr), mem.cudaHandle.n // 4,
+        C.c_void_p(pk.ptr), pk.cudaHandle.n, C.c_void_p(lt.ptr), lt.cudaHandle.n // 4,
+        C.c_void_p(inp.ptr if inp is not None else 0), (inp.cudaHandle.n // 4) if inp is not None else 0,
+        nThreads, tgFloats, tgSize, err, 256, None)
+    if rc != 0:
+        handleGpuFailure(GpuBackend.gbCuda, "sessionMicroVmEnc", BybyCudaError(rc, err.value.decode()))
+    return True
+
+
+# --------------------------------------------------------------------------------------
+# Tensor-level entry points (torch device tensors; plumbing only - the math is the library's)
+# --------------------------------------------------------------------------------------
+
+def _ptr(t) -> C.c_void_p:
+    return C.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _dtype_code(t) -> int:
+    import torch
+    if t.dtype == torch.float32:
+        return _lib.DT_F32
+    if t.dtype == torch.bfloat16:
+        return _lib.DT_BF16
+    raise BybyCudaError(_lib.ERR_ARGS, f"unsupported element type {t.dtype} (float32 or bfloat16)")
+
+
+def _stream_ptr(stream) -> C.c_void_p:
+    import torch
+    s = torch.cuda.current_stream() if stream is None else stream
+    return C.c_void_p(s.cuda_stream)
+
+
+def tile_gemm(fmt: int, x, packed, out, *, M: int, K: int, N: int, scale_base: int = 0, lut=None,
+              lut_base: int = 0, route: int = _lib.ROUTE_AUTO, stream=None):
+    """out[M, N] = x[M, K] * dequant(W)^T for one OP_TILE_GEMM on device tensors.
+
+    x: float32/bfloat16 [M, K]; packed: uint8 weight slot; out: float32/bfloat16 [M, N];
+    lut: float32 table slot (format 0).  Asynchronous on `stream` (default: current)."""
+    check(load().bybycu_tile_gemm(
+        fmt, M, K, N, _ptr(x), _dtype_code(x), x.numel(), _ptr(packed), packed.numel() * packed.element_size(),
+        scale_base, _ptr(lut), 0 if lut is None else lut.numel(), lut_base, _ptr(out), _dtype_code(out),
+        out.numel(), route, _stream_ptr(stream)))
+    return out
+
+
+def route_for(fmt: int, M: int, K: int, N: int, x_dtype: int = _lib.DT_BF16) -> int:
+    r = C.c_int(0)
+    call("bybycu_route_for", fmt, M, K, N, x_dtype, C.byref(r))
+    return r.value
+
+
+def dequant(fmt: int, packed, w_out, *, K: int, N: int, scale_base: int = 0, lut=None, lut_base: int = 0,
+            stream=None):
+    check(load().bybycu_dequant(fmt, K, N, _ptr(packed), packed.numel() * packed.element_size(), scale_base,
+                                _ptr(lut), 0 if lut is None else lut.numel(), lut_base, _ptr(w_out),
+                                _stream_ptr(stream)))
+    return w_out
+
+
+class Q4B32Weights:
+    """Q4B32 weights resident on one device (the residentUploadQ4 role,
+    gpubackend.nim:2883-2919): one uint8 slot holding the nibbles [N, K/2] in the tile layout
+    followed by the fp16 scales [N, K/32] at byte ``scale_base`` (16-byte aligned)."""
+
+    def __init__(self, nibbles, scales, device=None):
+        import torch
+        nib = torch.as_tensor(nibbles)
+        sc = torch.as_tensor(scales)
+        if nib.dtype != torch.uint8 or nib.dim() != 2:
+            raise BybyCudaError(_lib.ERR_ARGS, "nibbles must be uint8 [N, K/2]")
+        self.N, half = nib.shape
+        self.K = half * 2
+        if self.K % 32 or tuple(sc.shape) != (self.N, self.K // 32):
+            raise BybyCudaError(_lib.ERR_SHAPE, f"unsupported tile GEMM shape K={self.K} N={self.N}")
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        nb = self.N * half
+        self.scale_base = (nb + 15) // 16 * 16
+        self.packed = torch.zeros(self.scale_base + sc.numel() * 2, dtype=torch.uint8, device=dev)
+        self.packed[:nb].copy_(nib.reshape(-1).to(dev))
+        s16 = sc.reshape(-1).view(torch.int16) if sc.dtype in (torch.float16, torch.int16) else \
+            sc.reshape(-1).to(torch.float16).view(torch.int16)
+        self.packed[self.scale_base:].copy_(s16.to(dev).view(torch.uint8))
+
+    def matmul(self, x, out=None, *, route: int = _lib.ROUTE_AUTO, stream=None):
+        """out[M, N] = x[M, K] * W^T (sessionMatmulQ4's role for this format)."""
+        import torch
+        M = x.shape[0]
+        if out is None:
+            out = torch.empty(M, self.N, dtype=torch.float32, device=x.device)
+        return tile_gemm(TileFormatQ4B32, x, self.packed, out, M=M, K=self.K, N=self.N,
+                         scale_base=self.scale_base, route=route, stream=stream)
+
+
+__all__ = [
+    "GpuBackend", "parseBackend", "normalizeBackend", "detectBackend", "ensureGpuInit",
+    "setForbidCpuFallback", "gForbidCpuFallback", "handleGpuFailure", "SessionHandle",
+    "CudaResidentTensor", "sessionBegin", "sessionEnd", "sessionUpload", "sessionAllocScratch",
+    "sessionRead", "sessionFree", "sessionFp4GemmTensorCore", "sessionFp4GemmTiledEnc",
+    "sessionF16GemmTile", "sessionQ4B32Gemm", "sessionTileGemmReady", "sessionMicroVmEnc",
+    "tile_gemm", "route_for", "dequant", "Q4B32Weights", "tileWeightBytes", "TileFormatQ4B32",
+]

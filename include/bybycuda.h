@@ -1,0 +1,224 @@
+/* bybycuda.h - C ABI of libbybycuda.so, the B200 (sm_100a) implementation of BybyLang's
+ * 4-bit block-quantized tile-GEMM / GEMV path.
+ *
+ * Conventions (those of the reference's CPU C ABI, backends/cpu/cpu_kernels.h:39-121):
+ *   - plain C types only: device buffers are `void*` device pointers (the value a
+ *     CudaResidentTensor.dptr carries, gpubackend.nim:23-27), streams are `void*`
+ *     (a cudaStream_t; NULL = the legacy default stream);
+ *   - lengths are in elements of the slot's type, the packed-weight slot in bytes;
+ *   - every `int` return is 0 on success or a negative BYBYCU_ERR_* code, and the message
+ *     of the last failure on the calling host thread is copied by bybycu_last_error();
+ *   - the caller owns every buffer and nothing is retained across calls (except the
+ *     session handles of the session API, which the caller frees);
+ *   - there is no CPU fallback: a call that cannot run on the GPU returns an error.
+ *
+ * Weight formats of OP_TILE_GEMM (micro_kernel/session_vm.nim:106-122) accepted here:
+ *   0 FP4-KM  nibble bytes [N, K/2] from byte 0 of the packed slot (byte j of a 32-value group:
+ *             low nibble = element j, high nibble = element j+16), scale bytes [N, K/32] at
+ *             byte scale_base, weight = lut[lut_base + nibble] * lut[lut_base + 16 + scale byte]
+ *   1 FP16    IEEE halves [N, K] from byte 0 of the packed slot; no table
+ *   2 Q4B32   nibbles as format 0 holding signed int4 (two's complement, [-8, 7]); one IEEE
+ *             half scale per 32-value block, [N, K/32] row-major at byte scale_base;
+ *             weight = (float)q * (float)scale.  (New: no reference counterpart.)
+ */
+#ifndef BYBYCUDA_H
+#define BYBYCUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BYBYCU_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define BYBYCU_API __attribute__((visibility("default")))
+#else
+#define BYBYCU_API
+#endif
+
+/* status codes */
+#define BYBYCU_OK 0
+#define BYBYCU_ERR_ARGS (-1)      /* null pointer, negative size, bad enum value */
+#define BYBYCU_ERR_SHAPE (-2)     /* shape or format the op does not support */
+#define BYBYCU_ERR_RANGE (-3)     /* a slot is too small for the shape */
+#define BYBYCU_ERR_CUDA (-4)      /* CUDA runtime failure */
+#define BYBYCU_ERR_NODEV (-5)     /* no usable sm_100 device */
+#define BYBYCU_ERR_PROGRAM (-6)   /* VM program not accepted by the CUDA executor */
+#define BYBYCU_ERR_DEVICE (-7)    /* a kernel reported a device-side error (bounded wait) */
+#define BYBYCU_ERR_SESSION (-8)   /* session API used out of order */
+#define BYBYCU_ERR_PARITY (-9)    /* a parity gate failed */
+
+/* OP_TILE_GEMM weight formats */
+#define BYBYCU_FMT_FP4KM 0
+#define BYBYCU_FMT_F16 1
+#define BYBYCU_FMT_Q4B32 2
+
+/* element types of activations and outputs */
+#define BYBYCU_DT_F32 0
+#define BYBYCU_DT_BF16 1
+
+/* kernel routes */
+#define BYBYCU_ROUTE_AUTO 0   /* GEMV for M <= 16, tensor-core GEMM above */
+#define BYBYCU_ROUTE_GEMV 1   /* decode GEMV: TMA-streamed weights, register dequant */
+#define BYBYCU_ROUTE_TC 2     /* prefill GEMM: tcgen05 MMAs, fp32 accumulators in TMEM */
+#define BYBYCU_ROUTE_SIMT 3   /* CUDA-core FP32 tile loop, every format and shape */
+
+/* ---- library / device -------------------------------------------------------------- */
+
+/* ABI version of the loaded library. */
+BYBYCU_API int bybycu_version(void);
+
+/* Copies the last error message of this host thread (NUL-terminated, truncated to
+ * buf_len) and returns its status code.  Replaces the `err`/`err_len` pair of
+ * nimf_cpu_vm_run_slots (backends/cpu/cpu_vm.c:168-175) and sessionGetLastError
+ * (gpubackend.nim:2647-2667). */
+BYBYCU_API int bybycu_last_error(char* buf, int buf_len);
+
+/* Number of CUDA devices (detectBackend's probe, gpubackend.nim:131-142). */
+BYBYCU_API int bybycu_device_count(int* count);
+
+/* Makes `device` current on this host thread and checks it is an sm_100 part
+ * (ensureGpuInit for the `cuda` backend; BYBY_CUDA_DEVICE chooses it in the host layer). */
+BYBYCU_API int bybycu_init(int device);
+
+/* Device memory (the CudaResidentTensor stubs cuUpload / cuFree, gpubackend.nim:23-31). */
+BYBYCU_API int bybycu_malloc(void** dptr, int64_t bytes);
+BYBYCU_API int bybycu_free(void* dptr);
+BYBYCU_API int bybycu_upload(void* dst, const void* src, int64_t bytes, void* stream);
+BYBYCU_API int bybycu_download(void* dst, const void* src, int64_t bytes, void* stream);
+BYBYCU_API int bybycu_memset(void* dst, int value, int64_t bytes, void* stream);
+BYBYCU_API int bybycu_stream_create(void** stream);
+BYBYCU_API int bybycu_stream_destroy(void* stream);
+BYBYCU_API int bybycu_synchronize(void* stream);
+
+/* Reads and clears the device-side error word that kernels set when a bounded wait runs
+ * out (synchronises the device first). *code = 0 when no kernel reported an error. */
+BYBYCU_API int bybycu_device_error(int* code);
+
+/* ---- the tile GEMM op -------------------------------------------------------------- */
+
+/* out[M, N] = x[M, K] * dequant(W)[N, K]^T for one OP_TILE_GEMM (session_vm.nim:106-122,
+ * :383-416), the slots of the micro-VM: out = slot 1, packed = slot 2, lut = slot 3,
+ * x = slot 4 (micro_kernel/tile_gemm.nim:16-18).  Replaces the CPU VM arm
+ * backends/cpu/cpu_vm.c:541-628 and the Vulkan dispatch tryTileGemm
+ * (backends/vulkan/vulkan_driver.nim:2599-2646) with the same size checks.
+ *   fmt        BYBYCU_FMT_*;  M > 0 rows, K > 0 a multiple of 32, N > 0 columns
+ *   x          device, x_dtype (F32 or BF16), x_len >= M*K elements
+ *   packed     device, packed_len bytes; scale_base = byte of the scale block (fmt 0, 2)
+ *   lut        device float table, lut_len floats, lut_base = first of its 272 floats
+ *              (fmt 0 only; may be NULL otherwise)
+ *   out        device, out_dtype (F32 or BF16), out_len >= M*N elements
+ *   route      BYBYCU_ROUTE_*; AUTO picks by M, an explicit route fails with
+ *              BYBYCU_ERR_SHAPE if it cannot run the shape/format
+ * Asynchronous on `stream`. */
+BYBYCU_API int bybycu_tile_gemm(int fmt, int M, int K, int N,
+                     const void* x, int x_dtype, int64_t x_len,
+                     const void* packed, int64_t packed_len, int64_t scale_base,
+                     const float* lut, int64_t lut_len, int64_t lut_base,
+                     void* out, int out_dtype, int64_t out_len,
+                     int route, void* stream);
+
+/* The same op with HOST activations and output and DEVICE-resident weights: copies x in,
+ * runs the op and copies out back, synchronising `stream` before it returns.  The
+ * immediate-mode form of the path (gpuMatmulQ4, gpubackend.nim:806-843). */
+BYBYCU_API int bybycu_tile_gemm_host(int fmt, int M, int K, int N,
+                          const void* x_host, int x_dtype,
+                          const void* packed, int64_t packed_len, int64_t scale_base,
+                          const float* lut, int64_t lut_len, int64_t lut_base,
+                          void* out_host, int out_dtype,
+                          void* x_dev, void* out_dev, int route, void* stream);
+
+/* Dequantises W to fp32 w[N, K] (the bit-exact check of the format decode:
+ * cpu_vm.c:612-617 for format 0). */
+BYBYCU_API int bybycu_dequant(int fmt, int K, int N, const void* packed, int64_t packed_len,
+                   int64_t scale_base, const float* lut, int64_t lut_len, int64_t lut_base,
+                   float* w_out, void* stream);
+
+/* The route AUTO takes for a shape, after the same checks as bybycu_tile_gemm. */
+BYBYCU_API int bybycu_route_for(int fmt, int M, int K, int N, int x_dtype, int* route);
+
+/* Device-pointer twin of nimf_cpu_vm_run_slots (backends/cpu/cpu_kernels.h:118-121,
+ * cpu_vm.c:178-182): runs a micro-VM program whose first op is OP_TILE_GEMM (formats
+ * 0/1/2, followed by the canonical tile ops), OP_FP4_COOP_GEMM, OP_Q4_GEMV or
+ * OP_Q4_COOP_GEMM.  `code` is HOST memory; mem/packed/lut/in_f32 are device slots with the
+ * reference's lengths (floats, bytes, floats, floats).  in_f32 = NULL reads x from mem.
+ * Any other program returns BYBYCU_ERR_PROGRAM and -1-style message in err. */
+BYBYCU_API int bybycu_vm_run_slots(const uint32_t* code, int n_words, float* mem, int mem_len,
+                        const uint8_t* packed, int packed_len, const float* lut, int lut_len,
+                        const float* in_f32, int in_len, int n_threads, int tg_floats,
+                        int tg_size, char* err, int err_len, void* stream);
+
+/* ---- session API (gpubackend.nim:1042-2722, the `cuda` branch) ------------------------ */
+
+/* sessionBegin / sessionEnd (gpubackend.nim:1042, :2422): one open session per host
+ * thread on the current device's session stream; End waits for every encoded op and
+ * reports the first failure. */
+BYBYCU_API int bybycu_session_begin(void);
+BYBYCU_API int bybycu_session_end(void);
+/* sessionUpload (gpubackend.nim:1133): a device copy of `bytes` host bytes. */
+BYBYCU_API int bybycu_session_upload(const void* host, int64_t bytes, void** handle);
+/* sessionAllocScratch (gpubackend.nim:1295): n_floats zeroed floats. */
+BYBYCU_API int bybycu_session_alloc_scratch(int64_t n_floats, void** handle);
+/* sessionRead (gpubackend.nim:2669): copies n_floats back (after sessionEnd). */
+BYBYCU_API int bybycu_session_read(const void* handle, float* host, int64_t n_floats);
+/* sessionFree (gpubackend.nim:2694). */
+BYBYCU_API int bybycu_session_free(void* handle);
+/* sessionFp4GemmTensorCore / sessionFp4GemmTiledEnc (gpubackend.nim:1442-1449, :1465-1473):
+ * FP4-KM tile GEMM c[M, N] = a[M, K] * W^T with w = nibbles then scale bytes
+ * (scaleBase = N*K/2) and the 272-float table at float 0 of lut; a is fp32.
+ * tensor_core != 0 takes the tensor-core route, else the FP32 register-tile route. */
+BYBYCU_API int bybycu_session_fp4_gemm(const void* a, const void* w, const void* lut, void* c,
+                            int M, int K, int N, int tensor_core);
+/* sessionF16GemmTile (gpubackend.nim:1475-1482): FP16 weights [N, K]. */
+BYBYCU_API int bybycu_session_f16_gemm(const void* a, const void* w, void* c, int M, int K, int N,
+                            int tensor_core);
+/* Q4B32 weights (format 2; scales [N, K/32] halves right after the nibbles). */
+BYBYCU_API int bybycu_session_q4b32_gemm(const void* a, const void* w, void* c, int M, int K, int N,
+                              int tensor_core);
+/* sessionTileGemmReady (gpubackend.nim:1484-1488 -> vulkanTileGemmReady,
+ * vulkan_driver.nim:2681-2762): the exact-data parity gate (M=37, K=128, N=80, every
+ * route that can run it, max rel err <= 1e-3), run once per process and format/route;
+ * *ready = 1 when it passed. */
+BYBYCU_API int bybycu_tile_gemm_ready(int fmt, int tensor_core, int* ready);
+
+/* ---- peer memory (the plumbing of the device-side all-gather) --------------------------- */
+
+/* Exports a cudaMalloc'ed device buffer as a 64-byte CUDA IPC handle another process can
+ * open.  No reference counterpart: the reference's workers exchange text over pipes
+ * (distributed.nim:224-276). */
+BYBYCU_API int bybycu_ipc_handle(const void* dptr, uint8_t handle[64]);
+/* Maps a peer process's buffer into this process on the current device (peer access is
+ * enabled by the mapping); *dptr is the local address of the peer buffer. */
+BYBYCU_API int bybycu_ipc_open(const uint8_t handle[64], void** dptr);
+BYBYCU_API int bybycu_ipc_close(void* dptr);
+
+/* ---- column sharding (distributed.nim:109-135) ----------------------------------------- */
+
+/* The column range [*n0, *n1) of `rank` among `world` shards of N columns: the
+ * largest-remainder split of distributed.nim:109-135 with equal weights, taken over blocks
+ * of `align` columns (the last block may be short). */
+BYBYCU_API int bybycu_shard_range(int N, int world, int rank, int align, int* n0, int* n1);
+
+/* One rank's share of a column-sharded tile GEMM whose output slices are exchanged in the
+ * same kernel: the rank computes out[:, n0:n1) from its shard of W (rows n0..n1 of the
+ * packed layout, `packed` pointing at the shard) and stores every element both into its own
+ * out and, over NVLink peer pointers, into the `out` buffer of every other rank
+ * (peer_out[r] = rank r's out as mapped on this device; peer_out[rank] = out).  It then
+ * raises its counter in every rank's signal array (peer_signal[r]: 9 uint32 - one counter
+ * per rank and the device-side epoch - zero before first use) and waits, bounded, until
+ * every rank's counter for this epoch is present in its own.  epoch = 0 keeps the epoch on
+ * the device (graph-capturable); epoch > 0 is the caller's count of calls, starting at 1.  out is [M, N] fp32 row-major on every rank.  Replaces the gather of text results
+ * in runShards (distributed.nim:304-375) with a device-side all-gather. */
+BYBYCU_API int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1,
+                               const void* x, int x_dtype,
+                               const void* packed, int64_t packed_len, int64_t scale_base,
+                               const float* lut, int64_t lut_len, int64_t lut_base,
+                               void* out, void* const* peer_out, uint32_t* const* peer_signal,
+                               int world, int rank, uint32_t epoch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,330 @@
+"""GPU parity of libbybycuda.so against the reference's CPU arithmetic, through the C ABI.
+
+Tolerances (written here, per route):
+* SIMT route: bit-identical to the reference CPU VM (same fmaf order).
+* GEMV route: the reference test's own check, max|diff| <= 1e-4 * max(1, max|ref|)
+  (tests/t_fp4_tile_gemm.nim:54-67), and per element |diff| <= 1e-3 * max(1, |ref|) (the
+  1e-3 relative bound of the path's parity gate, vulkan_driver.nim:2754).
+* dequantisation: bit-exact for every format.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from bybylang_b200 import _lib  # noqa: E402
+from bybylang_b200 import gpubackend as gb  # noqa: E402
+
+DEV = "cuda:0"
+PEAK_TOL = 1e-4
+ELEM_TOL = 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    gb.ensureGpuInit(gb.GpuBackend.gbCuda, 0)
+    yield
+    assert _lib.device_error() == 0
+
+
+def lib():
+    return _lib.load()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def run(fmt, M, K, N, x, packed, *, scale_base=0, lut=None, route=_lib.ROUTE_AUTO, out_dtype=torch.float32):
+    out = torch.full((M, N), float("nan"), dtype=out_dtype, device=DEV)
+    gb.tile_gemm(fmt, x, packed, out, M=M, K=K, N=N, scale_base=scale_base, lut=lut, route=route)
+    torch.cuda.synchronize()
+    return out
+
+
+def q4_slot(p, s):
+    """Nibbles then fp16 scales at a 16-byte aligned scale_base, as one device uint8 slot."""
+    nb = p.size
+    sb = (nb + 15) // 16 * 16
+    blob = np.zeros(sb + s.size * 2, np.uint8)
+    blob[:nb] = p.ravel()
+    blob[sb:] = np.ascontiguousarray(s, np.uint16).view(np.uint8).ravel()
+    return dev(blob), sb
+
+
+def assert_close(want, got, peak_tol=PEAK_TOL, elem_tol=ELEM_TOL, what=""):
+    want = np.asarray(want, np.float64)
+    got = np.asarray(got, np.float64)
+    assert np.isfinite(got).all(), what
+    d = np.abs(want - got)
+    peak = max(1.0, float(np.abs(want).max()))
+    assert d.max() <= peak_tol * peak, f"{what}: max|diff| {d.max():.3e} peak {peak:.3f}"
+    assert (d <= elem_tol * np.maximum(1.0, np.abs(want))).all(), f"{what}: per-element"
+
+
+# ----------------------------------------------------------------------------------------
+# SIMT route: bit-identical to the reference CPU VM
+# ----------------------------------------------------------------------------------------
+
+def test_simt_fp4km_reference_cases_bit_exact(golden):
+    g = golden["ref_tile_cases"]
+    for i in range(5):
+        M, K, N = (int(v) for v in g[f"fp4_{i}_shape"])
+        out = run(0, M, K, N, dev(g[f"fp4_{i}_x"]), dev(g[f"fp4_{i}_packed"]), scale_base=N * K // 2,
+                  lut=dev(g[f"fp4_{i}_table"]), route=_lib.ROUTE_SIMT)
+        assert np.array_equal(out.cpu().numpy(), g[f"fp4_{i}_dyn"]), f"case {i}"
+
+
+def test_simt_f16_reference_cases_bit_exact(golden):
+    g = golden["ref_tile_cases"]
+    for i in range(5):
+        M, K, N = (int(v) for v in g[f"f16_{i}_shape"])
+        out = run(1, M, K, N, dev(g[f"f16_{i}_x"]), dev(g[f"f16_{i}_halves"].view(np.uint8)), route=_lib.ROUTE_SIMT)
+        assert np.array_equal(out.cpu().numpy(), g[f"f16_{i}_dyn"]), f"case {i}"
+
+
+def test_simt_q4b32_bit_exact(golden, oracle_mod):
+    g = golden["ref_q4b32"]
+    for i in range(8):
+        M, K, N = (int(v) for v in g[f"q4_{i}_shape"])
+        slot, sb = q4_slot(g[f"q4_{i}_packed"], g[f"q4_{i}_scales"])
+        x = dev(oracle_mod.bf16_to_f32(g[f"q4_{i}_x_bf16"]))
+        out = run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_SIMT)
+        assert np.array_equal(out.cpu().numpy(), g[f"q4_{i}_vm"]), f"case {i}"
+        xb = dev(g[f"q4_{i}_x_bf16"]).view(torch.bfloat16)
+        out = run(2, M, K, N, xb, slot, scale_base=sb, route=_lib.ROUTE_SIMT)
+        assert np.array_equal(out.cpu().numpy(), g[f"q4_{i}_vm"]), f"case {i} bf16 input"
+
+
+# ----------------------------------------------------------------------------------------
+# GEMV route (format 2, M <= 16)
+# ----------------------------------------------------------------------------------------
+
+def test_gemv_q4b32_golden_cases(golden, oracle_mod):
+    g = golden["ref_q4b32"]
+    ran = 0
+    for i in range(8):
+        M, K, N = (int(v) for v in g[f"q4_{i}_shape"])
+        if M > 16:
+            continue
+        slot, sb = q4_slot(g[f"q4_{i}_packed"], g[f"q4_{i}_scales"])
+        xb = dev(g[f"q4_{i}_x_bf16"]).view(torch.bfloat16)
+        out = run(2, M, K, N, xb, slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+        assert_close(g[f"q4_{i}_vm"], out.cpu().numpy(), what=f"case {i} bf16")
+        xf = dev(oracle_mod.bf16_to_f32(g[f"q4_{i}_x_bf16"]))
+        out = run(2, M, K, N, xf, slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+        assert_close(g[f"q4_{i}_vm"], out.cpu().numpy(), what=f"case {i} f32")
+        ran += 1
+    assert ran == 5
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 11008), (16, 4096, 11008), (1, 11008, 4096), (16, 11008, 4096),
+                                   (4, 4096, 4096), (9, 4096, 12288)])
+def test_gemv_benchmark_shapes_against_oracle(M, K, N, oracle_mod):
+    O = oracle_mod
+    p, s = O.gen_q4b32(N, K)
+    xb = O.gen_x_bf16(M, K)
+    want = O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, M, K, N, threads=8)
+    slot, sb = q4_slot(p, s)
+    out = run(2, M, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert_close(want, out.cpu().numpy(), what=f"M={M} K={K} N={N}")
+
+
+def test_gemv_lm_head_columns_against_oracle(oracle_mod):
+    """C5 (N = 128256): the whole GEMM on the GPU, a column sample through the oracle."""
+    O = oracle_mod
+    M, K, N = 1, 4096, 128256
+    p, s = O.gen_q4b32(N, K)
+    xb = O.gen_x_bf16(M, K)
+    slot, sb = q4_slot(p, s)
+    out = run(2, M, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb, route=_lib.ROUTE_GEMV).cpu().numpy()
+    cols = np.r_[0:512, 60000:60512, N - 512:N]
+    want = O.tile_gemm_q4b32(O.bf16_to_f32(xb), p[cols], s[cols], M, K, len(cols), threads=8)
+    assert_close(want, out[:, cols], what="lm head")
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 32, 1), (2, 96, 15), (3, 288, 17), (7, 4128, 130), (8, 256, 16),
+                                   (12, 800, 33), (16, 64, 1000), (5, 4096, 1)])
+def test_gemv_ragged_shapes(M, K, N, oracle_mod):
+    O = oracle_mod
+    p, s = O.gen_q4b32(N, K, seed=1234 + M)
+    xb = O.gen_x_bf16(M, K, seed=99 + K)
+    want = O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, M, K, N)
+    slot, sb = q4_slot(p, s)
+    out = run(2, M, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert_close(want, out.cpu().numpy(), what=f"M={M} K={K} N={N}")
+    # an unaligned scale block (scale_base not a multiple of 16) takes the non-TMA scale loads
+    blob = np.zeros(p.size + 2 + s.size * 2, np.uint8)
+    blob[:p.size] = p.ravel()
+    blob[p.size + 2:] = s.view(np.uint8).ravel()
+    out = run(2, M, K, N, dev(xb).view(torch.bfloat16), dev(blob), scale_base=p.size + 2, route=_lib.ROUTE_GEMV)
+    assert_close(want, out.cpu().numpy(), what=f"M={M} K={K} N={N} unaligned scales")
+
+
+def test_gemv_bf16_output(oracle_mod):
+    O = oracle_mod
+    M, K, N = 3, 4096, 2048
+    p, s = O.gen_q4b32(N, K)
+    xb = O.gen_x_bf16(M, K)
+    slot, sb = q4_slot(p, s)
+    x = dev(xb).view(torch.bfloat16)
+    f32 = run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    b16 = run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_GEMV, out_dtype=torch.bfloat16)
+    assert torch.equal(f32.to(torch.bfloat16), b16)
+
+
+def test_auto_route_small_m_is_gemv(oracle_mod):
+    assert gb.route_for(2, 1, 4096, 11008) == _lib.ROUTE_GEMV
+    O = oracle_mod
+    p, s = O.gen_q4b32(96, 256)
+    xb = O.gen_x_bf16(2, 256)
+    slot, sb = q4_slot(p, s)
+    out = run(2, 2, 256, 96, dev(xb).view(torch.bfloat16), slot, scale_base=sb)
+    assert_close(O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, 2, 256, 96), out.cpu().numpy())
+
+
+# ----------------------------------------------------------------------------------------
+# Dequantisation: bit-exact
+# ----------------------------------------------------------------------------------------
+
+def test_dequant_bit_exact_all_formats(golden, oracle_mod):
+    O = oracle_mod
+    N, K = 80, 4096
+    p, s = O.gen_q4b32(N, K)
+    slot, sb = q4_slot(p, s)
+    w = torch.empty(N, K, dtype=torch.float32, device=DEV)
+    gb.dequant(2, slot, w, K=K, N=N, scale_base=sb)
+    torch.cuda.synchronize()
+    assert np.array_equal(w.cpu().numpy(), O.dequant_q4b32(p, s, N, K))
+    g = golden["ref_tile_cases"]
+    M, K, N = (int(v) for v in g["fp4_3_shape"])
+    w = torch.empty(N, K, dtype=torch.float32, device=DEV)
+    gb.dequant(0, dev(g["fp4_3_packed"]), w, K=K, N=N, scale_base=N * K // 2, lut=dev(g["fp4_3_table"]))
+    torch.cuda.synchronize()
+    assert np.array_equal(w.cpu().numpy(), O.dequant_fp4km(g["fp4_3_packed"], g["fp4_3_table"], N, K))
+    M, K, N = (int(v) for v in g["f16_4_shape"])
+    w = torch.empty(N, K, dtype=torch.float32, device=DEV)
+    gb.dequant(1, dev(g["f16_4_halves"].view(np.uint8)), w, K=K, N=N)
+    torch.cuda.synchronize()
+    assert np.array_equal(w.cpu().numpy(), O.f16_to_f32(g["f16_4_halves"]))
+
+
+# ----------------------------------------------------------------------------------------
+# The micro-VM twin and the session API
+# ----------------------------------------------------------------------------------------
+
+def _vm(code, mem_len, packed, lut, x):
+    mem = torch.zeros(mem_len, dtype=torch.float32, device=DEV)
+    err = C.create_string_buffer(256)
+    words = np.ascontiguousarray(code, np.uint32)
+    rc = lib().bybycu_vm_run_slots(words.ctypes.data_as(C.POINTER(C.c_uint32)), len(words),
+                                   C.c_void_p(mem.data_ptr()), mem_len, C.c_void_p(packed.data_ptr()),
+                                   packed.numel(), C.c_void_p(lut.data_ptr()), lut.numel(),
+                                   C.c_void_p(x.data_ptr()), x.numel(), 128, 64, 128, err, 256, None)
+    torch.cuda.synchronize()
+    assert rc == 0, err.value
+    return mem.cpu().numpy()
+
+
+def test_vm_programs_match_reference(golden, oracle_mod):
+    O = oracle_mod
+    g = golden["ref_tile_cases"]
+    for i in range(5):
+        M, K, N = (int(v) for v in g[f"fp4_{i}_shape"])
+        x, packed, table = dev(g[f"fp4_{i}_x"]), dev(g[f"fp4_{i}_packed"]), dev(g[f"fp4_{i}_table"])
+        for rows in (0, M):
+            got = _vm(O.fp4_tile_program(rows, K, N, N * K // 2), M * N, packed, table, x)
+            assert np.array_equal(got, g[f"fp4_{i}_dyn"].ravel()), f"case {i} rows {rows}"
+        if f"fp4_{i}_legacy" in g:
+            lut_word = (N * (K // 2) + N * (K // 32) + 3) // 4
+            blob = np.zeros(lut_word * 4 + 272 * 4, np.uint8)
+            blob[:g[f"fp4_{i}_packed"].size] = g[f"fp4_{i}_packed"]
+            blob[lut_word * 4:] = g[f"fp4_{i}_table"].view(np.uint8)
+            code = np.array([0xAC, M, K, N, 32, K // 32, 1], np.uint32)
+            db = dev(blob)
+            got = _vm(code, M * N, db, db.view(torch.float32), x)
+            assert np.array_equal(got, g[f"fp4_{i}_legacy"].ravel()), f"case {i} legacy"
+    q = golden["ref_q4b32"]
+    for i in range(8):
+        M, K, N = (int(v) for v in q[f"q4_{i}_shape"])
+        p, s = q[f"q4_{i}_packed"], q[f"q4_{i}_scales"]
+        xf = dev(O.bf16_to_f32(q[f"q4_{i}_x_bf16"]))
+        wq, sc, zp = O.q4b32_to_asym(p, s, N, K)
+        sbw = (N * (K // 2) + 3) // 4
+        blob = np.zeros((sbw + 2 * sc.size) * 4, np.uint8)
+        blob[:wq.size] = wq
+        f = blob.view(np.float32)
+        f[sbw:sbw + sc.size], f[sbw + sc.size:] = sc, zp
+        db = dev(blob)
+        got = _vm(np.array([0xAB, M, K, N, 32, K // 32, 1], np.uint32), M * N, db, db.view(torch.float32), xf)
+        assert np.array_equal(got, q[f"q4_{i}_q4gemv"].ravel()), f"q4 gemv case {i}"
+        slot, sb = q4_slot(p, s)
+        prog = np.array([0xB0 | (2 << 8), 0, K, N, sb, 0, 0xB1, 0xB2, 0xB4, 0xB5, 0x50, 0xB6, 0x50, 0xB3, 0xB7, 1],
+                        np.uint32)
+        got = _vm(prog, M * N, slot, torch.zeros(1, device=DEV), xf)
+        assert_close(q[f"q4_{i}_vm"].ravel(), got, what=f"format 2 program case {i}")
+
+
+def test_session_api_like_reference_test(golden):
+    """The reference test's gpuRun (t_fp4_tile_gemm.nim:104-117) on the cuda backend."""
+    be = gb.parseBackend("cuda")
+    g = golden["ref_tile_cases"]
+    for i in range(5):
+        M, K, N = (int(v) for v in g[f"fp4_{i}_shape"])
+        for tc in (True, False):
+            assert gb.sessionBegin(be)
+            hx = gb.sessionUpload(be, g[f"fp4_{i}_x"])
+            hw = gb.sessionUpload(be, g[f"fp4_{i}_packed"])
+            hl = gb.sessionUpload(be, g[f"fp4_{i}_table"])
+            o = gb.sessionAllocScratch(be, M * N)
+            enc = gb.sessionFp4GemmTensorCore if tc else gb.sessionFp4GemmTiledEnc
+            assert enc(be, hx, hw, hl, o, M, K, N)
+            assert gb.sessionEnd(be)
+            got = gb.sessionRead(be, o, M * N)
+            for h in (hx, hw, hl, o):
+                gb.sessionFree(be, h)
+            np.testing.assert_allclose(got, g[f"fp4_{i}_dyn"].ravel(), rtol=0,
+                                       atol=1e-4 * max(1.0, float(np.abs(g[f"fp4_{i}_dyn"]).max())))
+    assert gb.gForbidCpuFallback
+
+
+def test_session_errors_raise_not_fall_back():
+    be = gb.GpuBackend.gbCuda
+    assert gb.sessionBegin(be)
+    hx = gb.sessionUpload(be, np.zeros(64, np.float32))
+    o = gb.sessionAllocScratch(be, 16)
+    with pytest.raises(_lib.BybyCudaError, match="fallback is forbidden"):
+        gb.sessionQ4B32Gemm(be, hx, hx, o, 1, 64, 16)   # weight slot too small
+    with pytest.raises(_lib.BybyCudaError):
+        gb.sessionEnd(be)   # reports the session's first failure
+    gb.sessionFree(be, hx)
+    gb.sessionFree(be, o)
+
+
+def test_parity_gates():
+    be = gb.GpuBackend.gbCuda
+    for f16 in (False, True):
+        assert gb.sessionTileGemmReady(be, f16, False)
+    assert gb.sessionTileGemmReady(be, False, True, fmt=2)
+
+
+def test_host_io_entry_point(oracle_mod):
+    """bybycu_tile_gemm_host: host activations in, host output back (the e2e form)."""
+    O = oracle_mod
+    M, K, N = 1, 4096, 11008
+    p, s = O.gen_q4b32(N, K)
+    xb = O.gen_x_bf16(M, K)
+    slot, sb = q4_slot(p, s)
+    xh = torch.from_numpy(xb).pin_memory()
+    oh = torch.zeros(M, N, dtype=torch.float32).pin_memory()
+    xd = torch.empty(M, K, dtype=torch.bfloat16, device=DEV)
+    od = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    rc = lib().bybycu_tile_gemm_host(2, M, K, N, C.c_void_p(xh.data_ptr()), _lib.DT_BF16, C.c_void_p(slot.data_ptr()),
+                                     slot.numel(), sb, None, 0, 0, C.c_void_p(oh.data_ptr()), _lib.DT_F32,
+                                     C.c_void_p(xd.data_ptr()), C.c_void_p(od.data_ptr()), _lib.ROUTE_AUTO, None)
+    assert rc == 0, _lib.last_error()
+    assert_close(O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, M, K, N, threads=8), oh.numpy())

@@ -7,87 +7,142 @@
 //
 // Data movement (one persistent CTA per SM, warp-specialised):
 //   * the CTA owns a contiguous run of 16-row weight tiles, processed in passes of up to TP
-//     tiles; a pass walks K in chunks of 256 values (8 blocks of 32);
-//   * a producer warp streams, per chunk, each tile's 16 rows x 128 B of nibbles, the tiles'
-//     16 rows x 8 fp16 scales and the M x 256 activations with TMA (cp.async.bulk.tensor,
-//     128-byte swizzle for the nibbles and activations) into a ring of stages guarded by
-//     mbarriers ("full" completes on the transaction bytes, "empty" when all 8 consumer warps
-//     released the stage);
-//   * consumer warp w owns block w of every chunk for every tile of the pass.
+//     tiles; a pass walks K in chunks of KC values (2048, or 1024 / 512 when shared memory
+//     is short);
+//   * a producer warp streams each chunk with few, large TMA operations - the TMA unit's
+//     cost is per operation, so every weight box spans all rows of the pass:
+//       - nibbles: KC/256 boxes of 128 bytes x (16 * tiles) rows, 128-byte swizzle;
+//       - scales: one box of KC/32 halves x (16 * tiles) rows;
+//       - activations: one 1D bulk copy per activation row into a padded smem row;
+//     into a ring of stages guarded by mbarriers ("full" completes on the transaction bytes,
+//     "empty" when all 16 consumer warps released the stage);
+//   * consumer warp w owns blocks w, w+16, ... of every chunk, for every tile of the pass.
+//   * programmatic dependent launch: the weights of every initially free stage are requested
+//     before griddepcontrol.wait (they are not written by the previous kernel); activations and the
+//     outputs are touched only after it.
 //
 // Math per (tile, block) in one warp: the nibbles of rows g and g+8 (lane = 4g + t holds
 // bytes 4t..4t+3 of the block's 16) are turned into bf16 values 136 + q by one lop3 per pair
 // (magic exponent 0x43 = 128, nibble ^ 8 = q + 8) and fed as the A operand of two
 // mma.sync.m16n8k16 bf16 MMAs (low nibbles = k 0..15, high = k 16..31) whose B operand is
-// the raw bf16 activations.  The fp32 block sums therefore hold sum(q x) + 136 sum(x); the
-// offset is removed with the activation block sums, computed once per block by the same MMA
-// with an all-ones A, and the block scale is applied in fp32: acc += s * (D - 136 Sx).
-// q and x are exact in bf16, so the only rounding is the fp32 accumulation.  fp32
-// activations are split into two bf16 terms (hi + lo) and both are multiplied.
+// the raw bf16 activations.  The fp32 block sums would hold sum(q x) + 136 sum(x); the
+// offset is removed through the MMA's accumulator input, -136 Sx, where Sx (the activation
+// block sums) comes once per block from the same MMA with an all-ones A.  The block scale is
+// then applied in fp32: acc += s * D.  q and x are exact in bf16, so the only rounding is
+// the fp32 accumulation.  fp32 activations are split into two bf16 terms (hi + lo).
 //
-// The 8 warps' partial sums of a tile meet in shared memory at the end of a pass.
+// The 16 warps' partial sums of a tile meet in shared memory at the end of a pass, in a fixed
+// order (the result does not depend on timing).  Shared memory is read by 32-bit shared
+// addresses only.
+#include <cstdlib>
+#include <cstring>
+
 #include "kernels.h"
 
 namespace bybycu {
 
 namespace {
 
-constexpr int kConsumerWarps = 8;
+#ifndef BYBYCU_GEMV_WARPS
+#define BYBYCU_GEMV_WARPS 16
+#endif
+constexpr int kConsumerWarps = BYBYCU_GEMV_WARPS;   // 8 or 16
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kKC = 256;           // K values per stage: one 32-value block per consumer warp
 constexpr int kTileRows = 16;
-constexpr int kTileBytes = kTileRows * (kKC / 2);   // 2048: 16 swizzled 128-byte rows
-constexpr int kScaleTileBytes = kTileRows * 16;     // 16 rows x 8 halves
+constexpr int kRedSlots = 4;                        // partial-sum slots of the cross-warp reduction
 constexpr uint32_t kMagicA = 0x43084308u;           // bf16 128 | (nibble ^ 8) via lop3
 constexpr uint32_t kOnesBf16x2 = 0x3F803F80u;
 
 struct GemvParams {
     int M, K, N, G;
-    int n_tiles;
     int tiles_base, tiles_extra;   // contiguous tile split over the grid
+    int kc;                        // K values per chunk (512, 1024 or 2048)
     int n_chunks;
     int stages;
     int tp;                        // tiles per pass (<= TP)
-    int x_boxes;                   // activation boxes per stage
-    int x_box_rows_bytes;          // bytes of one activation box in shared memory (1 KiB aligned)
-    int scale_tma;                 // scales arrive by TMA (K % 256 == 0, aligned)
-    uint32_t stage_bytes;          // W tiles + scale tiles + activations
-    uint32_t w_off, s_off, x_off;  // offsets inside a stage
+    int scale_tma;                 // scales arrive by TMA (K % 256 == 0, 16-byte aligned)
+    int x_pitch;                   // bytes between activation rows in shared memory
+    uint32_t stage_bytes;          // W boxes + scale box + activations
+    uint32_t w_box_bytes;          // one nibble box: 16 * TP rows x 128 B
+    uint32_t s_off, x_off;         // offsets inside a stage
+    uint32_t s_pitch;              // bytes per row of the scale box
     const __half* scales;          // packed + scale_base
+    const uint8_t* x;              // activations [M, K] (global)
+    int x_elem;                    // 2 (bf16) or 4 (fp32)
     void* out;
     int out_bf16;
     int64_t out_ld, out_col0;
 };
 
-__device__ __forceinline__ uint32_t lop3_magic(uint32_t a, uint32_t mask) {
-    // (mask & (a ^ C)) | (~mask & C): nibble ^ 8 inside the mask, the bf16 exponent elsewhere.
-    uint32_t d;
-    asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(a), "r"(mask), "r"(kMagicA));
-    return d;
+// Three nibble maps and three scale maps: boxes of 16 * TP rows (full pass), 16 * (TP - 1)
+// rows (the short pass of a balanced split) and 16 rows (any other remainder).
+struct GemvMaps {
+    CUtensorMap w[3];
+    CUtensorMap s[3];
+};
+
+// The nibbles in bits 0-3 and 16-19 of `a` as two bf16 values 128 + (nibble ^ 8) = 136 + q:
+// (a & 0x000F000F) ^ 0x43084308 (the bf16 exponent of 128, and the xor with 8), one LOP3.
+__device__ __forceinline__ uint32_t lop3_magic(uint32_t a) { return (a & 0x000F000Fu) ^ kMagicA; }
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) { return __byte_perm(a, b, sel); }
+
+// d = a * b + c  (m16n8k16, bf16 inputs, fp32 accumulators)
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                         const float (&c)[4]) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %11, %12, %13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+          "f"(c[3]));
 }
 
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t d;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-    return d;
+// d = a * b + c  (m16n8k16, fp16 inputs, fp32 accumulators)
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                        const float (&c)[4]) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %11, %12, %13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+          "f"(c[3]));
 }
 
-__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+// fp16 dequantisation: the low nibbles (bits 0-3 / 16-19) become 1024 + (nibble ^ 8) =
+// 1032 + q, the high nibbles stay in place (bits 4-7 / 20-23, still mantissa in fp16) and
+// become 1024 + 16 (nibble ^ 8) = 1152 + 16 q; one LOP3 each.
+__device__ __forceinline__ uint32_t f16_lo(uint32_t a) { return (a & 0x000F000Fu) ^ 0x64086408u; }
+__device__ __forceinline__ uint32_t f16_hi(uint32_t a) { return (a & 0x00F000F0u) ^ 0x64806480u; }
+
+// bf16 pair -> fp16 pair (exact for |x| >= 2^-17), optionally scaled by 1/16 (exact).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t v, float scale) {
+    const float lo = __uint_as_float(v << 16) * scale, hi = __uint_as_float(v & 0xFFFF0000u) * scale;
+    const __half2 h = __floats2half2_rn(lo, hi);
+    uint32_t r;
+    memcpy(&r, &h, sizeof r);
+    return r;
 }
 
 // The B fragment of one 16-k half block for activation row `m` (lane = 4g + t):
 // k slots (2t, 2t+1) <-> elements (4t, 4t+2), slots (2t+8, 2t+9) <-> (4t+1, 4t+3), matching
-// the A fragment built from the nibble bytes 4t..4t+3.  `e4` holds elements 4t..4t+3 as
-// bf16 pairs (e01, e23).
+// the A fragment built from the nibble bytes 4t..4t+3.  (e01, e23) hold elements 4t..4t+3.
 __device__ __forceinline__ void b_frag(uint32_t e01, uint32_t e23, uint32_t& b0, uint32_t& b1) {
     b0 = prmt(e01, e23, 0x5410);
     b1 = prmt(e01, e23, 0x7632);
+}
+
+// Plain C++ loads from the shared window: ordinary memory accesses, so the compiler may
+// schedule them freely among the math but never above a barrier wait (a memory clobber).
+__device__ __forceinline__ uint32_t sh_u32(const uint8_t* smem, uint32_t off) {
+    return *reinterpret_cast<const uint32_t*>(smem + off);
+}
+__device__ __forceinline__ uint2 sh_u64(const uint8_t* smem, uint32_t off) {
+    return *reinterpret_cast<const uint2*>(smem + off);
+}
+
+__device__ __forceinline__ float2 half2_bits_to_float2(uint32_t v) {
+    __half2 h;
+    memcpy(&h, &v, sizeof h);
+    return __half22float2(h);
 }
 
 // Split 4 fp32 activations (elements 4t..4t+3) into bf16 hi/lo pairs in B-fragment order.
@@ -104,18 +159,104 @@ __device__ __forceinline__ void split_f32(const float4 v, uint32_t& h0, uint32_t
     l1 = *reinterpret_cast<const uint32_t*>(&bl);
 }
 
-template <int TP, int NT, bool XF32>
+// The producer: lane 0 of the last warp streams every (pass, chunk) iteration of this CTA into
+// the stage ring (see the file comment).  Shared by the M = 1 and the general kernels.
+__device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvParams& p, uint8_t* smem,
+                                              uint64_t* full_bar, uint64_t* empty_bar, volatile int* s_abort,
+                                              int lane, int tile_begin, int my_tiles, int total_it) {
+    const int wboxes = p.kc / 256;
+    if (lane == 0) {
+        for (int i = 0; i < 3; ++i) {
+            prefetch_tensormap(&maps.w[i]);
+            if (p.scale_tma) prefetch_tensormap(&maps.s[i]);
+        }
+        const uint64_t policy = l2_policy_evict_first();
+        // Issues the weight part of iteration (chunk, t0) into stage s and arms its barrier.
+        auto issue_weights = [&](int s, int chunk, int t0) {
+            const int nt = min(p.tp, tile_begin + my_tiles - t0);
+            const int k0 = chunk * p.kc;
+            const int kn = min(p.kc, p.K - k0);
+            const uint32_t rows = nt * kTileRows;
+            const uint32_t bytes = wboxes * rows * 128 + (p.scale_tma ? rows * p.s_pitch : 0) +
+                                   p.M * static_cast<uint32_t>(kn) * p.x_elem;
+            uint8_t* st = smem + static_cast<size_t>(s) * p.stage_bytes;
+            mbar_arrive_expect_tx(&full_bar[s], bytes);
+            // one box per 16 * nt rows when nt is TP or TP - 1, else one per tile
+            const int mi = nt == p.tp ? 0 : (nt == p.tp - 1 ? 1 : 2);
+            const int pieces = mi == 2 ? nt : 1;
+            for (int q = 0; q < pieces; ++q) {
+                const int row = (t0 + q) * kTileRows;
+                const uint32_t roff = q * kTileRows * 128;
+                for (int bx = 0; bx < wboxes; ++bx)
+                    tma_load_2d_hint(st + bx * p.w_box_bytes + roff, &maps.w[mi], &full_bar[s], k0 / 2 + bx * 128,
+                                     row, policy);
+                if (p.scale_tma)
+                    tma_load_2d(st + p.s_off + q * kTileRows * p.s_pitch, &maps.s[mi], &full_bar[s], k0 / 32, row);
+            }
+        };
+        // Issues the activation rows of iteration `chunk` into stage s.
+        auto issue_x = [&](int s, int chunk) {
+            const int k0 = chunk * p.kc;
+            const uint32_t x_row_bytes = static_cast<uint32_t>(min(p.kc, p.K - k0)) * p.x_elem;
+            uint8_t* st = smem + static_cast<size_t>(s) * p.stage_bytes;
+            for (int m = 0; m < p.M; ++m)
+                bulk_load_1d(st + p.x_off + m * p.x_pitch, p.x + (static_cast<size_t>(m) * p.K + k0) * p.x_elem,
+                             x_row_bytes, &full_bar[s]);
+        };
+        // Prologue: the weights of every free stage before griddepcontrol.wait (the previous
+        // kernel does not write them), the activations after it.
+        const int first = min(p.stages, total_it);
+        {
+            int chunk = 0, t0 = tile_begin;
+            for (int it = 0; it < first; ++it) {
+                issue_weights(it, chunk, t0);
+                if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
+            }
+            pdl_wait();
+            chunk = 0;
+            for (int it = 0; it < first; ++it) {
+                issue_x(it, chunk);
+                if (++chunk == p.n_chunks) chunk = 0;
+            }
+        }
+        int issued = first;
+        int s = first % p.stages, round = first / p.stages;
+        int chunk = first % p.n_chunks, t0 = tile_begin + (first / p.n_chunks) * p.tp;
+        for (int it = first; it < total_it; ++it) {
+            if (*s_abort) break;
+            if (!mbar_wait_bounded(&empty_bar[s], (round - 1) & 1, kDevErrEmptyWait)) {
+                *s_abort = 1;
+                break;
+            }
+            issue_weights(s, chunk, t0);
+            issue_x(s, chunk);
+            issued = it + 1;
+            if (++s == p.stages) { s = 0; ++round; }
+            if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
+        }
+        // Before the CTA may exit, every copy it issued must have landed.
+        for (int it = max(0, issued - p.stages); it < issued; ++it) {
+            const int ds = it % p.stages;
+            if (!mbar_wait_bounded(&full_bar[ds], (it / p.stages) & 1, kDevErrDrainWait)) break;
+        }
+    }
+}
+
+template <int TP, int NT, bool XF32, bool STMA>
 __global__ void __launch_bounds__(kThreads, 1)
-gemv_q4b32_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                  const __grid_constant__ CUtensorMap smap, const GemvParams p) {
+gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
+    constexpr int H = XF32 ? 2 : 1;   // bf16 terms per activation
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stages = smem;
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(stages + static_cast<size_t>(p.stages) * p.stage_bytes);
+    // 1 KiB-aligned base, kept in the shared window (32-bit addresses, shared loads only)
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* const smem = smem_raw + (base - raw);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(p.stages) * p.stage_bytes);
     uint64_t* empty_bar = full_bar + p.stages;
     volatile int* s_abort = reinterpret_cast<volatile int*>(empty_bar + p.stages);
-    float* red = reinterpret_cast<float*>(empty_bar + p.stages + 2);   // [8][TP][NT][32][4]
+    const uint32_t red = smem_u32(empty_bar + p.stages + 2);   // [kRedSlots][TP * NT * 128] floats
 
+    pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // contiguous tile run of this CTA
@@ -136,52 +277,12 @@ gemv_q4b32_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
     __syncthreads();
 
     if (warp == kConsumerWarps) {
-        // ------------------------------------------------------------------ producer
-        if (lane == 0) {
-            prefetch_tensormap(&wmap);
-            prefetch_tensormap(&xmap);
-            if (p.scale_tma) prefetch_tensormap(&smap);
-            const uint64_t policy = l2_policy_evict_first();
-            int issued = 0;
-            for (int it = 0; it < total_it; ++it) {
-                const int s = it % p.stages;
-                if (it >= p.stages) {
-                    if (*s_abort) break;
-                    if (!mbar_wait_bounded(&empty_bar[s], ((it / p.stages) - 1) & 1, kDevErrEmptyWait)) {
-                        *s_abort = 1;
-                        break;
-                    }
-                }
-                const int pass = it / p.n_chunks, chunk = it % p.n_chunks;
-                const int t0 = tile_begin + pass * p.tp;
-                const int nt = min(p.tp, tile_begin + my_tiles - t0);
-                const uint32_t bytes = nt * kTileBytes + (p.scale_tma ? nt * kScaleTileBytes : 0) +
-                                       p.x_boxes * (p.M * 128);
-                uint8_t* st = stages + static_cast<size_t>(s) * p.stage_bytes;
-                mbar_arrive_expect_tx(&full_bar[s], bytes);
-                for (int i = 0; i < nt; ++i) {
-                    tma_load_2d_hint(st + p.w_off + i * kTileBytes, &wmap, &full_bar[s], chunk * (kKC / 2),
-                                     (t0 + i) * kTileRows, policy);
-                    if (p.scale_tma)
-                        tma_load_2d(st + p.s_off + i * kScaleTileBytes, &smap, &full_bar[s], chunk * 8,
-                                    (t0 + i) * kTileRows);
-                }
-                const int box_elems = XF32 ? 32 : 64;
-                for (int bx = 0; bx < p.x_boxes; ++bx)
-                    tma_load_2d(st + p.x_off + bx * p.x_box_rows_bytes, &xmap, &full_bar[s],
-                                chunk * kKC + bx * box_elems, 0);
-                issued = it + 1;
-            }
-            // Before the CTA may exit, every copy it issued must have landed.
-            for (int it = max(0, issued - p.stages); it < issued; ++it) {
-                const int s = it % p.stages;
-                if (!mbar_wait_bounded(&full_bar[s], (it / p.stages) & 1, kDevErrDrainWait)) break;
-            }
-        }
+        gemv_producer(maps, p, smem, full_bar, empty_bar, s_abort, lane, tile_begin, my_tiles, total_it);
         return;
     }
 
     // ---------------------------------------------------------------------- consumers
+    pdl_wait();   // outputs may be read by the previous kernel; activations come from it
     const int g = lane >> 2, t = lane & 3;
     float acc[TP][NT][4];
 #pragma unroll
@@ -191,126 +292,148 @@ gemv_q4b32_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
 #pragma unroll
             for (int v = 0; v < 4; ++v) acc[i][j][v] = 0.0f;
     const uint32_t ones[4] = {kOnesBf16x2, kOnesBf16x2, kOnesBf16x2, kOnesBf16x2};
+    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    const int qblocks = p.kc / (32 * kConsumerWarps);   // blocks of this warp per chunk: warp, warp + W, ...
 
+    int s = 0, round = 0, chunk = 0, t0 = tile_begin;
     for (int it = 0; it < total_it; ++it) {
-        const int s = it % p.stages;
-        const int pass = it / p.n_chunks, chunk = it % p.n_chunks;
-        const int t0 = tile_begin + pass * p.tp;
         const int nt = min(p.tp, tile_begin + my_tiles - t0);
         bool ok = !*s_abort;
-        if (ok && !mbar_wait_bounded(&full_bar[s], (it / p.stages) & 1, kDevErrFullWait)) {
+        if (ok && !mbar_wait_bounded(&full_bar[s], round & 1, kDevErrFullWait)) {
             *s_abort = 1;
             ok = false;
         }
-        const int c = chunk * 8 + warp;   // the 32-value block of this warp
-        if (ok && c < p.G) {
-            const uint8_t* st = stages + static_cast<size_t>(s) * p.stage_bytes;
-            // ---- activation fragments of block c (B operands) and their block sums
-            uint32_t blo[NT][XF32 ? 2 : 1][2], bhi[NT][XF32 ? 2 : 1][2];
+        const uint32_t st = base + static_cast<uint32_t>(s) * p.stage_bytes;
+        for (int qb = 0; qb < qblocks; ++qb) {
+            const int cb = warp + kConsumerWarps * qb;   // block within the chunk
+            const int c = chunk * (p.kc / 32) + cb;  // block within the row
+            if (!ok || c >= p.G) break;
+            // ---- activation fragments of block c (B operands); the offset term 136 * sum(x)
+            //      goes into the MMA accumulator input
+            uint32_t blo[NT][H][2], bhi[NT][H][2];
+            float negcorr[NT][4];
 #pragma unroll
             for (int j = 0; j < NT; ++j) {
                 const int m = j * 8 + g;
                 const bool live = m < p.M;
+                const uint32_t xr = st + p.x_off + m * p.x_pitch;
                 if constexpr (!XF32) {
-                    // bf16 box: 64 elements (128 B) per row; element e0 = 32*(w&1) + 4t
-                    const uint8_t* box = st + p.x_off + (warp >> 1) * p.x_box_rows_bytes + m * 128;
-                    const int jlo = 4 * (warp & 1) + (t >> 1), jhi = jlo + 2;
-                    const int sub = 8 * (t & 1);
                     uint2 lo = make_uint2(0u, 0u), hi = make_uint2(0u, 0u);
                     if (live) {
-                        lo = *reinterpret_cast<const uint2*>(box + ((jlo ^ (m & 7)) << 4) + sub);
-                        hi = *reinterpret_cast<const uint2*>(box + ((jhi ^ (m & 7)) << 4) + sub);
+                        lo = lds_u64(xr + (32 * cb + 4 * t) * 2);
+                        hi = lds_u64(xr + (32 * cb + 16 + 4 * t) * 2);
                     }
                     b_frag(lo.x, lo.y, blo[j][0][0], blo[j][0][1]);
                     b_frag(hi.x, hi.y, bhi[j][0][0], bhi[j][0][1]);
                 } else {
-                    // fp32 box: 32 elements (128 B) per row, one box per block
-                    const uint8_t* box = st + p.x_off + warp * p.x_box_rows_bytes + m * 128;
                     float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
                     if (live) {
-                        lo = *reinterpret_cast<const float4*>(box + ((t ^ (m & 7)) << 4));
-                        hi = *reinterpret_cast<const float4*>(box + (((4 + t) ^ (m & 7)) << 4));
+                        const uint4 a = lds_u128(xr + (32 * cb + 4 * t) * 4);
+                        const uint4 bb = lds_u128(xr + (32 * cb + 16 + 4 * t) * 4);
+                        lo = make_float4(__uint_as_float(a.x), __uint_as_float(a.y), __uint_as_float(a.z),
+                                         __uint_as_float(a.w));
+                        hi = make_float4(__uint_as_float(bb.x), __uint_as_float(bb.y), __uint_as_float(bb.z),
+                                         __uint_as_float(bb.w));
                     }
                     split_f32(lo, blo[j][0][0], blo[j][0][1], blo[j][1][0], blo[j][1][1]);
                     split_f32(hi, bhi[j][0][0], bhi[j][0][1], bhi[j][1][0], bhi[j][1][1]);
                 }
-            }
-            float corr[NT][4];
-#pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                float sx[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                for (int h = 0; h < (XF32 ? 2 : 1); ++h) {
-                    mma_bf16(sx, ones, blo[j][h][0], blo[j][h][1]);
-                    mma_bf16(sx, ones, bhi[j][h][0], bhi[j][h][1]);
+                float sx[4];
+                mma_bf16(sx, ones, blo[j][0][0], blo[j][0][1], zero4);
+                mma_bf16(sx, ones, bhi[j][0][0], bhi[j][0][1], sx);
+                if constexpr (XF32) {
+                    mma_bf16(sx, ones, blo[j][1][0], blo[j][1][1], sx);
+                    mma_bf16(sx, ones, bhi[j][1][0], bhi[j][1][1], sx);
                 }
 #pragma unroll
-                for (int v = 0; v < 4; ++v) corr[j][v] = 136.0f * sx[v];
+                for (int v = 0; v < 4; ++v) negcorr[j][v] = -136.0f * sx[v];
             }
-            // ---- per tile: dequantise rows g and g+8 of block c, two MMAs, scale in fp32
+            // this lane's word of block cb in the nibble box (row g; row g + 8 is 1 KiB further)
+            const uint32_t wl = st + (cb >> 3) * p.w_box_bytes + g * 128 + ((((cb & 7) ^ g)) << 4) + 4 * t;
+            const uint32_t sl = st + p.s_off + g * p.s_pitch +
+                                (p.s_pitch == 128 ? ((((cb >> 3) ^ g) << 4) + 2 * (cb & 7)) : 2 * cb);
+            // ---- per tile: dequantise rows g and g+8 of block c, two MMAs, scale in fp32.
+            //      Every tile slot runs (no branch, so the compiler interleaves the TP
+            //      independent tiles); the partial sums of slots >= nt are never stored.
 #pragma unroll
             for (int i = 0; i < TP; ++i) {
-                if (i < nt) {
-                    const uint8_t* wt = st + p.w_off + i * kTileBytes;
-                    const uint32_t off = g * 128 + ((warp ^ g) << 4) + 4 * t;
-                    const uint32_t w0 = *reinterpret_cast<const uint32_t*>(wt + off);
-                    const uint32_t w8 = *reinterpret_cast<const uint32_t*>(wt + off + 1024);
-                    float s0, s8;
+                const uint32_t wt = wl + i * (kTileRows * 128);
+                const uint32_t w0 = lds_u32(wt);
+                const uint32_t w8 = lds_u32(wt + 1024);
+                float s0, s8;
+                if constexpr (STMA) {
+                    const uint32_t sc = sl + i * kTileRows * p.s_pitch;
+                    s0 = __half2float(__ushort_as_half(lds_u16(sc)));
+                    s8 = __half2float(__ushort_as_half(lds_u16(sc + 8 * p.s_pitch)));
+                } else {
                     const int64_t row0 = static_cast<int64_t>(t0 + i) * kTileRows + g;
-                    if (p.scale_tma) {
-                        const __half* sc = reinterpret_cast<const __half*>(st + p.s_off + i * kScaleTileBytes);
-                        s0 = __half2float(sc[g * 8 + warp]);
-                        s8 = __half2float(sc[(g + 8) * 8 + warp]);
-                    } else {
-                        s0 = row0 < p.N ? __half2float(p.scales[row0 * p.G + c]) : 0.0f;
-                        s8 = row0 + 8 < p.N ? __half2float(p.scales[(row0 + 8) * p.G + c]) : 0.0f;
-                    }
-                    uint32_t alo[4], ahi[4];
-                    alo[0] = lop3_magic(w0, 0x000F000Fu);
-                    alo[1] = lop3_magic(w8, 0x000F000Fu);
-                    alo[2] = lop3_magic(w0 >> 8, 0x000F000Fu);
-                    alo[3] = lop3_magic(w8 >> 8, 0x000F000Fu);
-                    ahi[0] = lop3_magic(w0 >> 4, 0x000F000Fu);
-                    ahi[1] = lop3_magic(w8 >> 4, 0x000F000Fu);
-                    ahi[2] = lop3_magic(w0 >> 12, 0x000F000Fu);
-                    ahi[3] = lop3_magic(w8 >> 12, 0x000F000Fu);
+                    s0 = (i < nt && row0 < p.N) ? __half2float(p.scales[row0 * p.G + c]) : 0.0f;
+                    s8 = (i < nt && row0 + 8 < p.N) ? __half2float(p.scales[(row0 + 8) * p.G + c]) : 0.0f;
+                }
+                uint32_t alo[4], ahi[4];
+                alo[0] = lop3_magic(w0);
+                alo[1] = lop3_magic(w8);
+                alo[2] = lop3_magic(w0 >> 8);
+                alo[3] = lop3_magic(w8 >> 8);
+                ahi[0] = lop3_magic(w0 >> 4);
+                ahi[1] = lop3_magic(w8 >> 4);
+                ahi[2] = lop3_magic(w0 >> 12);
+                ahi[3] = lop3_magic(w8 >> 12);
 #pragma unroll
-                    for (int j = 0; j < NT; ++j) {
-                        float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                        for (int h = 0; h < (XF32 ? 2 : 1); ++h) {
-                            mma_bf16(d, alo, blo[j][h][0], blo[j][h][1]);
-                            mma_bf16(d, ahi, bhi[j][h][0], bhi[j][h][1]);
-                        }
-                        acc[i][j][0] = fmaf(s0, d[0] - corr[j][0], acc[i][j][0]);
-                        acc[i][j][1] = fmaf(s0, d[1] - corr[j][1], acc[i][j][1]);
-                        acc[i][j][2] = fmaf(s8, d[2] - corr[j][2], acc[i][j][2]);
-                        acc[i][j][3] = fmaf(s8, d[3] - corr[j][3], acc[i][j][3]);
+                for (int j = 0; j < NT; ++j) {
+                    float d[4];
+                    mma_bf16(d, alo, blo[j][0][0], blo[j][0][1], negcorr[j]);
+                    mma_bf16(d, ahi, bhi[j][0][0], bhi[j][0][1], d);
+                    if constexpr (XF32) {
+                        mma_bf16(d, alo, blo[j][1][0], blo[j][1][1], d);
+                        mma_bf16(d, ahi, bhi[j][1][0], bhi[j][1][1], d);
                     }
+                    acc[i][j][0] = fmaf(s0, d[0], acc[i][j][0]);
+                    acc[i][j][1] = fmaf(s0, d[1], acc[i][j][1]);
+                    acc[i][j][2] = fmaf(s8, d[2], acc[i][j][2]);
+                    acc[i][j][3] = fmaf(s8, d[3], acc[i][j][3]);
                 }
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[s]);
+        if (++s == p.stages) { s = 0; ++round; }
 
         if (chunk == p.n_chunks - 1) {
-            // ---- end of pass: the 8 warps' partial sums meet in shared memory
-            float* mine = red + static_cast<size_t>(warp) * TP * NT * 128;
+            // ---- end of pass: the warps' partial sums meet in shared memory in a fixed order:
+            //      the last four warps store, then each group of four below adds in turn
+            constexpr int E = TP * NT * 128;
+            const uint32_t slot = red + static_cast<uint32_t>((warp & 3) * E * 4);
+#pragma unroll
+            for (int phase = kConsumerWarps / 4 - 1; phase >= 0; --phase) {
+                if ((warp >> 2) == phase) {
+#pragma unroll
+                    for (int i = 0; i < TP; ++i)
+#pragma unroll
+                        for (int j = 0; j < NT; ++j) {
+                            const uint32_t a = slot + ((i * NT + j) * 32 + lane) * 16;
+                            if (phase == kConsumerWarps / 4 - 1) {
+                                sts_v4(a, acc[i][j][0], acc[i][j][1], acc[i][j][2], acc[i][j][3]);
+                            } else {
+                                const float4 o = lds_v4f(a);
+                                sts_v4(a, o.x + acc[i][j][0], o.y + acc[i][j][1], o.z + acc[i][j][2],
+                                       o.w + acc[i][j][3]);
+                            }
+                        }
+                }
+                named_barrier(1, kConsumerWarps * 32);
+            }
 #pragma unroll
             for (int i = 0; i < TP; ++i)
 #pragma unroll
                 for (int j = 0; j < NT; ++j)
 #pragma unroll
-                    for (int v = 0; v < 4; ++v) {
-                        mine[((i * NT + j) * 32 + lane) * 4 + v] = acc[i][j][v];
-                        acc[i][j][v] = 0.0f;
-                    }
-            named_barrier(1, kConsumerWarps * 32);
+                    for (int v = 0; v < 4; ++v) acc[i][j][v] = 0.0f;
             const int entries = nt * NT * 128;
             for (int e = threadIdx.x; e < entries; e += kConsumerWarps * 32) {
                 float sum = 0.0f;
 #pragma unroll
-                for (int w = 0; w < kConsumerWarps; ++w) sum += red[static_cast<size_t>(w) * TP * NT * 128 + e];
+                for (int w = 0; w < kRedSlots; ++w) sum += lds_f32(red + static_cast<uint32_t>((w * E + e) * 4));
                 const int v = e & 3, ln = (e >> 2) & 31, ij = e >> 7;
                 const int j = ij % NT, i = ij / NT;
                 const int gg = ln >> 2, tt = ln & 3;
@@ -324,36 +447,314 @@ gemv_q4b32_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
             }
             named_barrier(1, kConsumerWarps * 32);
         }
+        if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
     }
 }
 
-struct GemvPlan {
-    int tp, nt;
-    bool xf32;
-};
 
-template <int TP, int NT, bool XF32>
-int launch_t(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& smap,
-             const GemvParams& p, int grid, size_t smem, cudaStream_t stream) {
-    auto kern = gemv_q4b32_kernel<TP, NT, XF32>;
-    static bool configured = false;   // per instantiation; the limit is a device property
-    if (!configured) {
-        BYBYCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
-        configured = true;
+// ----------------------------------------------------------------------------------------
+// M = 1 (decode) kernel.  The MMA's N dimension carries 8 blocks instead of 8 activation
+// rows: column j of B holds block j's activations on that block's k slots and zeros on the
+// others (block-diagonal), so one chain of MMAs over a 256-value box of K accumulates
+// D[row][j] = offset_j + sum_{k in block j} q[row][k] x[k] for the box's blocks at once; the
+// offset (136 sum(x_j) for bf16 operands) comes from the same MMA with a constant A and is
+// removed in the fp32 epilogue, which runs once per chain instead of once per block.
+// kM1Warps consumer warps: kM1Warps / 4 per 256-value box of a 1024-value chunk, each owning
+// 8 / (kM1Warps / 4) blocks of the box.  The nibble dequantisation (one LOP3 per two weights,
+// after a shift) runs on the ALU pipe, the kernel's binding resource; the block-diagonal
+// selects are computed once per chunk and pinned in registers.
+// ----------------------------------------------------------------------------------------
+#ifndef BYBYCU_GEMV_M1_WARPS
+#define BYBYCU_GEMV_M1_WARPS 8
+#endif
+constexpr int kM1Warps = BYBYCU_GEMV_M1_WARPS;   // 8 or 16
+constexpr int kM1Threads = (kM1Warps + 1) * 32;
+constexpr int kM1KC = 1024;
+constexpr int kM1Parts = kM1Warps / 4;            // warps per box
+constexpr int kM1Blocks = 8 / kM1Parts;           // blocks per warp
+
+template <int TP, bool STMA, bool F16A>
+__global__ void __launch_bounds__(kM1Threads, 1)
+gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
+    constexpr int S = 2 * kM1Blocks;   // MMA steps per warp per box (low / high half per block)
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* const smem = smem_raw + (base - raw);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(p.stages) * p.stage_bytes);
+    uint64_t* empty_bar = full_bar + p.stages;
+    volatile int* s_abort = reinterpret_cast<volatile int*>(empty_bar + p.stages);
+    const uint32_t red = smem_u32(empty_bar + p.stages + 2);   // [kM1Warps][TP][16] floats
+
+    pdl_launch_dependents();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x;
+    const int my_tiles = p.tiles_base + (b < p.tiles_extra ? 1 : 0);
+    const int tile_begin = b * p.tiles_base + min(b, p.tiles_extra);
+    const int passes = (my_tiles + p.tp - 1) / p.tp;
+    const int total_it = passes * p.n_chunks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], kM1Warps);
+        }
+        *s_abort = 0;
+        fence_mbar_init();
     }
-    kern<<<grid, kThreads, smem, stream>>>(wmap, xmap, smap, p);
+    __syncthreads();
+
+    if (warp == kM1Warps) {
+        gemv_producer(maps, p, smem, full_bar, empty_bar, s_abort, lane, tile_begin, my_tiles, total_it);
+        return;
+    }
+
+    const int g = lane >> 2, t = lane & 3;
+    const int box = warp / kM1Parts, part = warp % kM1Parts;   // blocks part*kM1Blocks .. +kM1Blocks-1
+    const int blk0 = part * kM1Blocks;
+    float acc[TP][2];
+#pragma unroll
+    for (int i = 0; i < TP; ++i) acc[i][0] = acc[i][1] = 0.0f;
+    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    // per-block word offsets inside a tile (row g; row g+8 is 1 KiB further), swizzled
+    uint32_t woff[kM1Blocks];
+#pragma unroll
+    for (int q = 0; q < kM1Blocks; ++q) woff[q] = g * 128 + (((blk0 + q) ^ g) << 4) + 4 * t;
+    bool waited = false;
+
+    int s = 0, round = 0, chunk = 0, t0 = tile_begin;
+    for (int it = 0; it < total_it; ++it) {
+        const int nt = min(p.tp, tile_begin + my_tiles - t0);
+        bool ok = !*s_abort;
+        if (ok && !mbar_wait_bounded(&full_bar[s], round & 1, kDevErrFullWait)) {
+            *s_abort = 1;
+            ok = false;
+        }
+        const int c0 = chunk * (kM1KC / 32) + box * 8;   // first block of this warp's box
+        if (ok && c0 + blk0 < p.G) {
+            const uint32_t st = static_cast<uint32_t>(s) * p.stage_bytes;   // offset of the stage in smem
+            // ---- block g of the box: this lane's activation fragments (zero past K)
+            const bool live = c0 + g < p.G;
+            const uint32_t xr = st + p.x_off + (32 * (box * 8 + g) + 4 * t) * 2;
+            uint2 lo = make_uint2(0u, 0u), hi = make_uint2(0u, 0u);
+            if (live) {
+                lo = sh_u64(smem, xr);
+                hi = sh_u64(smem, xr + 32);
+            }
+            uint32_t xl0, xl1, xh0, xh1;
+            b_frag(lo.x, lo.y, xl0, xl1);
+            b_frag(hi.x, hi.y, xh0, xh1);
+            if constexpr (F16A) {   // fp16 activations; the high half pre-scaled by 1/16
+                xl0 = bf16x2_to_f16x2(xl0, 1.0f);
+                xl1 = bf16x2_to_f16x2(xl1, 1.0f);
+                xh0 = bf16x2_to_f16x2(xh0, 0.0625f);
+                xh1 = bf16x2_to_f16x2(xh1, 0.0625f);
+            }
+            // block-diagonal B for this warp's S steps: step j (block blk0 + j/2, half j&1)
+            // is nonzero only in that block's column, i.e. on lanes whose g is that block
+            uint32_t bd[S][2];
+#pragma unroll
+            for (int j = 0; j < S; ++j) {
+                const bool mine = g == blk0 + (j >> 1);
+                bd[j][0] = mine ? ((j & 1) ? xh0 : xl0) : 0u;
+                bd[j][1] = mine ? ((j & 1) ? xh1 : xl1) : 0u;
+                asm volatile("" : "+r"(bd[j][0]), "+r"(bd[j][1]));   // keep them in registers
+            }
+            // the offsets of this warp's columns (runs beside the tile chains)
+            float corr[4];
+            if constexpr (F16A) {
+                const uint32_t c_lo[4] = {0x64086408u, 0x64086408u, 0x64086408u, 0x64086408u};   // 1032
+                const uint32_t c_hi[4] = {0x64806480u, 0x64806480u, 0x64806480u, 0x64806480u};   // 1152
+                mma_f16(corr, c_lo, bd[0][0], bd[0][1], zero4);
+                mma_f16(corr, c_hi, bd[1][0], bd[1][1], corr);
+#pragma unroll
+                for (int j = 2; j < S; j += 2) {
+                    mma_f16(corr, c_lo, bd[j][0], bd[j][1], corr);
+                    mma_f16(corr, c_hi, bd[j + 1][0], bd[j + 1][1], corr);
+                }
+            } else {
+                const uint32_t c136[4] = {0x43084308u, 0x43084308u, 0x43084308u, 0x43084308u};   // 136
+                mma_bf16(corr, c136, bd[0][0], bd[0][1], zero4);
+#pragma unroll
+                for (int j = 1; j < S; ++j) mma_bf16(corr, c136, bd[j][0], bd[j][1], corr);
+            }
+            const uint32_t wbox = st + box * p.w_box_bytes;
+#pragma unroll
+            for (int i = 0; i < TP; ++i) {
+                float d[4];
+#pragma unroll
+                for (int q = 0; q < kM1Blocks; ++q) {
+                    const uint32_t wt = wbox + i * (kTileRows * 128) + woff[q];
+                    const uint32_t w0 = sh_u32(smem, wt);
+                    const uint32_t w8 = sh_u32(smem, wt + 1024);
+                    uint32_t alo[4], ahi[4];
+                    if constexpr (F16A) {
+                        const uint32_t v0 = w0 >> 8, v8 = w8 >> 8;
+                        alo[0] = f16_lo(w0);
+                        alo[1] = f16_lo(w8);
+                        alo[2] = f16_lo(v0);
+                        alo[3] = f16_lo(v8);
+                        ahi[0] = f16_hi(w0);
+                        ahi[1] = f16_hi(w8);
+                        ahi[2] = f16_hi(v0);
+                        ahi[3] = f16_hi(v8);
+                        if (q == 0) mma_f16(d, alo, bd[0][0], bd[0][1], zero4);
+                        else mma_f16(d, alo, bd[2 * q][0], bd[2 * q][1], d);
+                        mma_f16(d, ahi, bd[2 * q + 1][0], bd[2 * q + 1][1], d);
+                    } else {
+                        alo[0] = lop3_magic(w0);
+                        alo[1] = lop3_magic(w8);
+                        alo[2] = lop3_magic(w0 >> 8);
+                        alo[3] = lop3_magic(w8 >> 8);
+                        ahi[0] = lop3_magic(w0 >> 4);
+                        ahi[1] = lop3_magic(w8 >> 4);
+                        ahi[2] = lop3_magic(w0 >> 12);
+                        ahi[3] = lop3_magic(w8 >> 12);
+                        if (q == 0) mma_bf16(d, alo, bd[0][0], bd[0][1], zero4);
+                        else mma_bf16(d, alo, bd[2 * q][0], bd[2 * q][1], d);
+                        mma_bf16(d, ahi, bd[2 * q + 1][0], bd[2 * q + 1][1], d);
+                    }
+                }
+                // scales of blocks 2t and 2t+1 of the box for rows g and g+8 (the columns of
+                // the box's other warps hold zeros on this warp)
+                float2 sg, sg8;
+                if constexpr (STMA) {
+                    const uint32_t sa = st + p.s_off + (i * kTileRows + g) * p.s_pitch + (box * 8 + 2 * t) * 2;
+                    sg = half2_bits_to_float2(sh_u32(smem, sa));
+                    sg8 = half2_bits_to_float2(sh_u32(smem, sa + 8 * p.s_pitch));
+                } else {
+                    const int64_t r0 = static_cast<int64_t>(t0 + i) * kTileRows + g;
+                    const int ca = c0 + 2 * t, cc = ca + 1;
+                    const bool v0 = i < nt && r0 < p.N, v8 = i < nt && r0 + 8 < p.N;
+                    sg.x = (v0 && ca < p.G) ? __half2float(p.scales[r0 * p.G + ca]) : 0.0f;
+                    sg.y = (v0 && cc < p.G) ? __half2float(p.scales[r0 * p.G + cc]) : 0.0f;
+                    sg8.x = (v8 && ca < p.G) ? __half2float(p.scales[(r0 + 8) * p.G + ca]) : 0.0f;
+                    sg8.y = (v8 && cc < p.G) ? __half2float(p.scales[(r0 + 8) * p.G + cc]) : 0.0f;
+                }
+                acc[i][0] = fmaf(sg.x, d[0] - corr[0], acc[i][0]);
+                acc[i][0] = fmaf(sg.y, d[1] - corr[1], acc[i][0]);
+                acc[i][1] = fmaf(sg8.x, d[2] - corr[2], acc[i][1]);
+                acc[i][1] = fmaf(sg8.y, d[3] - corr[3], acc[i][1]);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[s]);
+        if (++s == p.stages) { s = 0; ++round; }
+
+        if (chunk == p.n_chunks - 1) {
+            if (!waited) {   // the previous kernel may still read the outputs
+                pdl_wait();
+                waited = true;
+            }
+            // ---- end of pass: rows g and g+8 summed over the quad, then over the warps
+#pragma unroll
+            for (int i = 0; i < TP; ++i) {
+                float v0 = acc[i][0], v8 = acc[i][1];
+                v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+                v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
+                v8 += __shfl_xor_sync(0xffffffffu, v8, 1);
+                v8 += __shfl_xor_sync(0xffffffffu, v8, 2);
+                if (t == 0) {
+                    sts_f32(red + ((warp * TP + i) * 16 + g) * 4, v0);
+                    sts_f32(red + ((warp * TP + i) * 16 + g + 8) * 4, v8);
+                }
+                acc[i][0] = acc[i][1] = 0.0f;
+            }
+            named_barrier(1, kM1Warps * 32);
+            for (int e = threadIdx.x; e < nt * 16; e += kM1Warps * 32) {
+                float sum = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kM1Warps; ++w) sum += lds_f32(red + ((w * TP) * 16 + e) * 4);
+                const int64_t n = static_cast<int64_t>(t0) * kTileRows + e;
+                if (n < p.N) {
+                    const int64_t oi = p.out_col0 + n;
+                    if (p.out_bf16) reinterpret_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(sum);
+                    else reinterpret_cast<float*>(p.out)[oi] = sum;
+                }
+            }
+            named_barrier(1, kM1Warps * 32);
+        }
+        if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
+    }
+}
+
+bool pdl_enabled() {
+    static const int on = [] {
+        const char* e = getenv("BYBY_CUDA_PDL");
+        return (e && e[0] == '0') ? 0 : 1;
+    }();
+    return on != 0;
+}
+
+template <int TP, int NT, bool XF32, bool STMA>
+int launch_t(const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, cudaStream_t stream) {
+    auto kern = gemv_q4b32_kernel<TP, NT, XF32, STMA>;
+    static uint64_t configured = 0;   // per device: the opt-in smem limit is a function attribute
+    int dev = 0;
+    BYBYCU_CUDA_TRY(cudaGetDevice(&dev));
+    if (!(configured >> (dev & 63) & 1)) {
+        BYBYCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
+        configured |= uint64_t(1) << (dev & 63);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, p));
     BYBYCU_LAUNCH_CHECK("gemv_q4b32_kernel");
     return BYBYCU_OK;
 }
 
-template <int TP>
-int dispatch_tp(int nt, bool xf32, const CUtensorMap& w, const CUtensorMap& x, const CUtensorMap& s,
-                const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
-    if (nt == 1) return xf32 ? launch_t<TP, 1, true>(w, x, s, p, grid, smem, st)
-                             : launch_t<TP, 1, false>(w, x, s, p, grid, smem, st);
-    return xf32 ? launch_t<TP, 2, true>(w, x, s, p, grid, smem, st)
-                : launch_t<TP, 2, false>(w, x, s, p, grid, smem, st);
+// fp16 operands with the high nibbles dequantised in place (5 ALU ops per 8 weights instead
+// of 7); BYBY_CUDA_GEMV_F16=0 selects the bf16 operands (offset 136 instead of 1032/1152).
+bool m1_f16() {
+    static const int on = [] {
+        const char* e = getenv("BYBY_CUDA_GEMV_F16");
+        return (e && e[0] == '0') ? 0 : 1;
+    }();
+    return on != 0;
 }
+
+template <int TP, bool STMA>
+int launch_m1(const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, cudaStream_t stream) {
+    auto kern = m1_f16() ? gemv_m1_kernel<TP, STMA, true> : gemv_m1_kernel<TP, STMA, false>;
+    static uint64_t configured[2] = {0, 0};
+    int dev = 0;
+    BYBYCU_CUDA_TRY(cudaGetDevice(&dev));
+    const int fi = m1_f16() ? 1 : 0;
+    if (!(configured[fi] >> (dev & 63) & 1)) {
+        BYBYCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
+        configured[fi] |= uint64_t(1) << (dev & 63);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kM1Threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, maps, p));
+    BYBYCU_LAUNCH_CHECK("gemv_m1_kernel");
+    return BYBYCU_OK;
+}
+
+template <int TP, int NT>
+int dispatch_x(bool xf32, const GemvMaps& m, const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
+    if (p.scale_tma)
+        return xf32 ? launch_t<TP, NT, true, true>(m, p, grid, smem, st) : launch_t<TP, NT, false, true>(m, p, grid, smem, st);
+    return xf32 ? launch_t<TP, NT, true, false>(m, p, grid, smem, st) : launch_t<TP, NT, false, false>(m, p, grid, smem, st);
+}
+
+size_t round1k(size_t v) { return (v + 1023) / 1024 * 1024; }
 
 }  // namespace
 
@@ -371,75 +772,108 @@ int launch_gemv(const GemmArgs& a) {
     DeviceInfo dev;
     if (int rc = current_device_info(&dev)) return rc;
     const bool xf32 = a.x_dtype == BYBYCU_DT_F32;
+    const int ntn = a.M > 8 ? 2 : 1;
+    const int xe = xf32 ? 4 : 2;
     const int n_tiles = static_cast<int>(ceil_div(a.N, kTileRows));
     const int grid = std::min(n_tiles, dev.sm_count);
     const int tiles_max = static_cast<int>(ceil_div(n_tiles, grid));
-    const int tp = tiles_max <= 1 ? 1 : tiles_max <= 2 ? 2 : tiles_max <= 4 ? 4 : tiles_max <= 5 ? 5 : 8;
-    const int ntn = a.M > 8 ? 2 : 1;
+    const uint8_t* scale_ptr = a.packed + a.scale_base;
+    const int G = a.K / 32;
+    const bool scale_tma = (G % 8 == 0) && ((reinterpret_cast<uintptr_t>(scale_ptr) & 15u) == 0);
+    const size_t budget = static_cast<size_t>(dev.max_smem_optin) - 1024 - 64;
+
+    const bool m1 = a.M == 1 && !xf32;
+    // K chunk: 512 values (fine pipelining: compute starts after the first 1/(K/512) of the
+    // data) with boxes spanning all rows of the pass; larger chunks only when M is large.
+    int kc = 0, tp = 0, tpl = 0, stages = 0;
+    size_t stage_bytes = 0, red_bytes = 0;
+    uint32_t s_pitch = 0, w_box = 0, s_off = 0, x_off = 0;
+    int x_pitch = 0;
+    for (int kc_try : {512, 1024, 2048}) {
+        if (m1 && kc_try != kM1KC) continue;   // the M = 1 kernel: one 256-value box per warp
+        const int tp_try = std::min(tiles_max, (ntn == 2 || m1) ? 5 : 8);
+        const int tpl_try = tp_try <= 2 ? 2 : tp_try <= 5 ? 5 : 8;
+        const uint32_t rows = 16 * tpl_try;
+        const uint32_t sp = static_cast<uint32_t>(kc_try / 32 * 2);
+        const uint32_t wb = rows * 128;
+        const uint32_t so = (kc_try / 256) * wb;
+        const uint32_t xo = static_cast<uint32_t>(so + round1k(scale_tma ? rows * sp : 0));
+        const int xp = kc_try * xe + 32;
+        const size_t sb = round1k(xo + static_cast<size_t>(a.M) * xp);
+        const size_t rb = m1 ? static_cast<size_t>(kM1Warps) * tpl_try * 16 * sizeof(float)
+                             : static_cast<size_t>(kRedSlots) * tpl_try * ntn * 128 * sizeof(float);
+        const int nch = static_cast<int>(ceil_div(a.K, kc_try));
+        const int want = static_cast<int>(ceil_div(tiles_max, tp_try)) * nch;
+        const int st = static_cast<int>((budget - rb) / (sb + 16));
+        if (st >= std::min(m1 ? 2 : 4, want) && st >= 1) {
+            kc = kc_try; tp = tp_try; tpl = tpl_try; stages = std::min(st, want);
+            stage_bytes = sb; red_bytes = rb; s_pitch = sp; w_box = wb; s_off = so; x_off = xo; x_pitch = xp;
+            break;
+        }
+    }
+    if (!kc) return set_error(BYBYCU_ERR_SHAPE, "GEMV: shared memory too small for M=%d", a.M);
+    // Ring depth.  The M = 1 kernel keeps two chunks in flight: all chunks requested at once
+    // complete together (the first one late), two let compute start on the first chunk early
+    // while the second streams.  BYBY_CUDA_GEMV_STAGES overrides (tuning).
+    if (m1) stages = std::min(stages, 2);
+    if (const char* e = getenv("BYBY_CUDA_GEMV_STAGES")) {
+        const int cap = atoi(e);
+        if (cap >= 1) stages = std::min(std::max(cap, 1), std::max(stages, cap));
+    }
 
     GemvParams p{};
-    p.M = a.M; p.K = a.K; p.N = a.N; p.G = a.K / 32;
-    p.n_tiles = n_tiles;
+    p.M = a.M; p.K = a.K; p.N = a.N; p.G = G;
     p.tiles_base = n_tiles / grid;
     p.tiles_extra = n_tiles % grid;
-    p.n_chunks = static_cast<int>(ceil_div(a.K, kKC));
-    p.tp = std::min(tp, tiles_max);
-    const uint8_t* scale_ptr = a.packed + a.scale_base;
-    p.scale_tma = (a.K % kKC == 0) && ((reinterpret_cast<uintptr_t>(scale_ptr) & 15u) == 0);
-    p.x_boxes = xf32 ? kKC / 32 : kKC / 64;
-    p.x_box_rows_bytes = static_cast<int>(ceil_div(a.M * 128, 1024) * 1024);
-    p.w_off = 0;
-    p.s_off = tp * kTileBytes;
-    p.x_off = p.s_off + static_cast<uint32_t>(ceil_div(tp * kScaleTileBytes, 1024) * 1024);
-    p.stage_bytes = p.x_off + p.x_boxes * p.x_box_rows_bytes;
+    p.kc = kc;
+    p.n_chunks = static_cast<int>(ceil_div(a.K, kc));
+    p.stages = stages;
+    p.tp = tp;
+    p.scale_tma = scale_tma;
+    p.x_pitch = x_pitch;
+    p.stage_bytes = static_cast<uint32_t>(stage_bytes);
+    p.w_box_bytes = w_box;
+    p.s_off = s_off;
+    p.x_off = x_off;
+    p.s_pitch = s_pitch;
     p.scales = reinterpret_cast<const __half*>(scale_ptr);
+    p.x = static_cast<const uint8_t*>(a.x);
+    p.x_elem = xe;
     p.out = a.out;
     p.out_bf16 = a.out_dtype == BYBYCU_DT_BF16;
     p.out_ld = a.out_ld;
     p.out_col0 = a.out_col0;
+    const size_t smem = 1024 + static_cast<size_t>(stages) * (stage_bytes + 16) + 16 + red_bytes;
 
-    const size_t red_bytes = static_cast<size_t>(kConsumerWarps) * tp * ntn * 128 * sizeof(float);
-    const size_t fixed = 1024 /*align slack*/ + red_bytes + 64;
-    const size_t budget = static_cast<size_t>(dev.max_smem_optin);
-    const int passes_max = static_cast<int>(ceil_div(tiles_max, p.tp));
-    const int want = passes_max * p.n_chunks;
-    int stages = static_cast<int>((budget - fixed) / (p.stage_bytes + 16));
-    stages = std::max(1, std::min(stages, want));
-    if (stages < 2 && want > 1)
-        return set_error(BYBYCU_ERR_SHAPE, "GEMV: shared memory too small for M=%d", a.M);
-    p.stages = stages;
-    const size_t smem = fixed + static_cast<size_t>(stages) * (p.stage_bytes + 16);
-
-    CUtensorMap wmap, xmap, smap;
-    if (int rc = encode_tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.N, a.K / 2,
-                                      kKC / 2, kTileRows, CU_TENSOR_MAP_SWIZZLE_128B,
-                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
-        return rc;
-    if (xf32) {
-        if (int rc = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.x, a.K, a.M,
-                                          static_cast<uint64_t>(a.K) * 4, 32, a.M, CU_TENSOR_MAP_SWIZZLE_128B,
-                                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
+    GemvMaps maps;
+    const int box_rows[3] = {16 * tp, 16 * std::max(1, tp - 1), 16};
+    for (int i = 0; i < 3; ++i) {
+        if (int rc = encode_tensor_map_2d(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.N, a.K / 2,
+                                          128, box_rows[i], CU_TENSOR_MAP_SWIZZLE_128B,
+                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
             return rc;
-    } else {
-        if (int rc = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.M,
-                                          static_cast<uint64_t>(a.K) * 2, 64, a.M, CU_TENSOR_MAP_SWIZZLE_128B,
-                                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
-            return rc;
+        if (scale_tma) {
+            if (int rc = encode_tensor_map_2d(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, scale_ptr, G, a.N,
+                                              static_cast<uint64_t>(G) * 2, kc / 32, box_rows[i],
+                                              s_pitch == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
+                return rc;
+        } else {
+            maps.s[i] = maps.w[i];   // unused
+        }
     }
-    if (p.scale_tma) {
-        if (int rc = encode_tensor_map_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, scale_ptr, p.G, a.N,
-                                          static_cast<uint64_t>(p.G) * 2, 8, kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
-            return rc;
-    } else {
-        smap = wmap;   // unused
+    const cudaStream_t st = a.stream;
+    if (m1) {
+        if (scale_tma) return tpl == 2 ? launch_m1<2, true>(maps, p, grid, smem, st) : launch_m1<5, true>(maps, p, grid, smem, st);
+        return tpl == 2 ? launch_m1<2, false>(maps, p, grid, smem, st) : launch_m1<5, false>(maps, p, grid, smem, st);
     }
-    switch (tp) {
-        case 1: return dispatch_tp<1>(ntn, xf32, wmap, xmap, smap, p, grid, smem, a.stream);
-        case 2: return dispatch_tp<2>(ntn, xf32, wmap, xmap, smap, p, grid, smem, a.stream);
-        case 4: return dispatch_tp<4>(ntn, xf32, wmap, xmap, smap, p, grid, smem, a.stream);
-        case 5: return dispatch_tp<5>(ntn, xf32, wmap, xmap, smap, p, grid, smem, a.stream);
-        default: return dispatch_tp<8>(ntn, xf32, wmap, xmap, smap, p, grid, smem, a.stream);
+    if (ntn == 2) {
+        return tpl == 2 ? dispatch_x<2, 2>(xf32, maps, p, grid, smem, st) : dispatch_x<5, 2>(xf32, maps, p, grid, smem, st);
+    }
+    switch (tpl) {
+        case 2: return dispatch_x<2, 1>(xf32, maps, p, grid, smem, st);
+        case 5: return dispatch_x<5, 1>(xf32, maps, p, grid, smem, st);
+        default: return dispatch_x<8, 1>(xf32, maps, p, grid, smem, st);
     }
 }
 

@@ -815,10 +815,11 @@ int launch_gemv(const GemmArgs& a) {
     // Ring depth.  The M = 1 kernel keeps two chunks in flight: all chunks requested at once
     // complete together (the first one late), two let compute start on the first chunk early
     // while the second streams.  BYBY_CUDA_GEMV_STAGES overrides (tuning).
-    if (m1) stages = std::min(stages, 2);
+    const int fit = stages;   // the most that fit in shared memory (and are useful)
+    if (m1) stages = std::min(fit, 2);
     if (const char* e = getenv("BYBY_CUDA_GEMV_STAGES")) {
-        const int cap = atoi(e);
-        if (cap >= 1) stages = std::min(std::max(cap, 1), std::max(stages, cap));
+        const int want_stages = atoi(e);
+        if (want_stages >= 1) stages = std::min(fit, want_stages);
     }
 
     GemvParams p{};

@@ -82,9 +82,11 @@ uint16_t half_bits_exact(float v) {
 }
 
 // The exact-data case of vulkanTileGemmReady (M=37, K=128, N=80): every product and partial
-// sum is exact in fp32 (and in fp16 inputs for the tensor-core routes).
+// sum is exact in fp32 (and in fp16 inputs for the tensor-core routes).  The tensor-core gate
+// uses K=256, the smallest K that route tiles.
 int run_gate(int fmt, int tensor_core, int* ready) {
-    constexpr int M = 37, K = 128, N = 80, G = K / 32;
+    constexpr int M = 37, N = 80;
+    const int K = tensor_core ? 256 : 128, G = K / 32;
     std::vector<float> x(M * K), table(272, 0.0f), expected(M * N, 0.0f);
     for (int i = 0; i < M * K; ++i) x[i] = static_cast<float>((i * 7 + 3) % 33 - 16) / 64.0f;
     std::vector<uint8_t> w;

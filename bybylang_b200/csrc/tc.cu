@@ -1,13 +1,594 @@
-// tc.cu - the prefill GEMM route (tcgen05).  Not built yet: the route reports that it
-// cannot run any shape, so AUTO never selects it.
+// tc.cu - the prefill GEMM route: Q4B32 weights x activations on the 5th-generation tensor
+// cores (tcgen05), one persistent CTA per SM.
+//
+// The reference computes the same product with OP_TILE_GEMM's "matmul" phase
+// (micro_kernel/tile_gemm.nim:20-34, backends/cpu/cpu_vm.c:605-626): out[m][n] =
+// sum_k x[m][k] * w[n][k] in fp32.  Here:
+//
+//   * a pre-pass converts the activations to fp16 (exact for bf16 inputs inside the fp16
+//     range) and permutes K inside every 32-block into the order the dequantizer produces
+//     weight pairs in (stage_x_kernel);
+//   * four dequant warps turn each weight row's nibbles into fp16 w = RNE(q * s) - one
+//     rounding per weight - and store them straight into tensor memory, where they are the
+//     MMA's A operand (128 weight rows = 128 TMEM lanes, two K elements per 32-bit column);
+//     no shared-memory traffic for A;
+//   * the fp16 activations come by TMA (128-byte swizzle) into a shared-memory ring and are
+//     the MMA's B operand (256 tokens per tile, K-major);
+//   * one thread issues tcgen05.mma 128x256x16 into an fp32 accumulator in TMEM;
+//   * after the K loop the same four warps read the accumulator back (tcgen05.ld) and store
+//     out[token][feature] (fp32 or bf16).
+//
+// Every wait is bounded (%globaltimer): on a timeout the kernel records an error code in
+// g_device_error, drains its copies and MMAs, frees its tensor memory and returns.
 #include "kernels.h"
 
+#include <mutex>
+
 namespace bybycu {
+namespace tc {
 
-bool tc_supports(const GemmArgs&) { return false; }
+constexpr int kBM = 128;          // weight rows (output features) per tile = MMA M
+constexpr int kBN = 256;          // tokens per tile = MMA N
+constexpr int kXK = 64;           // K per activation stage: one 128-byte swizzle row of fp16
+constexpr int kWK = 256;          // K per weight stage: 128 packed bytes per row
+constexpr int kStages = 4;        // activation stages in shared memory = A slots in TMEM
+constexpr int kWStages = 3;       // weight stages in shared memory
+constexpr int kSubs = kWK / kXK;  // activation stages per weight stage
+constexpr int kThreads = 256;     // 8 warps: X TMA, MMA, W TMA, idle, 4 x dequant/epilogue
+constexpr int kDequantWarp0 = 4;
 
-int launch_tc(const GemmArgs&) {
-    return set_error(BYBYCU_ERR_SHAPE, "tensor-core route is not available in this build");
+constexpr uint32_t kXStageBytes = kBN * kXK * 2;    // 32 KiB
+constexpr uint32_t kWStageBytes = kBM * kWK / 2;    // 16 KiB
+constexpr uint32_t kSStageBytes = kBM * (kWK / 32) * 2;  // 2 KiB
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccCols = kBN;                 // fp32 accumulator: one column per token
+constexpr uint32_t kACols = kXK / 2;               // A slot: two fp16 per column
+
+constexpr uint32_t kOffX = 0;
+constexpr uint32_t kOffW = kOffX + kStages * kXStageBytes;
+constexpr uint32_t kOffS = kOffW + kWStages * kWStageBytes;
+constexpr uint32_t kOffBar = kOffS + kWStages * kSStageBytes;
+// barriers: x_full, stage_empty, a_full [kStages]; w_full, w_empty [kWStages]; d_full,
+// d_empty, done; then the TMEM base address and the abort flag
+constexpr uint32_t kNumBars = 3 * kStages + 2 * kWStages + 3;
+constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
+constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
+constexpr uint32_t kSmemBytes = kOffAbort + 4 + 1024;  // + alignment slack
+
+// Instruction descriptor of kind::f16: D fp32, A and B fp16, both K-major, M=128, N=256.
+constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(kBN >> 3) << 17) |
+                            (uint32_t(kBM >> 4) << 24);
+
+struct Maps {
+    CUtensorMap x;   // fp16 [M, K], box 64 x 256, 128-byte swizzle
+    CUtensorMap w;   // u8 [N, K/2], box 128 x 128, 128-byte swizzle
+    CUtensorMap s;   // u16 [N, K/32], box 8 x 128
+};
+
+struct Params {
+    int M, K, N;
+    int tiles_n;      // feature tiles (N / 128, rounded up)
+    int tiles;        // tiles_n * token tiles
+    void* out;
+    int64_t out_ld, out_col0;
+    int out_bf16;
+};
+
+// Bounded wait by plain try_wait polling.  With a suspend-time hint the waits of this kernel
+// slept through tcgen05.commit arrivals (the GEMM ran 8x slower), so it polls.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(err);
+            return false;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// tcgen05 wrappers
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Arrives on `bar` once every tcgen05 operation this thread issued before has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, 128 x 256 x 16, fp16 in, fp32 accumulate.
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
+    return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+#define TC_REG32(v) \
+    "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), \
+    "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), \
+    "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), \
+    "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+#define TC_OUT32(v) \
+    "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), \
+    "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), \
+    "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), \
+    "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+
+// This warp's 32 lanes, 32 consecutive 32-bit columns from `taddr`.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        TC_REG32(v)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : TC_OUT32(v)
+        : "r"(taddr)
+        : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// Dequantization into the MMA's K order
+//
+// A packed 32-block is 16 bytes; byte j holds k = j (low nibble) and k = 16 + j (high
+// nibble).  Word w (bytes 4w..4w+3) yields four fp16 pairs without any per-pair shift:
+//   col 4w+0: low nibbles of bytes 4w, 4w+2      -> k = 4w,      4w+2
+//   col 4w+1: high nibbles of bytes 4w, 4w+2     -> k = 16+4w,   18+4w
+//   col 4w+2: low nibbles of bytes 4w+1, 4w+3    -> k = 4w+1,    4w+3
+//   col 4w+3: high nibbles of bytes 4w+1, 4w+3   -> k = 17+4w,   19+4w
+// so MMA position kk = 2*col + half of a block reads activation k = kPerm[kk]; the pre-pass
+// writes the activations in that order.
+// ---------------------------------------------------------------------------------------
+__host__ __device__ constexpr int perm_src(int kk) {
+    // kk = 8w + p  ->  source k inside the 32-block
+    return (kk & 7) == 0 ? 4 * (kk >> 3)
+         : (kk & 7) == 1 ? 4 * (kk >> 3) + 2
+         : (kk & 7) == 2 ? 16 + 4 * (kk >> 3)
+         : (kk & 7) == 3 ? 18 + 4 * (kk >> 3)
+         : (kk & 7) == 4 ? 4 * (kk >> 3) + 1
+         : (kk & 7) == 5 ? 4 * (kk >> 3) + 3
+         : (kk & 7) == 6 ? 17 + 4 * (kk >> 3)
+                         : 19 + 4 * (kk >> 3);
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// One packed word -> four fp16x2 columns of w = RNE(q * s).  The nibble u is placed in the
+// mantissa of 1024 (low nibble, value 1032 + q after the sign flip) or at 16x (high nibble,
+// value 1152 + 16 q); the subtraction is exact, the product rounds once.  s16 = s / 16.
+__device__ __forceinline__ void dequant_word(uint32_t v, __half2 s, __half2 s16, uint32_t* col) {
+    const __half2 m_lo = bits_h2(0x64086408u), m_hi = bits_h2(0x64806480u);
+    const uint32_t vh = v >> 8;
+    col[0] = h2_bits(__hmul2(__hsub2(bits_h2((v & 0x000F000Fu) ^ 0x64086408u), m_lo), s));
+    col[1] = h2_bits(__hmul2(__hsub2(bits_h2((v & 0x00F000F0u) ^ 0x64806480u), m_hi), s16));
+    col[2] = h2_bits(__hmul2(__hsub2(bits_h2((vh & 0x000F000Fu) ^ 0x64086408u), m_lo), s));
+    col[3] = h2_bits(__hmul2(__hsub2(bits_h2((vh & 0x00F000F0u) ^ 0x64806480u), m_hi), s16));
+}
+
+// ---------------------------------------------------------------------------------------
+// Pre-pass: activations (bf16 or fp32) -> fp16 in the permuted K order.  One thread per
+// 32-block.  Values outside the fp16 range are recorded as a device error.
+// ---------------------------------------------------------------------------------------
+template <bool XF32>
+__global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x, uint4* __restrict__ xp,
+                                                      int64_t nblocks) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= nblocks) return;
+    float v[32];
+    if (XF32) {
+        const float4* src = reinterpret_cast<const float4*>(x) + i * 8;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float4 f = __ldg(src + q);
+            v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+        }
+    } else {
+        const uint4* src = reinterpret_cast<const uint4*>(x) + i * 4;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 u = __ldg(src + q);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                v[8 * q + 2 * e] = __uint_as_float(w[e] << 16);
+                v[8 * q + 2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
+            }
+        }
+    }
+    bool range_ok = true;
+    uint32_t o[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        const float a = v[perm_src(2 * c)], b = v[perm_src(2 * c + 1)];
+        range_ok &= fabsf(a) < 65520.0f && fabsf(b) < 65520.0f;
+        o[c] = h2_bits(__floats2half2_rn(a, b));
+    }
+    if (!range_ok) record_device_error(kDevErrActRange);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) xp[i * 4 + q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+}
+
+// ---------------------------------------------------------------------------------------
+// The GEMM kernel
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* x_full = bars;
+    uint64_t* stage_empty = bars + kStages;
+    uint64_t* a_full = bars + 2 * kStages;
+    uint64_t* w_full = bars + 3 * kStages;
+    uint64_t* w_empty = w_full + kWStages;
+    uint64_t* d_full = w_empty + kWStages;
+    uint64_t* d_empty = d_full + 1;
+    uint64_t* done_bar = d_full + 2;
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + kOffTmemSlot);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kOffAbort);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&x_full[i], 1);
+            mbar_init(&stage_empty[i], 1);
+            mbar_init(&a_full[i], 128);
+        }
+        for (int i = 0; i < kWStages; ++i) {
+            mbar_init(&w_full[i], 1);
+            mbar_init(&w_empty[i], 128);
+        }
+        mbar_init(d_full, 1);
+        mbar_init(d_empty, 128);
+        mbar_init(done_bar, 1);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int n_ks = p.K / kXK;            // activation stages per tile
+    const int n_kw = p.K / kWK;            // weight stages per tile
+    const int my_tiles = p.tiles > static_cast<int>(blockIdx.x)
+                             ? (p.tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                             : 0;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ activation producer
+        if (lane == 0) {
+            prefetch_tensormap(&maps.x);
+            int issued = 0;
+            for (int t = 0; t < my_tiles && !*s_abort; ++t) {
+                const int tile = blockIdx.x + t * gridDim.x;
+                const int tok0 = (tile / p.tiles_n) * kBN;
+                for (int ks = 0; ks < n_ks; ++ks) {
+                    const int s = issued % kStages, r = issued / kStages;
+                    if (r > 0 && !wait_bar(&stage_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
+                        *s_abort = 1;
+                        break;
+                    }
+                    if (*s_abort) break;
+                    mbar_arrive_expect_tx(&x_full[s], kXStageBytes);
+                    tma_load_2d(smem + kOffX + s * kXStageBytes, &maps.x, &x_full[s], ks * kXK, tok0);
+                    ++issued;
+                }
+            }
+            for (int it = issued > kStages ? issued - kStages : 0; it < issued; ++it)
+                if (!wait_bar(&x_full[it % kStages], (it / kStages) & 1, kDevErrDrainWait)) break;
+        }
+    } else if (warp == 2) {
+        // ---------------------------------------------------------------- weight producer
+        if (lane == 0) {
+            prefetch_tensormap(&maps.w);
+            prefetch_tensormap(&maps.s);
+            const uint64_t policy = l2_policy_evict_last();
+            int issued = 0;
+            for (int t = 0; t < my_tiles && !*s_abort; ++t) {
+                const int tile = blockIdx.x + t * gridDim.x;
+                const int row0 = (tile % p.tiles_n) * kBM;
+                for (int kw = 0; kw < n_kw; ++kw) {
+                    const int s = issued % kWStages, r = issued / kWStages;
+                    if (r > 0 && !wait_bar(&w_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
+                        *s_abort = 1;
+                        break;
+                    }
+                    if (*s_abort) break;
+                    mbar_arrive_expect_tx(&w_full[s], kWStageBytes + kSStageBytes);
+                    tma_load_2d_hint(smem + kOffW + s * kWStageBytes, &maps.w, &w_full[s], kw * (kWK / 2), row0, policy);
+                    tma_load_2d_hint(smem + kOffS + s * kSStageBytes, &maps.s, &w_full[s], kw * (kWK / 32), row0, policy);
+                    ++issued;
+                }
+            }
+            for (int it = issued > kWStages ? issued - kWStages : 0; it < issued; ++it)
+                if (!wait_bar(&w_full[it % kWStages], (it / kWStages) & 1, kDevErrDrainWait)) break;
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            int consumed = 0;
+            for (int t = 0; t < my_tiles && !*s_abort; ++t) {
+                if (t > 0 && !wait_bar(d_empty, (t - 1) & 1, kDevErrMmaWait)) {
+                    *s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                bool ok = true;
+                for (int ks = 0; ks < n_ks; ++ks) {
+                    const int s = consumed % kStages, r = consumed / kStages;
+                    if (!wait_bar(&x_full[s], r & 1, kDevErrFullWait) ||
+                        !wait_bar(&a_full[s], r & 1, kDevErrFullWait) || *s_abort) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t bdesc = sw128_desc(base + kOffX + s * kXStageBytes);
+                    const uint32_t a0 = tmem + kAccCols + s * kACols;
+#pragma unroll
+                    for (int k16 = 0; k16 < kXK / 16; ++k16)
+                        mma_ts(tmem, a0 + k16 * 8, bdesc + static_cast<uint64_t>(k16 * 2), (ks | k16) != 0);
+                    tc_commit(&stage_empty[s]);
+                    ++consumed;
+                }
+                if (!ok) {
+                    *s_abort = 1;
+                    break;
+                }
+                tc_commit(d_full);
+            }
+            // every MMA issued above has completed before the tensor memory is freed
+            tc_commit(done_bar);
+            wait_bar(done_bar, 0, kDevErrMmaWait);
+        }
+    } else if (warp >= kDequantWarp0) {
+        // ----------------------------------------------------- dequantizer + epilogue
+        const int sub = warp & 3;                  // TMEM lane quarter this warp may access
+        const int row = sub * 32 + lane;           // weight row inside the tile
+        const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
+        int w_used = 0, a_made = 0;
+        for (int t = 0; t < my_tiles; ++t) {
+            const int tile = blockIdx.x + t * gridDim.x;
+            const int feat = (tile % p.tiles_n) * kBM + row;
+            const int tok0 = (tile / p.tiles_n) * kBN;
+            bool ok = true;
+            for (int kw = 0; kw < n_kw && ok; ++kw) {
+                const int ws = w_used % kWStages;
+                if (!wait_bar(&w_full[ws], (w_used / kWStages) & 1, kDevErrFullWait) || *s_abort) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t wrow = base + kOffW + ws * kWStageBytes + row * 128;
+                uint4 chunk[8];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) chunk[c] = lds_u128(wrow + ((c ^ (row & 7)) << 4));
+                const uint4 sc = lds_u128(base + kOffS + ws * kSStageBytes + row * 16);
+                mbar_arrive(&w_empty[ws]);
+                ++w_used;
+                const uint32_t sw[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+                for (int q = 0; q < kSubs; ++q) {
+                    const int s = a_made % kStages, r = a_made / kStages;
+                    if (r > 0 && !wait_bar(&stage_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
+                        ok = false;
+                        break;
+                    }
+                    if (*s_abort) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint32_t col[32];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int c = 2 * q + h;
+                        const __half2 s2 = __half2half2(bits_h2(sw[c >> 1]).x);
+                        const __half2 sv = (c & 1) ? __half2half2(bits_h2(sw[c >> 1]).y) : s2;
+                        const __half2 s16 = __hmul2(sv, bits_h2(0x2C002C00u));   // x 1/16
+                        const uint4 u = chunk[c];
+                        dequant_word(u.x, sv, s16, &col[16 * h + 0]);
+                        dequant_word(u.y, sv, s16, &col[16 * h + 4]);
+                        dequant_word(u.z, sv, s16, &col[16 * h + 8]);
+                        dequant_word(u.w, sv, s16, &col[16 * h + 12]);
+                    }
+                    tmem_st32(tmem + lane_addr + kAccCols + s * kACols, col);
+                    tc_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&a_full[s]);
+                    ++a_made;
+                }
+            }
+            if (!ok) {
+                *s_abort = 1;
+                break;
+            }
+            // ---- epilogue: accumulator -> out[token][feature]
+            if (!wait_bar(d_full, t & 1, kDevErrMmaWait)) {
+                *s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            const bool feat_ok = feat < p.N;
+#pragma unroll 1
+            for (int c0 = 0; c0 < kBN; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_addr + c0, v);
+                tc_wait_ld();
+                if (feat_ok) {
+                    const int nt = min(32, p.M - (tok0 + c0));
+                    if (p.out_bf16) {
+                        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + p.out_col0 + feat +
+                                           static_cast<int64_t>(tok0 + c0) * p.out_ld;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nt) o[j * p.out_ld] = __float2bfloat16_rn(__uint_as_float(v[j]));
+                    } else {
+                        float* o = reinterpret_cast<float*>(p.out) + p.out_col0 + feat +
+                                   static_cast<int64_t>(tok0 + c0) * p.out_ld;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nt) o[j * p.out_ld] = __uint_as_float(v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(d_empty);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace tc
+
+bool tc_supports(const GemmArgs& a) {
+    if (a.fmt != BYBYCU_FMT_Q4B32) return false;
+    if (a.K < tc::kWK || a.K % tc::kWK != 0 || a.M < 1 || a.N < 1) return false;
+    if (a.x_dtype != BYBYCU_DT_BF16 && a.x_dtype != BYBYCU_DT_F32) return false;
+    if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0) return false;
+    if (reinterpret_cast<uintptr_t>(a.packed) % 16 != 0) return false;
+    if ((reinterpret_cast<uintptr_t>(a.packed) + static_cast<uintptr_t>(a.scale_base)) % 16 != 0) return false;
+    const size_t esz = a.out_dtype == BYBYCU_DT_BF16 ? 2 : 4;
+    if (reinterpret_cast<uintptr_t>(a.out) % esz != 0) return false;
+    DeviceInfo info;
+    if (current_device_info(&info) != BYBYCU_OK) return false;
+    return info.cc_major == 10 && info.max_smem_optin >= static_cast<int>(tc::kSmemBytes);
+}
+
+// Stream-ordered scratch for the staged activations: one pool per device that keeps its
+// memory between calls (the default pool returns it at every synchronization, and mapping
+// it again costs more than the GEMM).
+static int scratch_pool(int device, cudaMemPool_t* pool) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {};
+    if (device < 0 || device >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", device);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!pools[device]) {
+        cudaMemPoolProps props = {};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        cudaMemPool_t p = nullptr;
+        BYBYCU_CUDA_TRY(cudaMemPoolCreate(&p, &props));
+        uint64_t keep = UINT64_MAX;
+        cudaError_t e = cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+        if (e != cudaSuccess) {
+            cudaMemPoolDestroy(p);
+            return cuda_fail(e, "cudaMemPoolSetAttribute(release threshold)");
+        }
+        pools[device] = p;
+    }
+    *pool = pools[device];
+    return BYBYCU_OK;
+}
+
+int launch_tc(const GemmArgs& a) {
+    if (!tc_supports(a))
+        return set_error(BYBYCU_ERR_SHAPE,
+                         "tensor-core route needs format 2, K %% 256 == 0, 16-byte aligned x, packed and scales "
+                         "(M=%d K=%d N=%d)", a.M, a.K, a.N);
+    DeviceInfo info;
+    if (int rc = current_device_info(&info)) return rc;
+    static std::once_flag attr_once[16];
+    static cudaError_t attr_rc[16];
+    const int dev = info.device & 15;
+    std::call_once(attr_once[dev], [&] {
+        attr_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(tc::kSmemBytes));
+    });
+    if (attr_rc[dev] != cudaSuccess) return cuda_fail(attr_rc[dev], "cudaFuncSetAttribute(tc gemm)");
+
+    // activations -> fp16, permuted, in stream-ordered scratch
+    const size_t xp_bytes = static_cast<size_t>(a.M) * a.K * 2;
+    void* xp = nullptr;
+    cudaMemPool_t pool = nullptr;
+    if (int rc = scratch_pool(info.device, &pool)) return rc;
+    BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
+    const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
+    const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
+    if (a.x_dtype == BYBYCU_DT_F32)
+        tc::stage_x_kernel<true><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+    else
+        tc::stage_x_kernel<false><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+    cudaError_t le = cudaGetLastError();
+    if (le != cudaSuccess) {
+        cudaFreeAsync(xp, a.stream);
+        return cuda_fail(le, "stage_x_kernel");
+    }
+
+    tc::Maps maps;
+    int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xp, a.K, a.M,
+                                  static_cast<uint64_t>(a.K) * 2, tc::kXK, tc::kBN, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    if (!rc)
+        rc = encode_tensor_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.N, a.K / 2,
+                                  tc::kWK / 2, tc::kBM, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    if (!rc)
+        rc = encode_tensor_map_2d(&maps.s, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.packed + a.scale_base, a.K / 32, a.N,
+                                  static_cast<uint64_t>(a.K / 32) * 2, tc::kWK / 32, tc::kBM,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+    if (rc) {
+        cudaFreeAsync(xp, a.stream);
+        return rc;
+    }
+    tc::Params p;
+    p.M = a.M;
+    p.K = a.K;
+    p.N = a.N;
+    p.tiles_n = static_cast<int>(ceil_div(a.N, tc::kBM));
+    const int64_t tiles = static_cast<int64_t>(p.tiles_n) * ceil_div(a.M, tc::kBN);
+    if (tiles > (1 << 30)) {
+        cudaFreeAsync(xp, a.stream);
+        return set_error(BYBYCU_ERR_SHAPE, "tensor-core route: too many tiles (M=%d N=%d)", a.M, a.N);
+    }
+    p.tiles = static_cast<int>(tiles);
+    p.out = a.out;
+    p.out_ld = a.out_ld;
+    p.out_col0 = a.out_col0;
+    p.out_bf16 = a.out_dtype == BYBYCU_DT_BF16;
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, info.sm_count));
+    tc::gemm_kernel<<<grid, tc::kThreads, tc::kSmemBytes, a.stream>>>(maps, p);
+    le = cudaGetLastError();
+    cudaError_t fe = cudaFreeAsync(xp, a.stream);
+    if (le != cudaSuccess) return cuda_fail(le, "tc gemm_kernel");
+    if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc scratch)");
+    return BYBYCU_OK;
 }
 
 }  // namespace bybycu

@@ -19,7 +19,9 @@ torch = pytest.importorskip("torch")
 from bybylang_b200 import _lib  # noqa: E402
 from bybylang_b200 import gpubackend as gb  # noqa: E402
 
-DEV = "cuda:0"
+from gpu_helpers import DEV, dev, q4_slot, run  # noqa: E402
+from gpu_helpers import assert_close as _assert_close  # noqa: E402
+
 PEAK_TOL = 1e-4
 ELEM_TOL = 1e-3
 
@@ -35,35 +37,8 @@ def lib():
     return _lib.load()
 
 
-def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
-
-
-def run(fmt, M, K, N, x, packed, *, scale_base=0, lut=None, route=_lib.ROUTE_AUTO, out_dtype=torch.float32):
-    out = torch.full((M, N), float("nan"), dtype=out_dtype, device=DEV)
-    gb.tile_gemm(fmt, x, packed, out, M=M, K=K, N=N, scale_base=scale_base, lut=lut, route=route)
-    torch.cuda.synchronize()
-    return out
-
-
-def q4_slot(p, s):
-    """Nibbles then fp16 scales at a 16-byte aligned scale_base, as one device uint8 slot."""
-    nb = p.size
-    sb = (nb + 15) // 16 * 16
-    blob = np.zeros(sb + s.size * 2, np.uint8)
-    blob[:nb] = p.ravel()
-    blob[sb:] = np.ascontiguousarray(s, np.uint16).view(np.uint8).ravel()
-    return dev(blob), sb
-
-
 def assert_close(want, got, peak_tol=PEAK_TOL, elem_tol=ELEM_TOL, what=""):
-    want = np.asarray(want, np.float64)
-    got = np.asarray(got, np.float64)
-    assert np.isfinite(got).all(), what
-    d = np.abs(want - got)
-    peak = max(1.0, float(np.abs(want).max()))
-    assert d.max() <= peak_tol * peak, f"{what}: max|diff| {d.max():.3e} peak {peak:.3f}"
-    assert (d <= elem_tol * np.maximum(1.0, np.abs(want))).all(), f"{what}: per-element"
+    _assert_close(want, got, peak_tol, elem_tol, what)
 
 
 # ----------------------------------------------------------------------------------------

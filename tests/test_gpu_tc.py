@@ -1,0 +1,147 @@
+"""GPU parity of the tensor-core (tcgen05) prefill route against the reference's CPU arithmetic.
+
+Tolerance: the route rounds every dequantised weight once to fp16 (w = RNE(q * s)) and the
+activations to fp16 (exact for bf16 inputs inside the fp16 range), then accumulates in fp32 -
+the same rounding the reference accepts for its fp16 cooperative lowering
+(micro_kernel/tile_gemm.nim:322-325, 414).  Outputs are checked with the reference test's
+metric, max|diff| <= tol * max(1, max|ref|) (tests/t_fp4_tile_gemm.nim:54-67), at the path's
+tolerance tol = 1e-3 (vulkan_driver.nim:2754); the measured error is ~1e-4.  A per-element
+relative bound does not apply: rounding W to fp16 leaves an absolute error of about
+2^-12 * sqrt(K) * rms(x * w) on every output, whatever its size.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from bybylang_b200 import _lib  # noqa: E402
+from bybylang_b200 import gpubackend as gb  # noqa: E402
+
+from gpu_helpers import assert_close, dev, peak_err, q4_slot, run  # noqa: E402
+
+TC_TOL = 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    gb.ensureGpuInit(gb.GpuBackend.gbCuda, 0)
+    yield
+    assert _lib.device_error() == 0
+
+
+def _case(O, M, K, N, seed=0):
+    p, s = O.gen_q4b32(N, K, seed=O.Xorshift32.SEED + seed)
+    xb = O.gen_x_bf16(M, K, seed=O.Xorshift32.SEED + 2 + seed)
+    slot, sb = q4_slot(p, s)
+    return p, s, xb, slot, sb
+
+
+def test_tc_golden_cases(golden, oracle_mod):
+    """The reference VM's outputs (tests/golden/ref_q4b32.npz) for every case the route tiles."""
+    g = golden["ref_q4b32"]
+    ran = 0
+    for i in range(8):
+        M, K, N = (int(v) for v in g[f"q4_{i}_shape"])
+        if K % 256:
+            continue
+        slot, sb = q4_slot(g[f"q4_{i}_packed"], g[f"q4_{i}_scales"])
+        xb = dev(g[f"q4_{i}_x_bf16"]).view(torch.bfloat16)
+        out = run(2, M, K, N, xb, slot, scale_base=sb, route=_lib.ROUTE_TC)
+        assert_close(g[f"q4_{i}_vm"], out.cpu().numpy(), TC_TOL, what=f"case {i} bf16")
+        xf = dev(oracle_mod.bf16_to_f32(g[f"q4_{i}_x_bf16"]))
+        out = run(2, M, K, N, xf, slot, scale_base=sb, route=_lib.ROUTE_TC)
+        assert_close(g[f"q4_{i}_vm"], out.cpu().numpy(), TC_TOL, what=f"case {i} f32")
+        ran += 1
+    assert ran == 3
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 256, 1), (17, 256, 130), (256, 512, 128), (300, 768, 200),
+                                   (513, 1024, 384), (1000, 2048, 77)])
+def test_tc_ragged_shapes_against_oracle(M, K, N, oracle_mod):
+    """Partial token tiles (M % 256) and partial weight-row tiles (N % 128)."""
+    O = oracle_mod
+    p, s, xb, slot, sb = _case(O, M, K, N, seed=M + N)
+    want = O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, M, K, N, threads=8)
+    out = run(2, M, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb, route=_lib.ROUTE_TC)
+    assert_close(want, out.cpu().numpy(), TC_TOL, what=f"M={M} K={K} N={N}")
+
+
+def test_tc_prefill_c3_full_size():
+    """Config C3 (M=2048, K=N=4096), every output: against the SIMT route, which is
+    bit-identical to the reference CPU VM (checked in test_gpu_parity.py)."""
+    from bybylang_b200.formats import synthetic_q4b32, synthetic_x
+    M, K, N = 2048, 4096, 4096
+    nib, sc = synthetic_q4b32(N, K, seed=11, device="cuda:0")
+    w = gb.Q4B32Weights(nib, sc, device="cuda:0")
+    x = synthetic_x(M, K, seed=12, device="cuda:0")
+    tc = w.matmul(x, route=_lib.ROUTE_TC)
+    ref = w.matmul(x, route=_lib.ROUTE_SIMT)
+    torch.cuda.synchronize()
+    err = peak_err(ref.cpu().numpy(), tc.cpu().numpy())
+    assert err <= TC_TOL, f"peak-normalised error {err:.3e}"
+    assert err <= 5e-4   # fp16 weights: ~1e-4 expected; a layout slip gives O(1)
+
+
+def test_tc_prefill_rows_against_oracle(oracle_mod):
+    """C3 shape, sampled token rows through the CPU oracle directly."""
+    O = oracle_mod
+    M, K, N = 2048, 4096, 4096
+    p, s, xb, slot, sb = _case(O, M, K, N, seed=5)
+    out = run(2, M, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb, route=_lib.ROUTE_TC).cpu().numpy()
+    rows = np.r_[0:8, 255:259, 1023:1027, 2040:2048]
+    want = O.tile_gemm_q4b32(O.bf16_to_f32(xb[rows]), p, s, len(rows), K, N, threads=8)
+    assert_close(want, out[rows], TC_TOL, what="C3 sampled rows")
+
+
+def test_tc_bf16_output_is_rounded_f32_output(oracle_mod):
+    O = oracle_mod
+    M, K, N = 300, 1024, 256
+    p, s, xb, slot, sb = _case(O, M, K, N, seed=3)
+    x = dev(xb).view(torch.bfloat16)
+    f32 = run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_TC)
+    b16 = run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_TC, out_dtype=torch.bfloat16)
+    assert torch.equal(f32.to(torch.bfloat16), b16)
+
+
+def test_tc_deterministic_across_calls(oracle_mod):
+    O = oracle_mod
+    M, K, N = 512, 2048, 640
+    p, s, xb, slot, sb = _case(O, M, K, N, seed=4)
+    x = dev(xb).view(torch.bfloat16)
+    a = run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_TC)
+    b = run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_TC)
+    assert torch.equal(a, b)
+
+
+def test_auto_route_prefill_is_tc(oracle_mod):
+    assert gb.route_for(2, 2048, 4096, 4096) == _lib.ROUTE_TC
+    assert gb.route_for(2, 64, 4096, 128256) == _lib.ROUTE_TC
+    assert gb.route_for(2, 16, 4096, 4096) == _lib.ROUTE_GEMV
+    assert gb.route_for(2, 64, 4128, 4096) != _lib.ROUTE_TC    # K % 256 != 0
+    O = oracle_mod
+    M, K, N = 40, 512, 96
+    p, s, xb, slot, sb = _case(O, M, K, N, seed=6)
+    out = run(2, M, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb)
+    assert_close(O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, M, K, N), out.cpu().numpy(), TC_TOL)
+
+
+def test_tc_rejects_untileable_shapes(oracle_mod):
+    O = oracle_mod
+    M, K, N = 32, 288, 64
+    p, s, xb, slot, sb = _case(O, M, K, N)
+    with pytest.raises(_lib.BybyCudaError, match="tensor-core route"):
+        run(2, M, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb, route=_lib.ROUTE_TC)
+
+
+def test_tc_activation_outside_fp16_range_is_reported(oracle_mod):
+    """|x| >= 65520 cannot be staged as fp16: the pre-pass records device error 7 (no fault)."""
+    O = oracle_mod
+    M, K, N = 20, 256, 128
+    p, s, xb, slot, sb = _case(O, M, K, N)
+    x = dev(xb).view(torch.bfloat16).clone()
+    x[3, 17] = 1.0e6
+    run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_TC)
+    assert _lib.device_error() == 7
+    assert _lib.device_error() == 0   # read-and-clear

@@ -63,6 +63,7 @@ SIGNATURES = {
                          _vp, _i32, _i64, _i32, _vp],
     "bybycu_tile_gemm_host": [_i32, _i32, _i32, _i32, _vp, _i32, _vp, _i64, _i64, _vp, _i64, _i64,
                               _vp, _i32, _vp, _vp, _i32, _vp],
+    "bybycu_tile_gemm_noalloc": [_i32, _i32, _i32, _vp, _i32, _i64, _vp, _i64, _i64, _vp, _i32, _i64, _vp],
     "bybycu_dequant": [_i32, _i32, _i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp],
     "bybycu_route_for": [_i32, _i32, _i32, _i32, _i32, C.POINTER(_i32)],
     "bybycu_vm_run_slots": [C.POINTER(_u32), _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32,

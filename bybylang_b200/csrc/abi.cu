@@ -280,6 +280,26 @@ int bybycu_tile_gemm(int fmt, int M, int K, int N, const void* x, int x_dtype, i
                           out_dtype, out_len, route, static_cast<cudaStream_t>(stream));
 }
 
+int bybycu_tile_gemm_noalloc(int M, int K, int N, const void* x, int x_dtype, int64_t x_len, const void* packed,
+                             int64_t packed_len, int64_t scale_base, void* out, int out_dtype, int64_t out_len,
+                             void* stream) {
+    if (!x || !packed || !out) return set_error(BYBYCU_ERR_ARGS, "tile GEMM slot is missing");
+    if ((x_dtype != BYBYCU_DT_F32 && x_dtype != BYBYCU_DT_BF16) ||
+        (out_dtype != BYBYCU_DT_F32 && out_dtype != BYBYCU_DT_BF16))
+        return set_error(BYBYCU_ERR_ARGS, "tile GEMM element types must be F32 or BF16");
+    if (int rc = check_tile_gemm(BYBYCU_FMT_Q4B32, M, K, N, x_len, packed_len, scale_base, 0, 0, out_len)) return rc;
+    GemmArgs a;
+    a.fmt = BYBYCU_FMT_Q4B32; a.M = M; a.K = K; a.N = N;
+    a.x = x; a.x_dtype = x_dtype;
+    a.packed = static_cast<const uint8_t*>(packed);
+    a.packed_len = packed_len;
+    a.scale_base = scale_base;
+    a.out = out; a.out_dtype = out_dtype;
+    a.out_ld = N; a.out_col0 = 0;
+    a.stream = static_cast<cudaStream_t>(stream);
+    return launch_tc_static_scratch(a);
+}
+
 int bybycu_tile_gemm_host(int fmt, int M, int K, int N, const void* x_host, int x_dtype, const void* packed,
                           int64_t packed_len, int64_t scale_base, const float* lut, int64_t lut_len, int64_t lut_base,
                           void* out_host, int out_dtype, void* x_dev, void* out_dev, int route, void* stream) {

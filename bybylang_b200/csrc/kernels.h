@@ -33,6 +33,8 @@ int launch_gemv(const GemmArgs& a);
 // Prefill GEMM route: tcgen05 MMAs from shared-memory fp16 tiles, fp32 accumulators in TMEM.
 bool tc_supports(const GemmArgs& a);
 int launch_tc(const GemmArgs& a);
+// The same route staging its activations in a fixed module array instead of pool memory.
+int launch_tc_static_scratch(const GemmArgs& a);
 
 int launch_dequant(int fmt, int K, int N, const uint8_t* packed, int64_t scale_base,
                    const float* lut, float* w, cudaStream_t stream);

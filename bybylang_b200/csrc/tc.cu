@@ -518,39 +518,34 @@ static int scratch_pool(int device, cudaMemPool_t* pool) {
     return BYBYCU_OK;
 }
 
-int launch_tc(const GemmArgs& a) {
+// Checks, device info and the kernel attribute shared by both scratch sources.
+static int tc_prepare(const GemmArgs& a, DeviceInfo* info) {
     if (!tc_supports(a))
         return set_error(BYBYCU_ERR_SHAPE,
                          "tensor-core route needs format 2, K %% 256 == 0, 16-byte aligned x, packed and scales "
                          "(M=%d K=%d N=%d)", a.M, a.K, a.N);
-    DeviceInfo info;
-    if (int rc = current_device_info(&info)) return rc;
+    if (int rc = current_device_info(info)) return rc;
     static std::once_flag attr_once[16];
     static cudaError_t attr_rc[16];
-    const int dev = info.device & 15;
+    const int dev = info->device & 15;
     std::call_once(attr_once[dev], [&] {
         attr_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(tc::kSmemBytes));
     });
     if (attr_rc[dev] != cudaSuccess) return cuda_fail(attr_rc[dev], "cudaFuncSetAttribute(tc gemm)");
+    return BYBYCU_OK;
+}
 
-    // activations -> fp16, permuted, in stream-ordered scratch
-    const size_t xp_bytes = static_cast<size_t>(a.M) * a.K * 2;
-    void* xp = nullptr;
-    cudaMemPool_t pool = nullptr;
-    if (int rc = scratch_pool(info.device, &pool)) return rc;
-    BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
+// The staging pass and the GEMM, with `xp` (M * K fp16) as the staging buffer.  Allocates
+// nothing.
+static int tc_run(const GemmArgs& a, const DeviceInfo& info, void* xp) {
     const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
     const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
     if (a.x_dtype == BYBYCU_DT_F32)
         tc::stage_x_kernel<true><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
     else
         tc::stage_x_kernel<false><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
-    cudaError_t le = cudaGetLastError();
-    if (le != cudaSuccess) {
-        cudaFreeAsync(xp, a.stream);
-        return cuda_fail(le, "stage_x_kernel");
-    }
+    BYBYCU_LAUNCH_CHECK("stage_x_kernel");
 
     tc::Maps maps;
     int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xp, a.K, a.M,
@@ -563,20 +558,14 @@ int launch_tc(const GemmArgs& a) {
         rc = encode_tensor_map_2d(&maps.s, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.packed + a.scale_base, a.K / 32, a.N,
                                   static_cast<uint64_t>(a.K / 32) * 2, tc::kWK / 32, tc::kBM,
                                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
-    if (rc) {
-        cudaFreeAsync(xp, a.stream);
-        return rc;
-    }
+    if (rc) return rc;
     tc::Params p;
     p.M = a.M;
     p.K = a.K;
     p.N = a.N;
     p.tiles_n = static_cast<int>(ceil_div(a.N, tc::kBM));
     const int64_t tiles = static_cast<int64_t>(p.tiles_n) * ceil_div(a.M, tc::kBN);
-    if (tiles > (1 << 30)) {
-        cudaFreeAsync(xp, a.stream);
-        return set_error(BYBYCU_ERR_SHAPE, "tensor-core route: too many tiles (M=%d N=%d)", a.M, a.N);
-    }
+    if (tiles > (1 << 30)) return set_error(BYBYCU_ERR_SHAPE, "tensor-core route: too many tiles (M=%d N=%d)", a.M, a.N);
     p.tiles = static_cast<int>(tiles);
     p.out = a.out;
     p.out_ld = a.out_ld;
@@ -584,11 +573,60 @@ int launch_tc(const GemmArgs& a) {
     p.out_bf16 = a.out_dtype == BYBYCU_DT_BF16;
     const int grid = static_cast<int>(std::min<int64_t>(tiles, info.sm_count));
     tc::gemm_kernel<<<grid, tc::kThreads, tc::kSmemBytes, a.stream>>>(maps, p);
-    le = cudaGetLastError();
-    cudaError_t fe = cudaFreeAsync(xp, a.stream);
-    if (le != cudaSuccess) return cuda_fail(le, "tc gemm_kernel");
+    BYBYCU_LAUNCH_CHECK("tc gemm_kernel");
+    return BYBYCU_OK;
+}
+
+int launch_tc(const GemmArgs& a) {
+    DeviceInfo info;
+    if (int rc = tc_prepare(a, &info)) return rc;
+    // activations -> fp16, permuted, in stream-ordered scratch
+    const size_t xp_bytes = static_cast<size_t>(a.M) * a.K * 2;
+    void* xp = nullptr;
+    cudaMemPool_t pool = nullptr;
+    if (int rc = scratch_pool(info.device, &pool)) return rc;
+    BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
+    const int rc = tc_run(a, info, xp);
+    const cudaError_t fe = cudaFreeAsync(xp, a.stream);
+    if (rc) return rc;
     if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc scratch)");
     return BYBYCU_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// The same GEMM with staging scratch that is never allocated at call time: a fixed array in
+// the module's device memory, reserved when the library loads on a device.
+// ---------------------------------------------------------------------------------------
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;   // M * K <= 16 Mi activations
+__device__ __align__(256) uint8_t g_tc_static_scratch[kStaticScratchBytes];
+
+// The array's address on the current device, looked up once per device.
+static int static_scratch(int device, void** ptr) {
+    static std::mutex mu;
+    static void* ptrs[64] = {};
+    if (device < 0 || device >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", device);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[device]) {
+        void* p = nullptr;
+        BYBYCU_CUDA_TRY(cudaGetSymbolAddress(&p, g_tc_static_scratch));
+        ptrs[device] = p;
+    }
+    *ptr = ptrs[device];
+    return BYBYCU_OK;
+}
+
+int launch_tc_static_scratch(const GemmArgs& a) {
+    const size_t need = static_cast<size_t>(a.M) * a.K * 2;
+    if (need > kStaticScratchBytes)
+        return set_error(BYBYCU_ERR_RANGE,
+                         "static-scratch tensor-core GEMM stages M*K fp16 activations in a fixed %zu MiB array: "
+                         "M=%d K=%d needs %zu bytes (at most M*K = %zu)",
+                         kStaticScratchBytes >> 20, a.M, a.K, need, kStaticScratchBytes / 2);
+    DeviceInfo info;
+    if (int rc = tc_prepare(a, &info)) return rc;
+    void* xp = nullptr;
+    if (int rc = static_scratch(info.device, &xp)) return rc;
+    return tc_run(a, info, xp);
 }
 
 }  // namespace bybycu

@@ -130,6 +130,28 @@ BYBYCU_API int bybycu_tile_gemm_host(int fmt, int M, int K, int N,
                           void* out_host, int out_dtype,
                           void* x_dev, void* out_dev, int route, void* stream);
 
+/* The format-2 (Q4B32) tensor-core GEMM of bybycu_tile_gemm (route TC) for callers that
+ * cannot allocate device memory at call time - e.g. a serving process that reserved
+ * nearly all HBM for its own caches at start-up, where a call-time allocation can fail or
+ * stall on the allocator.  This entry point has no reference counterpart: the reference
+ * never stages activations, so it never needs scratch.
+ *   Scratch: the fp16 staging copy of x (M*K*2 bytes) lives in one fixed 32 MiB array of
+ *   the library's device memory, reserved when the library loads on a device; its address
+ *   is looked up once per device (cudaGetSymbolAddress).  Nothing is allocated or freed
+ *   per call.  No part of it needs to start at zero: every byte the GEMM reads is written
+ *   by the same call first.
+ *   Limit: M*K <= 16,777,216 (e.g. M=4096 at K=4096); larger shapes fail with
+ *   BYBYCU_ERR_RANGE before anything is launched.  Shapes the TC route cannot tile
+ *   (K % 256 != 0, unaligned slots) fail with BYBYCU_ERR_SHAPE.
+ *   Concurrency: there is one array per device.  Calls on the same stream are ordered and
+ *   safe; calls that may run at the same time on one device (different streams, or
+ *   different host threads) race on the array and corrupt each other's results.
+ * Arguments as bybycu_tile_gemm (fmt = 2, no table); asynchronous on `stream`. */
+BYBYCU_API int bybycu_tile_gemm_noalloc(int M, int K, int N,
+                             const void* x, int x_dtype, int64_t x_len,
+                             const void* packed, int64_t packed_len, int64_t scale_base,
+                             void* out, int out_dtype, int64_t out_len, void* stream);
+
 /* Dequantises W to fp32 w[N, K] (the bit-exact check of the format decode:
  * cpu_vm.c:612-617 for format 0). */
 BYBYCU_API int bybycu_dequant(int fmt, int K, int N, const void* packed, int64_t packed_len,

@@ -55,6 +55,19 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def profiled_traffic(summary: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the bench kernel,
+    from the committed ncu summary under profiles/ (one `--set full` capture)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", summary)) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
 
@@ -373,7 +386,9 @@ def main():
                        "global_batch": M_DEC, "algorithmic_bytes_per_step": STEP_BYTES,
                        "timing": "CUDA graph replay, CUDA events on the launching stream"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(achieved / hbm_peak, 4), "traffic": None, "peak_kind": peak_kind},
+                         "frac": round(achieved / hbm_peak, 4), "traffic": profiled_traffic("gemv_m1_decode_c2.md"),
+                         "traffic_source": "ncu --set full, one launch: profiles/gemv_m1_decode_c2.md",
+                         "algorithmic_bytes": STEP_BYTES, "peak_kind": peak_kind},
             "cpu_baseline": base, "e2e": e2e, "gpu_launches": steps * launches_per_step, "clocks": clocks,
             "prefill": prefill,
         }

@@ -1,5 +1,5 @@
 // tc.cu - the prefill GEMM route: Q4B32 weights x activations on the 5th-generation tensor
-// cores (tcgen05), one persistent CTA per SM.
+// cores (tcgen05), CTA pairs (cta_group::2) persistent over the output tiles.
 //
 // The reference computes the same product with OP_TILE_GEMM's "matmul" phase
 // (micro_kernel/tile_gemm.nim:20-34, backends/cpu/cpu_vm.c:605-626): out[m][n] =
@@ -8,15 +8,17 @@
 //   * a pre-pass converts the activations to fp16 (exact for bf16 inputs inside the fp16
 //     range) and permutes K inside every 32-block into the order the dequantizer produces
 //     weight pairs in (stage_x_kernel);
-//   * four dequant warps turn each weight row's nibbles into fp16 w = RNE(q * s) - one
-//     rounding per weight - and store them straight into tensor memory, where they are the
-//     MMA's A operand (128 weight rows = 128 TMEM lanes, two K elements per 32-bit column);
-//     no shared-memory traffic for A;
-//   * the fp16 activations come by TMA (128-byte swizzle) into a shared-memory ring and are
-//     the MMA's B operand (256 tokens per tile, K-major);
-//   * one thread issues tcgen05.mma 128x256x16 into an fp32 accumulator in TMEM;
-//   * after the K loop the same four warps read the accumulator back (tcgen05.ld) and store
-//     out[token][feature] (fp32 or bf16).
+//   * a pair tile is 256 weight rows (output features) x 128 tokens.  Each CTA of the pair
+//     dequantizes its 128 weight rows into fp16 w = RNE(q * s) - one rounding per weight -
+//     straight into its own tensor memory, where they are the MMA's A operand (one row per
+//     TMEM lane, two K elements per 32-bit column): no shared-memory traffic for A;
+//   * each CTA TMA-loads 64 of the tile's 128 token rows (128-byte swizzle); the pair's MMA
+//     (M=256, N=128, K=16) reads both halves, so every activation byte crosses a shared-memory
+//     port once per 256 weight rows - half of what a single-CTA 128-row tile needs, which is
+//     what bounds the tensor pipe here;
+//   * one thread of the even CTA issues the MMAs into fp32 accumulators in both CTAs' TMEM;
+//     the accumulators are double-buffered, so the epilogue warps read tile t back
+//     (tcgen05.ld) and store out[token][feature] while the MMAs of tile t+1 run.
 //
 // Every wait is bounded (%globaltimer): on a timeout the kernel records an error code in
 // g_device_error, drains its copies and MMAs, frees its tensor memory and returns.
@@ -27,47 +29,63 @@
 namespace bybycu {
 namespace tc {
 
-constexpr int kBM = 128;          // weight rows (output features) per tile = MMA M
-constexpr int kBN = 256;          // tokens per tile = MMA N
-constexpr int kXK = 64;           // K per activation stage: one 128-byte swizzle row of fp16
-constexpr int kWK = 256;          // K per weight stage: 128 packed bytes per row
-constexpr int kStages = 4;        // activation stages in shared memory = A slots in TMEM
-constexpr int kWStages = 3;       // weight stages in shared memory
-constexpr int kSubs = kWK / kXK;  // activation stages per weight stage
-constexpr int kThreads = 256;     // 8 warps: X TMA, MMA, W TMA, idle, 4 x dequant/epilogue
+constexpr int kRowsCta = 128;       // weight rows per CTA (MMA M = 2 x 128 per pair)
+constexpr int kRowsPair = 256;
+constexpr int kBN = 128;            // tokens per pair tile = MMA N
+constexpr int kTokCta = kBN / 2;    // token rows each CTA loads
+constexpr int kXK = 128;            // K per activation stage: two 128-byte swizzle rows of fp16
+constexpr int kXSub = 64;           // K per 128-byte swizzle row (one TMA box)
+constexpr int kWK = 256;            // K per weight stage: 128 packed bytes per row
+constexpr int kStages = 4;          // activation stages in shared memory = A slots in TMEM
+constexpr int kWStages = 3;         // weight stages in shared memory
+constexpr int kSubs = kWK / kXK;    // activation stages per weight stage
+// 16 warps: 0 X TMA, 1 MMA (even CTA) + TMEM alloc, 2 W TMA, 3 X relay (odd CTA),
+// 4-11 dequant (two groups of four: even / odd activation stages), 12-15 epilogue
+constexpr int kThreads = 512;
 constexpr int kDequantWarp0 = 4;
+constexpr int kEpilogueWarp0 = 12;
 
-constexpr uint32_t kXStageBytes = kBN * kXK * 2;    // 32 KiB
-constexpr uint32_t kWStageBytes = kBM * kWK / 2;    // 16 KiB
-constexpr uint32_t kSStageBytes = kBM * (kWK / 32) * 2;  // 2 KiB
+constexpr uint32_t kXStageBytes = kTokCta * kXK * 2;         // 16 KiB per CTA
+constexpr uint32_t kXSubBytes = kTokCta * kXSub * 2;         // 8 KiB
+constexpr uint32_t kWStageBytes = kRowsCta * kWK / 2;        // 16 KiB
+constexpr uint32_t kSStageBytes = kRowsCta * (kWK / 32) * 2; // 2 KiB
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccCols = kBN;                 // fp32 accumulator: one column per token
+constexpr uint32_t kAccCols = kBN;                 // one accumulator buffer: a column per token
+constexpr uint32_t kAOff = 2 * kAccCols;           // A slots after the two accumulator buffers
 constexpr uint32_t kACols = kXK / 2;               // A slot: two fp16 per column
+static_assert(kAOff + kStages * kACols <= kTmemCols, "tensor memory budget");
 
 constexpr uint32_t kOffX = 0;
 constexpr uint32_t kOffW = kOffX + kStages * kXStageBytes;
 constexpr uint32_t kOffS = kOffW + kWStages * kWStageBytes;
 constexpr uint32_t kOffBar = kOffS + kWStages * kSStageBytes;
-// barriers: x_full, stage_empty, a_full [kStages]; w_full, w_empty [kWStages]; d_full,
-// d_empty, done; then the TMEM base address and the abort flag
-constexpr uint32_t kNumBars = 3 * kStages + 2 * kWStages + 3;
+// barriers: full, stage_empty [kStages]; w_full, w_empty [kWStages]; d_full, d_empty [2];
+// done; then the TMEM base address and the abort flag
+constexpr uint32_t kNumBars = 2 * kStages + 2 * kWStages + 5;
+// Arrivals that complete a stage on rank 0: its own TMA (with the bytes), the odd CTA's relay
+// and the eight dequant warps of the pair.  The MMA thread polls this one barrier per stage:
+// every shared-memory access of that thread stalls it for ~140 cycles while the tensor core
+// streams operands, so it makes one per eight MMAs.
+constexpr uint32_t kFullArrivals = 1 + 1 + 8;
 constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
 constexpr uint32_t kSmemBytes = kOffAbort + 4 + 1024;  // + alignment slack
+// more than half an SM's shared memory: one CTA per SM, whatever the register count
+static_assert(kSmemBytes > 116 * 1024, "one CTA per SM");
 
-// Instruction descriptor of kind::f16: D fp32, A and B fp16, both K-major, M=128, N=256.
+// Instruction descriptor of kind::f16: D fp32, A and B fp16, both K-major, M=256, N=128.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(kBN >> 3) << 17) |
-                            (uint32_t(kBM >> 4) << 24);
+                            (uint32_t(kRowsPair >> 4) << 24);
 
 struct Maps {
-    CUtensorMap x;   // fp16 [M, K], box 64 x 256, 128-byte swizzle
+    CUtensorMap x;   // fp16 [M, K], box 64 (K) x 64 (tokens), 128-byte swizzle
     CUtensorMap w;   // u8 [N, K/2], box 128 x 128, 128-byte swizzle
     CUtensorMap s;   // u16 [N, K/32], box 8 x 128
 };
 
 struct Params {
     int M, K, N;
-    int tiles_n;      // feature tiles (N / 128, rounded up)
+    int tiles_n;      // 256-row weight tiles (N / 256, rounded up)
     int tiles;        // tiles_n * token tiles
     void* out;
     int64_t out_ld, out_col0;
@@ -75,7 +93,11 @@ struct Params {
 };
 
 // Bounded wait by plain try_wait polling.  With a suspend-time hint the waits of this kernel
-// slept through tcgen05.commit arrivals (the GEMM ran 8x slower), so it polls.
+// slept through tcgen05.commit arrivals (the GEMM ran 8x slower), so it polls.  The polls
+// keep the default CTA-scope acquire even where the arrivals come from the peer CTA: what
+// they order is complete before the arrive is issued (TMA complete_tx, tcgen05.wait::st /
+// wait::ld), and a cluster-scope acquire costs the polling thread a memory barrier each time,
+// which starved the MMA issuer.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_t err) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
@@ -91,33 +113,65 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, uint32_
 }
 
 // ---------------------------------------------------------------------------------------
-// tcgen05 wrappers
+// Cluster (CTA pair) helpers
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Shared::cluster address of the same object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// Arrive on a barrier given by its shared::cluster address (this CTA's or the peer's), with
+// the default release semantics (see wait_bar).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// tcgen05 wrappers (every tcgen05 operation of the kernel is cta_group::2)
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem), "r"(ncols)
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem), "r"(ncols)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Arrives on `bar` once every tcgen05 operation this thread issued before has completed.
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+// Arrives on `bar` in both CTAs of the pair once every tcgen05 operation this thread issued
+// before has completed.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(static_cast<uint16_t>(0x3))
+        : "memory");
+}
+// The same, arriving on this CTA's `bar` only.
+__device__ __forceinline__ void tc_commit_local(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
 
-// D[tmem] (+)= A[tmem] * B[smem]^T, 128 x 256 x 16, fp16 in, fp32 accumulate.
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem]^T over the pair: 256 x 128 x 16, fp16 in, fp32 accumulate.
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
         : "memory");
 }
@@ -238,8 +292,9 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x
     for (int q = 0; q < 4; ++q) xp[i * 4 + q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
 }
 
+
 // ---------------------------------------------------------------------------------------
-// The GEMM kernel
+// The GEMM kernel (launched as clusters of two CTAs; rank 0 issues the MMAs)
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -247,45 +302,48 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* smem = smem_raw + (base - raw);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-    uint64_t* x_full = bars;
-    uint64_t* stage_empty = bars + kStages;
-    uint64_t* a_full = bars + 2 * kStages;
-    uint64_t* w_full = bars + 3 * kStages;
+    // full[s]: on rank 0 the whole stage is ready (both activation halves, both A slots);
+    // on rank 1 its own activation half landed (its relay forwards that to rank 0)
+    uint64_t* full = bars;
+    uint64_t* stage_empty = bars + kStages;      // the pair's MMAs finished with the stage
+    uint64_t* w_full = bars + 2 * kStages;
     uint64_t* w_empty = w_full + kWStages;
-    uint64_t* d_full = w_empty + kWStages;
-    uint64_t* d_empty = d_full + 1;
-    uint64_t* done_bar = d_full + 2;
+    uint64_t* d_full = w_empty + kWStages;       // [2] accumulator buffer complete
+    uint64_t* d_empty = d_full + 2;              // [2] (rank 0) both epilogues read it
+    uint64_t* done_bar = d_full + 4;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + kOffTmemSlot);
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kOffAbort);
 
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
-            mbar_init(&x_full[i], 1);
+            mbar_init(&full[i], leader ? kFullArrivals : 1);
             mbar_init(&stage_empty[i], 1);
-            mbar_init(&a_full[i], 128);
         }
         for (int i = 0; i < kWStages; ++i) {
             mbar_init(&w_full[i], 1);
-            mbar_init(&w_empty[i], 128);
+            mbar_init(&w_empty[i], 8);       // both dequant groups
         }
-        mbar_init(d_full, 1);
-        mbar_init(d_empty, 128);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&d_full[b], 1);
+            mbar_init(&d_empty[b], 8);       // four epilogue warps in each CTA
+        }
         mbar_init(done_bar, 1);
         *s_abort = 0;
         fence_mbar_init();
     }
     if (warp == 1) tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), kTmemCols);
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();   // both CTAs' barriers initialised and tensor memory allocated
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    const int pair = static_cast<int>(blockIdx.x >> 1), pairs = static_cast<int>(gridDim.x >> 1);
+    const int my_tiles = p.tiles > pair ? (p.tiles - 1 - pair) / pairs + 1 : 0;
     const int n_ks = p.K / kXK;            // activation stages per tile
     const int n_kw = p.K / kWK;            // weight stages per tile
-    const int my_tiles = p.tiles > static_cast<int>(blockIdx.x)
-                             ? (p.tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
-                             : 0;
 
     if (warp == 0) {
         // ------------------------------------------------------------ activation producer
@@ -293,8 +351,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             prefetch_tensormap(&maps.x);
             int issued = 0;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
-                const int tile = blockIdx.x + t * gridDim.x;
-                const int tok0 = (tile / p.tiles_n) * kBN;
+                const int tile = pair + t * pairs;
+                const int tok = (tile / p.tiles_n) * kBN + static_cast<int>(rank) * kTokCta;
                 for (int ks = 0; ks < n_ks; ++ks) {
                     const int s = issued % kStages, r = issued / kStages;
                     if (r > 0 && !wait_bar(&stage_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
@@ -302,13 +360,34 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         break;
                     }
                     if (*s_abort) break;
-                    mbar_arrive_expect_tx(&x_full[s], kXStageBytes);
-                    tma_load_2d(smem + kOffX + s * kXStageBytes, &maps.x, &x_full[s], ks * kXK, tok0);
+                    mbar_arrive_expect_tx(&full[s], kXStageBytes);
+                    uint8_t* dst = smem + kOffX + s * kXStageBytes;
+                    tma_load_2d(dst, &maps.x, &full[s], ks * kXK, tok);
+                    tma_load_2d(dst + kXSubBytes, &maps.x, &full[s], ks * kXK + kXSub, tok);
                     ++issued;
                 }
             }
-            for (int it = issued > kStages ? issued - kStages : 0; it < issued; ++it)
-                if (!wait_bar(&x_full[it % kStages], (it / kStages) & 1, kDevErrDrainWait)) break;
+            // rank 1 waits for its copies to land; rank 0's own full barrier also counts the
+            // other arrivals, so it waits for the pair's MMAs to release the stages instead
+            for (int it = issued > kStages ? issued - kStages : 0; it < issued; ++it) {
+                const bool landed = leader ? wait_bar(&stage_empty[it % kStages], (it / kStages) & 1, kDevErrDrainWait)
+                                           : wait_bar(&full[it % kStages], (it / kStages) & 1, kDevErrDrainWait);
+                if (!landed) break;
+            }
+        }
+    } else if (warp == 3) {
+        // ------------------------------- (odd CTA) tells rank 0 that its half has landed
+        if (!leader && lane == 0) {
+            const uint32_t lead_full = map_to_rank(full, 0);
+            const int total = my_tiles * n_ks;
+            for (int i = 0; i < total; ++i) {
+                const int s = i % kStages;
+                if (!wait_bar(&full[s], (i / kStages) & 1, kDevErrFullWait) || *s_abort) {
+                    *s_abort = 1;
+                    break;
+                }
+                mbar_arrive_cluster(lead_full + 8u * s);
+            }
         }
     } else if (warp == 2) {
         // ---------------------------------------------------------------- weight producer
@@ -318,8 +397,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             const uint64_t policy = l2_policy_evict_last();
             int issued = 0;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
-                const int tile = blockIdx.x + t * gridDim.x;
-                const int row0 = (tile % p.tiles_n) * kBM;
+                const int tile = pair + t * pairs;
+                const int row0 = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta;
                 for (int kw = 0; kw < n_kw; ++kw) {
                     const int s = issued % kWStages, r = issued / kWStages;
                     if (r > 0 && !wait_bar(&w_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
@@ -337,105 +416,116 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 if (!wait_bar(&w_full[it % kWStages], (it / kWStages) & 1, kDevErrDrainWait)) break;
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
+        // ------------------------------------------------------- MMA issuer (rank 0 only)
+        if (leader && lane == 0) {
             int consumed = 0;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
-                if (t > 0 && !wait_bar(d_empty, (t - 1) & 1, kDevErrMmaWait)) {
+                const int b = t & 1, u = t >> 1;
+                if (u > 0 && !wait_bar(&d_empty[b], (u - 1) & 1, kDevErrMmaWait)) {
                     *s_abort = 1;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t d_tmem = tmem + b * kAccCols;
                 bool ok = true;
                 for (int ks = 0; ks < n_ks; ++ks) {
                     const int s = consumed % kStages, r = consumed / kStages;
-                    if (!wait_bar(&x_full[s], r & 1, kDevErrFullWait) ||
-                        !wait_bar(&a_full[s], r & 1, kDevErrFullWait) || *s_abort) {
+                    if (!wait_bar(&full[s], r & 1, kDevErrFullWait)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint64_t bdesc = sw128_desc(base + kOffX + s * kXStageBytes);
-                    const uint32_t a0 = tmem + kAccCols + s * kACols;
+                    const uint32_t a0 = tmem + kAOff + s * kACols;
 #pragma unroll
-                    for (int k16 = 0; k16 < kXK / 16; ++k16)
-                        mma_ts(tmem, a0 + k16 * 8, bdesc + static_cast<uint64_t>(k16 * 2), (ks | k16) != 0);
-                    tc_commit(&stage_empty[s]);
+                    for (int k16 = 0; k16 < kXK / 16; ++k16) {
+                        // 16-K steps advance 32 bytes inside a 128-byte swizzle row, then jump
+                        // to the next 64-K box
+                        const uint64_t bk = bdesc + static_cast<uint64_t>((k16 >> 2) * (kXSubBytes >> 4) + (k16 & 3) * 2);
+                        mma_pair(d_tmem, a0 + k16 * 8, bk, (ks | k16) != 0);
+                    }
+                    tc_commit_pair(&stage_empty[s]);
                     ++consumed;
                 }
                 if (!ok) {
                     *s_abort = 1;
                     break;
                 }
-                tc_commit(d_full);
+                tc_commit_pair(&d_full[b]);
             }
             // every MMA issued above has completed before the tensor memory is freed
-            tc_commit(done_bar);
+            tc_commit_local(done_bar);
             wait_bar(done_bar, 0, kDevErrMmaWait);
         }
-    } else if (warp >= kDequantWarp0) {
-        // ----------------------------------------------------- dequantizer + epilogue
-        const int sub = warp & 3;                  // TMEM lane quarter this warp may access
-        const int row = sub * 32 + lane;           // weight row inside the tile
-        const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
-        int w_used = 0, a_made = 0;
-        for (int t = 0; t < my_tiles; ++t) {
-            const int tile = blockIdx.x + t * gridDim.x;
-            const int feat = (tile % p.tiles_n) * kBM + row;
-            const int tok0 = (tile / p.tiles_n) * kBN;
-            bool ok = true;
+    } else if (warp < kEpilogueWarp0) {
+        // ------------------------------------------------------------------ dequantizers
+        // A weight stage (K=256) holds two activation stages; group 0 fills the even ones,
+        // group 1 the odd ones.  Each warp owns the TMEM lane quarter (warp % 4) = 32 rows.
+        const int grp = (warp - kDequantWarp0) >> 2;
+        const int quarter = warp & 3;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t lead_full = map_to_rank(full, 0);
+        int w_used = 0;
+        bool ok = true;
+        for (int t = 0; t < my_tiles && ok; ++t) {
             for (int kw = 0; kw < n_kw && ok; ++kw) {
                 const int ws = w_used % kWStages;
-                if (!wait_bar(&w_full[ws], (w_used / kWStages) & 1, kDevErrFullWait) || *s_abort) {
-                    ok = false;
-                    break;
-                }
+                ok = wait_bar(&w_full[ws], (w_used / kWStages) & 1, kDevErrFullWait) && !*s_abort;
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                // this group's four 32-blocks of the weight stage: c = 4 * grp + h
                 const uint32_t wrow = base + kOffW + ws * kWStageBytes + row * 128;
-                uint4 chunk[8];
+                uint4 chunk[4];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) chunk[c] = lds_u128(wrow + ((c ^ (row & 7)) << 4));
+                for (int h = 0; h < 4; ++h) chunk[h] = lds_u128(wrow + (((4 * grp + h) ^ (row & 7)) << 4));
                 const uint4 sc = lds_u128(base + kOffS + ws * kSStageBytes + row * 16);
-                mbar_arrive(&w_empty[ws]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&w_empty[ws]);
                 ++w_used;
-                const uint32_t sw[4] = {sc.x, sc.y, sc.z, sc.w};
+                const int i = t * n_ks + kw * kSubs + grp;          // stage index; i % 2 == grp
+                const int s = i % kStages, r = i / kStages;
+                if (r > 0) ok = wait_bar(&stage_empty[s], (r - 1) & 1, kDevErrEmptyWait);
+                ok = __all_sync(0xffffffffu, ok && !*s_abort);
+                if (!ok) break;
+                tc_fence_after();
+                // scales of blocks 4 grp .. 4 grp + 3: two 32-bit words of the row's eight
+                const uint32_t sw0 = grp ? sc.z : sc.x, sw1 = grp ? sc.w : sc.y;
 #pragma unroll
-                for (int q = 0; q < kSubs; ++q) {
-                    const int s = a_made % kStages, r = a_made / kStages;
-                    if (r > 0 && !wait_bar(&stage_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
-                        ok = false;
-                        break;
-                    }
-                    if (*s_abort) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
+                for (int half = 0; half < 2; ++half) {
+                    const __half2 pr = bits_h2(half ? sw1 : sw0);
                     uint32_t col[32];
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const int c = 2 * q + h;
-                        const __half2 s2 = __half2half2(bits_h2(sw[c >> 1]).x);
-                        const __half2 sv = (c & 1) ? __half2half2(bits_h2(sw[c >> 1]).y) : s2;
+                        const __half2 sv = h ? __half2half2(pr.y) : __half2half2(pr.x);
                         const __half2 s16 = __hmul2(sv, bits_h2(0x2C002C00u));   // x 1/16
-                        const uint4 u = chunk[c];
+                        const uint4 u = chunk[2 * half + h];
                         dequant_word(u.x, sv, s16, &col[16 * h + 0]);
                         dequant_word(u.y, sv, s16, &col[16 * h + 4]);
                         dequant_word(u.z, sv, s16, &col[16 * h + 8]);
                         dequant_word(u.w, sv, s16, &col[16 * h + 12]);
                     }
-                    tmem_st32(tmem + lane_addr + kAccCols + s * kACols, col);
-                    tc_wait_st();
-                    tc_fence_before();
-                    mbar_arrive(&a_full[s]);
-                    ++a_made;
+                    tmem_st32(tmem + lane_addr + kAOff + s * kACols + half * 32, col);
                 }
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(lead_full + 8u * s);
             }
+        }
+        if (!ok) *s_abort = 1;
+    } else {
+        // ---------------------------------------------------------------------- epilogue
+        const int quarter = warp & 3;
+        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t lead_d_empty = map_to_rank(d_empty, 0);
+        for (int t = 0; t < my_tiles; ++t) {
+            const int b = t & 1, u = t >> 1;
+            const int tile = pair + t * pairs;
+            const int feat = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta + quarter * 32 + lane;
+            const int tok0 = (tile / p.tiles_n) * kBN;
+            const bool ok = __all_sync(0xffffffffu, wait_bar(&d_full[b], u & 1, kDevErrMmaWait));
             if (!ok) {
-                *s_abort = 1;
-                break;
-            }
-            // ---- epilogue: accumulator -> out[token][feature]
-            if (!wait_bar(d_full, t & 1, kDevErrMmaWait)) {
                 *s_abort = 1;
                 break;
             }
@@ -444,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 #pragma unroll 1
             for (int c0 = 0; c0 < kBN; c0 += 32) {
                 uint32_t v[32];
-                tmem_ld32(tmem + lane_addr + c0, v);
+                tmem_ld32(tmem + lane_addr + b * kAccCols + c0, v);
                 tc_wait_ld();
                 if (feat_ok) {
                     const int nt = min(32, p.M - (tok0 + c0));
@@ -464,11 +554,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 }
             }
             tc_fence_before();
-            mbar_arrive(d_empty);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(lead_d_empty + 8u * b);
         }
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync();   // neither CTA frees its tensor memory while the pair may still use it
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
@@ -518,27 +610,44 @@ static int scratch_pool(int device, cudaMemPool_t* pool) {
     return BYBYCU_OK;
 }
 
-// Checks, device info and the kernel attribute shared by both scratch sources.
-static int tc_prepare(const GemmArgs& a, DeviceInfo* info) {
+
+// Checks, device info, the kernel attribute and the number of CTA pairs that fit at once.
+static int tc_prepare(const GemmArgs& a, DeviceInfo* info, int* max_pairs) {
     if (!tc_supports(a))
         return set_error(BYBYCU_ERR_SHAPE,
                          "tensor-core route needs format 2, K %% 256 == 0, 16-byte aligned x, packed and scales "
                          "(M=%d K=%d N=%d)", a.M, a.K, a.N);
     if (int rc = current_device_info(info)) return rc;
-    static std::once_flag attr_once[16];
-    static cudaError_t attr_rc[16];
+    static std::once_flag once[16];
+    static cudaError_t prep_rc[16];
+    static int pairs[16];
     const int dev = info->device & 15;
-    std::call_once(attr_once[dev], [&] {
-        attr_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    std::call_once(once[dev], [&] {
+        prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(tc::kSmemBytes));
+        if (prep_rc[dev] != cudaSuccess) return;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2 * (info->sm_count / 2));
+        cfg.blockDim = dim3(tc::kThreads);
+        cfg.dynamicSmemBytes = tc::kSmemBytes;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        prep_rc[dev] = cudaOccupancyMaxActiveClusters(&pairs[dev], tc::gemm_kernel, &cfg);
     });
-    if (attr_rc[dev] != cudaSuccess) return cuda_fail(attr_rc[dev], "cudaFuncSetAttribute(tc gemm)");
+    if (prep_rc[dev] != cudaSuccess) return cuda_fail(prep_rc[dev], "tensor-core GEMM set-up");
+    if (pairs[dev] < 1) return set_error(BYBYCU_ERR_DEVICE, "no CTA pair of the tensor-core GEMM fits on the device");
+    *max_pairs = pairs[dev];
     return BYBYCU_OK;
 }
 
 // The staging pass and the GEMM, with `xp` (M * K fp16) as the staging buffer.  Allocates
 // nothing.
-static int tc_run(const GemmArgs& a, const DeviceInfo& info, void* xp) {
+static int tc_run(const GemmArgs& a, int max_pairs, void* xp) {
     const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
     const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
     if (a.x_dtype == BYBYCU_DT_F32)
@@ -549,21 +658,22 @@ static int tc_run(const GemmArgs& a, const DeviceInfo& info, void* xp) {
 
     tc::Maps maps;
     int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xp, a.K, a.M,
-                                  static_cast<uint64_t>(a.K) * 2, tc::kXK, tc::kBN, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  static_cast<uint64_t>(a.K) * 2, tc::kXSub, tc::kTokCta, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (!rc)
         rc = encode_tensor_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.N, a.K / 2,
-                                  tc::kWK / 2, tc::kBM, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+                                  tc::kWK / 2, tc::kRowsCta, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (!rc)
         rc = encode_tensor_map_2d(&maps.s, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.packed + a.scale_base, a.K / 32, a.N,
-                                  static_cast<uint64_t>(a.K / 32) * 2, tc::kWK / 32, tc::kBM,
+                                  static_cast<uint64_t>(a.K / 32) * 2, tc::kWK / 32, tc::kRowsCta,
                                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
     if (rc) return rc;
     tc::Params p;
     p.M = a.M;
     p.K = a.K;
     p.N = a.N;
-    p.tiles_n = static_cast<int>(ceil_div(a.N, tc::kBM));
+    p.tiles_n = static_cast<int>(ceil_div(a.N, tc::kRowsPair));
     const int64_t tiles = static_cast<int64_t>(p.tiles_n) * ceil_div(a.M, tc::kBN);
     if (tiles > (1 << 30)) return set_error(BYBYCU_ERR_SHAPE, "tensor-core route: too many tiles (M=%d N=%d)", a.M, a.N);
     p.tiles = static_cast<int>(tiles);
@@ -571,22 +681,34 @@ static int tc_run(const GemmArgs& a, const DeviceInfo& info, void* xp) {
     p.out_ld = a.out_ld;
     p.out_col0 = a.out_col0;
     p.out_bf16 = a.out_dtype == BYBYCU_DT_BF16;
-    const int grid = static_cast<int>(std::min<int64_t>(tiles, info.sm_count));
-    tc::gemm_kernel<<<grid, tc::kThreads, tc::kSmemBytes, a.stream>>>(maps, p);
-    BYBYCU_LAUNCH_CHECK("tc gemm_kernel");
+    const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = tc::kSmemBytes;
+    cfg.stream = a.stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel, maps, p));
     return BYBYCU_OK;
 }
 
 int launch_tc(const GemmArgs& a) {
     DeviceInfo info;
-    if (int rc = tc_prepare(a, &info)) return rc;
+    int max_pairs = 0;
+    if (int rc = tc_prepare(a, &info, &max_pairs)) return rc;
     // activations -> fp16, permuted, in stream-ordered scratch
     const size_t xp_bytes = static_cast<size_t>(a.M) * a.K * 2;
     void* xp = nullptr;
     cudaMemPool_t pool = nullptr;
     if (int rc = scratch_pool(info.device, &pool)) return rc;
     BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
-    const int rc = tc_run(a, info, xp);
+    const int rc = tc_run(a, max_pairs, xp);
     const cudaError_t fe = cudaFreeAsync(xp, a.stream);
     if (rc) return rc;
     if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc scratch)");
@@ -623,10 +745,11 @@ int launch_tc_static_scratch(const GemmArgs& a) {
                          "M=%d K=%d needs %zu bytes (at most M*K = %zu)",
                          kStaticScratchBytes >> 20, a.M, a.K, need, kStaticScratchBytes / 2);
     DeviceInfo info;
-    if (int rc = tc_prepare(a, &info)) return rc;
+    int max_pairs = 0;
+    if (int rc = tc_prepare(a, &info, &max_pairs)) return rc;
     void* xp = nullptr;
     if (int rc = static_scratch(info.device, &xp)) return rc;
-    return tc_run(a, info, xp);
+    return tc_run(a, max_pairs, xp);
 }
 
 }  // namespace bybycu

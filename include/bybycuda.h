@@ -200,9 +200,9 @@ BYBYCU_API int bybycu_session_f16_gemm(const void* a, const void* w, void* c, in
 BYBYCU_API int bybycu_session_q4b32_gemm(const void* a, const void* w, void* c, int M, int K, int N,
                               int tensor_core);
 /* sessionTileGemmReady (gpubackend.nim:1484-1488 -> vulkanTileGemmReady,
- * vulkan_driver.nim:2681-2762): the exact-data parity gate (M=37, K=128, N=80, every
- * route that can run it, max rel err <= 1e-3), run once per process and format/route;
- * *ready = 1 when it passed. */
+ * vulkan_driver.nim:2681-2762): the exact-data parity gate (M=37, K=128, N=80; K=256 for
+ * the tensor-core gate, the smallest K that route tiles; every route that can run it, max
+ * rel err <= 1e-3), run once per process and format/route; *ready = 1 when it passed. */
 BYBYCU_API int bybycu_tile_gemm_ready(int fmt, int tensor_core, int* ready);
 
 /* ---- peer memory (the plumbing of the device-side all-gather) --------------------------- */

@@ -151,27 +151,34 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Arrives on `bar` in both CTAs of the pair once every tcgen05 operation this thread issued
-// before has completed.
+// The MMA-issuing warp runs its loop converged (all 32 lanes) and one lane, chosen by
+// elect.sync, issues each tcgen05 operation.  Issuing from a single diverged lane instead
+// left the tensor pipe idle ~40% of the time between stages.
+
+// Arrives on `bar` in both CTAs of the pair once every tcgen05 operation issued before by
+// this warp's elected lane has completed.
 __device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
     asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+        "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(
             smem_u32(bar)),
         "h"(static_cast<uint16_t>(0x3))
         : "memory");
 }
 // The same, arriving on this CTA's `bar` only.
 __device__ __forceinline__ void tc_commit_local(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+    asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+                 "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar))
                  : "memory");
 }
 
 // D[tmem] (+)= A[tmem] * B[smem]^T over the pair: 256 x 128 x 16, fp16 in, fp32 accumulate.
 __device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t accumulate) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
         : "memory");
 }
@@ -416,12 +423,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 if (!wait_bar(&w_full[it % kWStages], (it / kWStages) & 1, kDevErrDrainWait)) break;
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------- MMA issuer (rank 0 only)
-        if (leader && lane == 0) {
-            int consumed = 0;
+        // ------------------------------------------------- MMA issuer (rank 0, whole warp)
+        // A stage's release (its commit) is issued after the next stage's first MMA, so the
+        // commit never stands between two MMAs in the issue stream.
+        if (leader) {
+            int consumed = 0, pending = -1;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
                 const int b = t & 1, u = t >> 1;
-                if (u > 0 && !wait_bar(&d_empty[b], (u - 1) & 1, kDevErrMmaWait)) {
+                if (u > 0 && !__all_sync(0xffffffffu, wait_bar(&d_empty[b], (u - 1) & 1, kDevErrMmaWait))) {
                     *s_abort = 1;
                     break;
                 }
@@ -430,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 bool ok = true;
                 for (int ks = 0; ks < n_ks; ++ks) {
                     const int s = consumed % kStages, r = consumed / kStages;
-                    if (!wait_bar(&full[s], r & 1, kDevErrFullWait)) {
+                    if (!__all_sync(0xffffffffu, wait_bar(&full[s], r & 1, kDevErrFullWait))) {
                         ok = false;
                         break;
                     }
@@ -443,19 +452,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         // to the next 64-K box
                         const uint64_t bk = bdesc + static_cast<uint64_t>((k16 >> 2) * (kXSubBytes >> 4) + (k16 & 3) * 2);
                         mma_pair(d_tmem, a0 + k16 * 8, bk, (ks | k16) != 0);
+                        if (k16 == 0 && pending >= 0) tc_commit_pair(&stage_empty[pending]);
                     }
-                    tc_commit_pair(&stage_empty[s]);
+                    pending = s;
                     ++consumed;
                 }
                 if (!ok) {
                     *s_abort = 1;
                     break;
                 }
+                tc_commit_pair(&stage_empty[pending]);   // the tile's last stage
+                pending = -1;
                 tc_commit_pair(&d_full[b]);
             }
+            if (pending >= 0) tc_commit_pair(&stage_empty[pending]);
             // every MMA issued above has completed before the tensor memory is freed
             tc_commit_local(done_bar);
-            wait_bar(done_bar, 0, kDevErrMmaWait);
+            __all_sync(0xffffffffu, wait_bar(done_bar, 0, kDevErrMmaWait));
         }
     } else if (warp < kEpilogueWarp0) {
         // ------------------------------------------------------------------ dequantizers

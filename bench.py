@@ -343,28 +343,40 @@ def main():
         Mp, Kp, Np = 2048, 4096, 4096
         try:
             if gb.route_for(2, Mp, Kp, Np) == _lib.ROUTE_TC:
-                nib, sc = synthetic_q4b32(Np, Kp, seed=SEED + 7, device=dev)
-                wp = gb.Q4B32Weights(nib, sc, device=dev)
-                xp = synthetic_x(Mp, Kp, seed=SEED + 8, device=dev)
-                op = torch.empty(Mp, Np, dtype=torch.bfloat16, device=dev)
-                flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
-                for _ in range(3):
-                    wp.matmul(xp, op, route=_lib.ROUTE_TC)
-                torch.cuda.synchronize()
-                times = []
-                for _ in range(20):
-                    flush.zero_()
-                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    a.record()
-                    wp.matmul(xp, op, route=_lib.ROUTE_TC)
-                    b.record()
-                    torch.cuda.synchronize()
-                    times.append(a.elapsed_time(b))
-                t = statistics.median(times)
+                # rotating (weights, activations, output) sets larger than 4x L2 together, so each
+                # call reads its inputs from HBM; calls run back to back on one stream
+                per_set = W_BYTES * Np // N_DEC + Mp * Kp * 2 + Mp * Np * 2
+                n_sets = max(2, -(-4 * L2_BYTES // per_set))
+                sets = []
+                for c in range(n_sets):
+                    nib, sc = synthetic_q4b32(Np, Kp, seed=SEED + 7 + c, device=dev)
+                    sets.append((gb.Q4B32Weights(nib, sc, device=dev),
+                                 synthetic_x(Mp, Kp, seed=SEED + 100 + c, device=dev),
+                                 torch.empty(Mp, Np, dtype=torch.bfloat16, device=dev)))
+                with torch.cuda.stream(stream):
+                    for i in range(2 * n_sets):
+                        wp, xp, op = sets[i % n_sets]
+                        wp.matmul(xp, op, route=_lib.ROUTE_TC, stream=stream)
+                stream.synchronize()
+                reps = 10 * n_sets
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                with torch.cuda.stream(stream):
+                    for i in range(reps):
+                        wp, xp, op = sets[i % n_sets]
+                        wp.matmul(xp, op, route=_lib.ROUTE_TC, stream=stream)
+                b.record(stream)
+                stream.synchronize()
+                assert _lib.device_error() == 0
+                t = a.elapsed_time(b) / reps
                 tf = 2.0 * Mp * Np * Kp / (t / 1e3) / 1e12
-                prefill = {"value": round(tf, 2), "unit": "TFLOP/s", "workload": "C3 M=2048 K=N=4096 Q4B32, bf16 out",
-                           "ms": round(t, 4), "frac": round(tf / tc_peak, 4), "peak": tc_peak,
-                           "l2": "flushed (252 MB write) before each of 20 timed launches"}
+                prefill = {"value": round(tf, 2), "unit": "TFLOP/s", "workload": "C3 M=2048 K=N=4096 Q4B32, x bf16, bf16 out",
+                           "ms_per_call": round(t, 5), "calls": reps,
+                           "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tc_peak, "unit": "TFLOP/s",
+                                        "frac": round(tf / tc_peak, 4), "peak_kind": peak_kind},
+                           "includes": "fp16 staging pass + tcgen05 GEMM (2 launches per call)",
+                           "l2": f"inputs larger than L2: {n_sets} rotating (W, x, out) sets ({n_sets * per_set >> 20} MiB), "
+                                 "back-to-back calls, CUDA events on the launching stream"}
         except _lib.BybyCudaError as e:
             prefill = {"error": str(e)}
 

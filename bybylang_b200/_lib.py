@@ -78,8 +78,8 @@ SIGNATURES = {
     "bybycu_session_f16_gemm": [_vp, _vp, _vp, _i32, _i32, _i32, _i32],
     "bybycu_session_q4b32_gemm": [_vp, _vp, _vp, _i32, _i32, _i32, _i32],
     "bybycu_tile_gemm_ready": [_i32, _i32, C.POINTER(_i32)],
-    "bybycu_ipc_handle": [_vp, C.c_char_p],
-    "bybycu_ipc_open": [C.c_char_p, C.POINTER(_vp)],
+    "bybycu_ipc_handle": [_vp, C.c_char_p, C.POINTER(_i64)],
+    "bybycu_ipc_open": [C.c_char_p, _i64, C.POINTER(_vp)],
     "bybycu_ipc_close": [_vp],
     "bybycu_shard_range": [_i32, _i32, _i32, _i32, C.POINTER(_i32), C.POINTER(_i32)],
     "bybycu_tile_gemm_allgather": [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _vp, _i64, _i64,

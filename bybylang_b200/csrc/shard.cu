@@ -9,6 +9,7 @@
 // data path and no load reads another GPU's memory.
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "kernels.h"
@@ -116,6 +117,34 @@ __global__ void wait_kernel(uint32_t* sig, int world, uint32_t epoch, uint32_t p
     if (threadIdx.x == 0 && epoch == 0) sig[kMaxRanks] = s_epoch;
 }
 
+// Peer allocations mapped into this process, shared by every pointer inside them.
+struct IpcMapping {
+    uint8_t handle[64];
+    void* base;
+    int refs;
+};
+std::mutex g_ipc_mu;
+std::vector<IpcMapping> g_ipc;
+
+// The allocation that contains dptr (cuMemGetAddressRange through the runtime's driver
+// entry point; no libcuda link).
+int allocation_range(const void* dptr, void** base, size_t* size) {
+    using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static RangeFn fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        BYBYCU_CUDA_TRY(cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !p) return set_error(BYBYCU_ERR_CUDA, "cuMemGetAddressRange is not available");
+        fn = reinterpret_cast<RangeFn>(p);
+    }
+    CUdeviceptr b = 0;
+    const CUresult r = fn(&b, size, reinterpret_cast<CUdeviceptr>(dptr));
+    if (r != CUDA_SUCCESS) return set_error(BYBYCU_ERR_ARGS, "ipc handle: %p is not device memory (%d)", dptr, static_cast<int>(r));
+    *base = reinterpret_cast<void*>(b);
+    return BYBYCU_OK;
+}
+
 }  // namespace
 }  // namespace bybycu
 
@@ -123,25 +152,55 @@ using namespace bybycu;
 
 extern "C" {
 
-int bybycu_ipc_handle(const void* dptr, uint8_t handle[64]) {
-    if (!dptr || !handle) return set_error(BYBYCU_ERR_ARGS, "ipc handle: bad arguments");
+int bybycu_ipc_handle(const void* dptr, uint8_t handle[64], int64_t* offset) {
+    if (!dptr || !handle || !offset) return set_error(BYBYCU_ERR_ARGS, "ipc handle: bad arguments");
+    // The handle names the whole allocation; a caching allocator hands out pointers inside
+    // larger blocks, so the pointer's offset in its allocation travels with the handle.
+    void* base = nullptr;
+    size_t size = 0;
+    if (int rc = allocation_range(dptr, &base, &size)) return rc;
     cudaIpcMemHandle_t h;
-    BYBYCU_CUDA_TRY(cudaIpcGetMemHandle(&h, const_cast<void*>(dptr)));
+    BYBYCU_CUDA_TRY(cudaIpcGetMemHandle(&h, base));
     static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
     memcpy(handle, &h, 64);
+    *offset = static_cast<const char*>(dptr) - static_cast<const char*>(base);
     return BYBYCU_OK;
 }
 
-int bybycu_ipc_open(const uint8_t handle[64], void** dptr) {
-    if (!dptr || !handle) return set_error(BYBYCU_ERR_ARGS, "ipc open: bad arguments");
+int bybycu_ipc_open(const uint8_t handle[64], int64_t offset, void** dptr) {
+    if (!dptr || !handle || offset < 0) return set_error(BYBYCU_ERR_ARGS, "ipc open: bad arguments");
+    std::lock_guard<std::mutex> lock(g_ipc_mu);
+    for (IpcMapping& m : g_ipc) {
+        if (memcmp(m.handle, handle, 64) == 0) {   // the allocation is mapped already
+            ++m.refs;
+            *dptr = static_cast<char*>(m.base) + offset;
+            return BYBYCU_OK;
+        }
+    }
     cudaIpcMemHandle_t h;
     memcpy(&h, handle, 64);
-    BYBYCU_CUDA_TRY(cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess));
+    IpcMapping m;
+    BYBYCU_CUDA_TRY(cudaIpcOpenMemHandle(&m.base, h, cudaIpcMemLazyEnablePeerAccess));
+    memcpy(m.handle, handle, 64);
+    m.refs = 1;
+    g_ipc.push_back(m);
+    *dptr = static_cast<char*>(m.base) + offset;
     return BYBYCU_OK;
 }
 
 int bybycu_ipc_close(void* dptr) {
-    if (dptr) BYBYCU_CUDA_TRY(cudaIpcCloseMemHandle(dptr));
+    if (!dptr) return BYBYCU_OK;
+    std::lock_guard<std::mutex> lock(g_ipc_mu);
+    // the mapping whose base is the highest one not above dptr
+    int best = -1;
+    for (size_t i = 0; i < g_ipc.size(); ++i)
+        if (g_ipc[i].base <= dptr && (best < 0 || g_ipc[i].base > g_ipc[best].base)) best = static_cast<int>(i);
+    if (best < 0) return set_error(BYBYCU_ERR_ARGS, "ipc close: %p is not an opened peer buffer", dptr);
+    if (--g_ipc[best].refs == 0) {
+        void* base = g_ipc[best].base;
+        g_ipc.erase(g_ipc.begin() + best);
+        BYBYCU_CUDA_TRY(cudaIpcCloseMemHandle(base));
+    }
     return BYBYCU_OK;
 }
 

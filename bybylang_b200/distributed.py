@@ -75,11 +75,12 @@ class PeerBuffers:
         self.out = torch.zeros(M, N, dtype=torch.float32, device=dev)
         self.signal = torch.zeros(64, dtype=torch.int32, device=dev)   # world counters used
         torch.cuda.synchronize()
-        h_out = C.create_string_buffer(64)
-        h_sig = C.create_string_buffer(64)
-        call("bybycu_ipc_handle", C.c_void_p(self.out.data_ptr()), h_out)
-        call("bybycu_ipc_handle", C.c_void_p(self.signal.data_ptr()), h_sig)
-        mine = (bytes(h_out.raw), bytes(h_sig.raw))
+        # each handle names the whole allocation; the offset locates the tensor inside it
+        h_out, h_sig = C.create_string_buffer(64), C.create_string_buffer(64)
+        o_out, o_sig = C.c_int64(0), C.c_int64(0)
+        call("bybycu_ipc_handle", C.c_void_p(self.out.data_ptr()), h_out, C.byref(o_out))
+        call("bybycu_ipc_handle", C.c_void_p(self.signal.data_ptr()), h_sig, C.byref(o_sig))
+        mine = (bytes(h_out.raw), o_out.value, bytes(h_sig.raw), o_sig.value)
         allh = [None] * world
         dist.all_gather_object(allh, mine, group=group)
         self._opened = []
@@ -90,8 +91,8 @@ class PeerBuffers:
                 sigs.append(self.signal.data_ptr())
                 continue
             po, ps = C.c_void_p(), C.c_void_p()
-            call("bybycu_ipc_open", C.c_char_p(allh[r][0]), C.byref(po))
-            call("bybycu_ipc_open", C.c_char_p(allh[r][1]), C.byref(ps))
+            call("bybycu_ipc_open", C.c_char_p(allh[r][0]), allh[r][1], C.byref(po))
+            call("bybycu_ipc_open", C.c_char_p(allh[r][2]), allh[r][3], C.byref(ps))
             self._opened += [po.value, ps.value]
             outs.append(po.value)
             sigs.append(ps.value)
@@ -143,7 +144,8 @@ class ShardedQ4B32:
         M = x.shape[0]
         width = slice_buf.shape[1]
         if self.local is not None:
-            self.local.matmul(x, out=slice_buf[:, :self.n1 - self.n0])
+            part = self.local.matmul(x)                   # contiguous [M, n1 - n0]
+            slice_buf[:, :self.n1 - self.n0].copy_(part)
         dist.all_gather_into_tensor(gathered, slice_buf, group=group)
         parts = gathered.view(self.world, M, width)
         cols = [shard_range(self.N, self.world, r) for r in range(self.world)]

@@ -280,7 +280,11 @@ def tile_gemm(fmt: int, x, packed, out, *, M: int, K: int, N: int, scale_base: i
     """out[M, N] = x[M, K] * dequant(W)^T for one OP_TILE_GEMM on device tensors.
 
     x: float32/bfloat16 [M, K]; packed: uint8 weight slot; out: float32/bfloat16 [M, N];
-    lut: float32 table slot (format 0).  Asynchronous on `stream` (default: current)."""
+    lut: float32 table slot (format 0).  Asynchronous on `stream` (default: current).
+    Every tensor must be contiguous: the library addresses the slots as dense arrays."""
+    for name, t in (("x", x), ("packed", packed), ("out", out), ("lut", lut)):
+        if t is not None and not t.is_contiguous():
+            raise BybyCudaError(_lib.ERR_ARGS, f"tile GEMM slot {name} must be contiguous")
     check(load().bybycu_tile_gemm(
         fmt, M, K, N, _ptr(x), _dtype_code(x), x.numel(), _ptr(packed), packed.numel() * packed.element_size(),
         scale_base, _ptr(lut), 0 if lut is None else lut.numel(), lut_base, _ptr(out), _dtype_code(out),

@@ -207,13 +207,16 @@ BYBYCU_API int bybycu_tile_gemm_ready(int fmt, int tensor_core, int* ready);
 
 /* ---- peer memory (the plumbing of the device-side all-gather) --------------------------- */
 
-/* Exports a cudaMalloc'ed device buffer as a 64-byte CUDA IPC handle another process can
- * open.  No reference counterpart: the reference's workers exchange text over pipes
+/* Exports the device allocation that holds `dptr` as a 64-byte CUDA IPC handle another
+ * process can open, and *offset = the byte offset of dptr inside that allocation (a caching
+ * allocator hands out pointers inside larger blocks; the handle always names the whole
+ * block).  No reference counterpart: the reference's workers exchange text over pipes
  * (distributed.nim:224-276). */
-BYBYCU_API int bybycu_ipc_handle(const void* dptr, uint8_t handle[64]);
-/* Maps a peer process's buffer into this process on the current device (peer access is
- * enabled by the mapping); *dptr is the local address of the peer buffer. */
-BYBYCU_API int bybycu_ipc_open(const uint8_t handle[64], void** dptr);
+BYBYCU_API int bybycu_ipc_handle(const void* dptr, uint8_t handle[64], int64_t* offset);
+/* Maps a peer process's allocation into this process on the current device (peer access is
+ * enabled by the mapping) and returns *dptr = its local base + offset.  Opening the same
+ * handle again reuses the mapping; every successful open needs one bybycu_ipc_close. */
+BYBYCU_API int bybycu_ipc_open(const uint8_t handle[64], int64_t offset, void** dptr);
 BYBYCU_API int bybycu_ipc_close(void* dptr);
 
 /* ---- column sharding (distributed.nim:109-135) ----------------------------------------- */

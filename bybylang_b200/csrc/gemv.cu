@@ -72,7 +72,24 @@ struct GemvParams {
     void* out;
     int out_bf16;
     int64_t out_ld, out_col0;
+    PeerGather pg;                 // world > 1: every output value also goes to every peer
 };
+
+// The fused all-gather: one output value to every other rank's buffer (plain NVLink stores).
+__device__ __forceinline__ void store_to_peers(const PeerGather& pg, int64_t oi, float v) {
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+        if (r < pg.world && r != pg.rank) pg.out[r][oi] = v;
+}
+
+// End of a GEMV launch that gathers: the barrier orders every consumer thread's stores before
+// thread 0's system-scope fence (fences are cumulative), then the last CTA signals the ranks
+// and waits for theirs.  One fence per CTA: a fence per thread cost microseconds per step.
+__device__ __forceinline__ void gemv_gather_end(const PeerGather& pg, uint32_t consumer_threads) {
+    if (pg.world <= 1) return;
+    named_barrier(2, consumer_threads);
+    if (threadIdx.x == 0) peer_gather_finish(pg);
+}
 
 // Three nibble maps and three scale maps: boxes of 16 * TP rows (full pass), 16 * (TP - 1)
 // rows (the short pass of a balanced split) and 16 rows (any other remainder).
@@ -443,12 +460,14 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
                     const int64_t oi = static_cast<int64_t>(m) * p.out_ld + p.out_col0 + n;
                     if (p.out_bf16) reinterpret_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(sum);
                     else reinterpret_cast<float*>(p.out)[oi] = sum;
+                    if (p.pg.world > 1) store_to_peers(p.pg, oi, sum);
                 }
             }
             named_barrier(1, kConsumerWarps * 32);
         }
         if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
     }
+    gemv_gather_end(p.pg, kConsumerWarps * 32);
 }
 
 
@@ -670,12 +689,14 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
                     const int64_t oi = p.out_col0 + n;
                     if (p.out_bf16) reinterpret_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(sum);
                     else reinterpret_cast<float*>(p.out)[oi] = sum;
+                    if (p.pg.world > 1) store_to_peers(p.pg, oi, sum);
                 }
             }
             named_barrier(1, kM1Warps * 32);
         }
         if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
     }
+    gemv_gather_end(p.pg, kM1Warps * 32);
 }
 
 bool pdl_enabled() {
@@ -768,7 +789,7 @@ bool gemv_supports(const GemmArgs& a) {
     return true;
 }
 
-int launch_gemv(const GemmArgs& a) {
+int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     DeviceInfo dev;
     if (int rc = current_device_info(&dev)) return rc;
     const bool xf32 = a.x_dtype == BYBYCU_DT_F32;
@@ -844,6 +865,10 @@ int launch_gemv(const GemmArgs& a) {
     p.out_bf16 = a.out_dtype == BYBYCU_DT_BF16;
     p.out_ld = a.out_ld;
     p.out_col0 = a.out_col0;
+    if (pg) {
+        if (p.out_bf16) return set_error(BYBYCU_ERR_ARGS, "GEMV all-gather: the gathered output is fp32");
+        p.pg = *pg;
+    }
     const size_t smem = 1024 + static_cast<size_t>(stages) * (stage_bytes + 16) + 16 + red_bytes;
 
     GemvMaps maps;

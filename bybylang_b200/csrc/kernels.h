@@ -24,12 +24,53 @@ struct GemmArgs {
     cudaStream_t stream = nullptr;
 };
 
+// Ranks of a column-sharded GEMM whose output slices are gathered over NVLink peer
+// pointers.  sig[r] is rank r's signal array: kMaxRanks counters (one per source rank), the
+// device-side epoch, and this rank's CTA completion counter.
+constexpr int kMaxRanks = 8;
+struct PeerGather {
+    int world = 1, rank = 0;
+    float* out[kMaxRanks] = {};      // every rank's output buffer as mapped here (out[rank] = local)
+    uint32_t* sig[kMaxRanks] = {};   // every rank's signal array as mapped here
+    uint32_t epoch = 0;              // 0: the epoch lives on the device (graph-capturable)
+};
+
+// Called by one thread of every CTA after all of the CTA's output stores (local and to the
+// peers).  The last CTA of the grid raises this rank's counter in every rank's signal array
+// and waits, bounded, until every rank's counter reached this epoch.  Returns false when the
+// wait ran out (the error is recorded in the device error word).
+__device__ __forceinline__ bool peer_gather_finish(const PeerGather& pg) {
+    __threadfence_system();   // this CTA's stores before its completion count
+    uint32_t* mine = pg.sig[pg.rank];
+    if (atomicAdd(mine + kMaxRanks + 1, 1u) != gridDim.x * gridDim.y * gridDim.z - 1) return true;
+    mine[kMaxRanks + 1] = 0;   // every CTA of this launch has counted
+    __threadfence_system();   // every CTA's stores before the signals
+    for (int r = 0; r < pg.world; ++r) atomicAdd_system(pg.sig[r] + pg.rank, 1u);
+    const uint32_t target = pg.epoch ? pg.epoch : mine[kMaxRanks] + 1;
+    bool ok = true;
+    for (int r = 0; r < pg.world && ok; ++r) {
+        const uint64_t t0 = globaltimer_ns();
+        for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
+            if (static_cast<int32_t>(v - target) >= 0) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                record_device_error(kDevErrPeerWait);
+                ok = false;
+                break;
+            }
+        }
+    }
+    if (!pg.epoch) mine[kMaxRanks] = target;
+    return ok;
+}
+
 // CUDA-core FP32 route: every format, every K % 32 == 0 shape.
 int launch_simt(const GemmArgs& a);
 // Decode GEMV route (format 2, M <= 16): TMA-streamed weights, bf16 mma.sync reductions with
 // exact per-block fp32 scaling.
 bool gemv_supports(const GemmArgs& a);
-int launch_gemv(const GemmArgs& a);
+int launch_gemv(const GemmArgs& a, const PeerGather* pg = nullptr);
 // Prefill GEMM route: tcgen05 MMAs from shared-memory fp16 tiles, fp32 accumulators in TMEM.
 bool tc_supports(const GemmArgs& a);
 int launch_tc(const GemmArgs& a);

@@ -2,11 +2,13 @@
 //
 // The split is distributed.nim's partition (distributed.nim:109-135): largest remainder
 // over equal weights, computed in float64 exactly as the reference does, taken over blocks
-// of `align` columns.  The exchange is device-side: each rank computes its column slice
-// and its kernels store the slice straight into every peer's output over NVLink (peer
-// pointers), then raise one counter per CTA in every rank's signal array; a one-CTA kernel
-// waits, bounded, for every rank's counters of this epoch.  No collective library is on the
-// data path and no load reads another GPU's memory.
+// of `align` columns.  The exchange is device-side: each rank computes its column slice and
+// stores it straight into every peer's output over NVLink (peer pointers) - from the GEMV's
+// own epilogue on the decode route, from a copy kernel after the other routes.  The last CTA
+// of that kernel raises this rank's counter in every rank's signal array and waits, bounded,
+// for every rank's counter of this epoch, so the launch completes only with the whole output
+// gathered.  No collective library is on the data path and no load reads another GPU's
+// memory.
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -23,13 +25,7 @@ int run_gemm(const GemmArgs& a, int route);
 
 namespace {
 
-constexpr int kMaxRanks = 8;
 constexpr int kExchangeCtas = 32;
-
-struct PeerSet {
-    float* out[kMaxRanks];
-    uint32_t* sig[kMaxRanks];
-};
 
 // Largest-remainder partition of `length` items over `world` equal weights
 // (distributed.nim:109-135): floor of length * (1 / world), then one more to the largest
@@ -57,9 +53,11 @@ std::vector<int> partition_equal(int length, int world) {
     return out;
 }
 
-// Copies out[:, n0:n1) of this rank into every other rank's out, then signals.
+// Copies out[:, n0:n1) of this rank into every other rank's out; the last CTA then signals
+// the ranks and waits for theirs (peer_gather_finish).  Used after the routes that do not
+// store to the peers themselves.
 __global__ void __launch_bounds__(256) exchange_kernel(const float* __restrict__ out, int M, int N, int n0, int n1,
-                                                       PeerSet peers, int world, int rank) {
+                                                       const PeerGather pg) {
     const int cols = n1 - n0;
     const int64_t total = static_cast<int64_t>(M) * cols;
     const bool vec = ((n0 | cols | N) & 3) == 0;
@@ -72,8 +70,9 @@ __global__ void __launch_bounds__(256) exchange_kernel(const float* __restrict__
             const int64_t c = (i % cols4) * 4;
             const int64_t off = m * N + n0 + c;
             const float4 v = *reinterpret_cast<const float4*>(out + off);
-            for (int r = 0; r < world; ++r)
-                if (r != rank) *reinterpret_cast<float4*>(peers.out[r] + off) = v;
+#pragma unroll
+            for (int r = 0; r < kMaxRanks; ++r)
+                if (r < pg.world && r != pg.rank) *reinterpret_cast<float4*>(pg.out[r] + off) = v;
         }
     } else {
         for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -81,40 +80,13 @@ __global__ void __launch_bounds__(256) exchange_kernel(const float* __restrict__
             const int64_t m = i / cols;
             const int64_t off = m * N + n0 + (i % cols);
             const float v = out[off];
-            for (int r = 0; r < world; ++r)
-                if (r != rank) peers.out[r][off] = v;
+#pragma unroll
+            for (int r = 0; r < kMaxRanks; ++r)
+                if (r < pg.world && r != pg.rank) pg.out[r][off] = v;
         }
     }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0)
-        for (int r = 0; r < world; ++r) atomicAdd_system(peers.sig[r] + rank, 1u);
-}
-
-// Waits until every rank's counter in this rank's signal array reached the target of this
-// epoch.  epoch == 0: the epoch is kept on the device (sig[kMaxRanks] counts this rank's
-// completed exchanges), so the launch sequence can be captured in a CUDA graph and replayed.
-__global__ void wait_kernel(uint32_t* sig, int world, uint32_t epoch, uint32_t per_epoch) {
-    __shared__ uint32_t s_epoch;
-    if (threadIdx.x == 0) s_epoch = epoch ? epoch : sig[kMaxRanks] + 1;
-    __syncthreads();
-    const uint32_t target = s_epoch * per_epoch;
-    const int r = threadIdx.x;
-    if (r < world) {
-        const uint64_t t0 = globaltimer_ns();
-        for (;;) {
-            uint32_t v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(sig + r) : "memory");
-            if (static_cast<int32_t>(v - target) >= 0) break;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                record_device_error(kDevErrPeerWait);
-                break;
-            }
-            __nanosleep(128);
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && epoch == 0) sig[kMaxRanks] = s_epoch;
+    __syncthreads();   // every thread's stores before thread 0's system-scope fence
+    if (threadIdx.x == 0) peer_gather_finish(pg);
 }
 
 // Peer allocations mapped into this process, shared by every pointer inside them.
@@ -224,14 +196,18 @@ int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1, con
         !packed)
         return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: bad arguments");
     if (n0 < 0 || n1 > N || n0 > n1) return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: bad column range");
-    PeerSet peers{};
+    PeerGather pg;
+    pg.world = world;
+    pg.rank = rank;
+    pg.epoch = epoch;
     for (int r = 0; r < world; ++r) {
         if (!peer_out[r] || !peer_signal[r]) return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: peer %d missing", r);
-        peers.out[r] = static_cast<float*>(peer_out[r]);
-        peers.sig[r] = peer_signal[r];
+        pg.out[r] = static_cast<float*>(peer_out[r]);
+        pg.sig[r] = peer_signal[r];
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int cols = n1 - n0;
+    bool fused = false;
     if (cols > 0) {
         if (int rc = check_tile_gemm(fmt, M, K, cols, static_cast<int64_t>(M) * K, packed_len, scale_base, lut_len,
                                      lut_base, static_cast<int64_t>(M) * cols))
@@ -245,12 +221,18 @@ int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1, con
         a.stream = s;
         int route = 0;
         if (int rc = choose_route(a, BYBYCU_ROUTE_AUTO, &route)) return rc;
-        if (int rc = run_gemm(a, route)) return rc;
+        if (route == BYBYCU_ROUTE_GEMV) {
+            // the GEMV stores every value to the peers itself and ends with the signals
+            if (int rc = launch_gemv(a, &pg)) return rc;
+            fused = true;
+        } else if (int rc = run_gemm(a, route)) {
+            return rc;
+        }
     }
-    exchange_kernel<<<kExchangeCtas, 256, 0, s>>>(static_cast<const float*>(out), M, N, n0, n1, peers, world, rank);
-    BYBYCU_LAUNCH_CHECK("exchange_kernel");
-    wait_kernel<<<1, 32, 0, s>>>(peer_signal[rank], world, epoch, static_cast<uint32_t>(kExchangeCtas));
-    BYBYCU_LAUNCH_CHECK("wait_kernel");
+    if (!fused) {
+        exchange_kernel<<<kExchangeCtas, 256, 0, s>>>(static_cast<const float*>(out), M, N, n0, n1, pg);
+        BYBYCU_LAUNCH_CHECK("exchange_kernel");
+    }
     return BYBYCU_OK;
 }
 

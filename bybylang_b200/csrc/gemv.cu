@@ -492,8 +492,10 @@ constexpr int kM1KC = 1024;
 constexpr int kM1Parts = kM1Warps / 4;            // warps per box
 constexpr int kM1Blocks = 8 / kM1Parts;           // blocks per warp
 
+// Two CTAs per SM: the register cap (96) lets the next launch's CTA sit beside the running
+// one, so its producer streams weights while this one computes (programmatic dependent launch).
 template <int TP, bool STMA, bool F16A>
-__global__ void __launch_bounds__(kM1Threads, 1)
+__global__ void __launch_bounds__(kM1Threads, 2)
 gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
     constexpr int S = 2 * kM1Blocks;   // MMA steps per warp per box (low / high half per block)
     extern __shared__ __align__(1024) uint8_t smem_raw[];

@@ -263,6 +263,7 @@ __device__ __forceinline__ void dequant_word(uint32_t v, __half2 s, __half2 s16,
 template <bool XF32>
 __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x, uint4* __restrict__ xp,
                                                       int64_t nblocks) {
+    pdl_launch_dependents();   // the GEMM may start its prologue; it waits before reading xp
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= nblocks) return;
     float v[32];
@@ -356,6 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // ------------------------------------------------------------ activation producer
         if (lane == 0) {
             prefetch_tensormap(&maps.x);
+            pdl_wait();   // the staging pass that writes xp has completed
             int issued = 0;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
                 const int tile = pair + t * pairs;
@@ -696,17 +698,21 @@ static int tc_run(const GemmArgs& a, int max_pairs, void* xp) {
     p.out_bf16 = a.out_dtype == BYBYCU_DT_BF16;
     const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // the GEMM's prologue, weight loads and first dequantization overlap the staging pass;
+    // only its activation producer waits for that pass (griddepcontrol.wait)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(tc::kThreads);
     cfg.dynamicSmemBytes = tc::kSmemBytes;
     cfg.stream = a.stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel, maps, p));
     return BYBYCU_OK;
 }

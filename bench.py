@@ -17,8 +17,9 @@ fp32 out - through libbybycuda's GEMV route.  Algorithmic bytes per step: 25,362
 
 N > 1 GPUs (torchrun, one process per GPU): weak scaling.  Each rank owns an 11008-column
 shard of a [11008*N, 4096] Q4B32 projection and every step ends with the device-side
-all-gather of the fp32 output slices over NVLink (bybycu_tile_gemm_allgather); value = all
-ranks' bytes / max-over-ranks time.
+all-gather of the fp32 output slices over NVLink (bybycu_tile_gemm_allgather: one launch, the
+GEMV stores to the peers itself); value = all ranks' bytes / max-over-ranks time.  e2e at N > 1:
+upload x, the gathered GEMV, download the whole [1, 11008*N] output, sync - on every rank.
 
 `--impl reference` times the reference's CPU implementation (oracle/_ref, column-sharded over
 all host threads) on the same workload and prints the same line with "impl": "reference".
@@ -247,7 +248,7 @@ def main():
                 C.c_void_p(w.packed.data_ptr()), w.packed.numel(), w.scale_base, None, 0, 0,
                 C.c_void_p(bufs.out.data_ptr()), bufs.peer_out, bufs.peer_sig, world, rank, 0,
                 C.c_void_p(stream.cuda_stream)))
-        launches_per_step = 3
+        launches_per_step = 1   # the GEMV stores to the peers and waits in the same launch
     else:
         outs = [torch.empty(M_DEC, N_DEC, dtype=torch.float32, device=dev) for _ in range(copies)]
 
@@ -310,6 +311,41 @@ def main():
 
     # ---- e2e through the C-ABI host entry (N = 1), host buffers, copies inside the timed region
     e2e = None
+    if world > 1:
+        # every step on every rank: pinned x -> device (bybycu_upload), the sharded GEMV with its
+        # device all-gather, the gathered [1, N_total] output -> pinned host (bybycu_download),
+        # stream sync; the max over ranks of the host-timed loop
+        lib = _lib.load()
+        xh = x.cpu().pin_memory()
+        oh = torch.empty(M_DEC, N_total, dtype=torch.float32).pin_memory()
+        xd = torch.empty_like(x)
+        sp = C.c_void_p(stream.cuda_stream)
+        x_bytes, o_bytes = M_DEC * K_DEC * 2, M_DEC * N_total * 4
+
+        def e2e_step(i):
+            w = weights[i % copies]
+            _lib.check(lib.bybycu_upload(C.c_void_p(xd.data_ptr()), C.c_void_p(xh.data_ptr()), x_bytes, sp))
+            _lib.check(lib.bybycu_tile_gemm_allgather(
+                2, M_DEC, K_DEC, N_total, n0, n1, C.c_void_p(xd.data_ptr()), _lib.DT_BF16,
+                C.c_void_p(w.packed.data_ptr()), w.packed.numel(), w.scale_base, None, 0, 0,
+                C.c_void_p(bufs.out.data_ptr()), bufs.peer_out, bufs.peer_sig, world, rank, 0, sp))
+            _lib.check(lib.bybycu_download(C.c_void_p(oh.data_ptr()), C.c_void_p(bufs.out.data_ptr()), o_bytes, sp))
+            _lib.check(lib.bybycu_synchronize(sp))
+        for i in range(max(args.warmup, 20)):
+            e2e_step(i)
+        n_e2e = min(steps, 5000)
+        dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(n_e2e):
+            e2e_step(i)
+        el = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+        dist.all_reduce(el, op=dist.ReduceOp.MAX)
+        el = float(el.item())
+        e2e = {"value": round(STEP_BYTES * world * n_e2e / el / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": x_bytes * world, "d2h_bytes_per_step": o_bytes * world,
+               "steps": n_e2e, "us_per_step": round(el / n_e2e * 1e6, 2),
+               "api": "bybycu_upload + bybycu_tile_gemm_allgather + bybycu_download + bybycu_synchronize "
+                      "(C ABI) on every rank, pinned host x/out, max over ranks"}
     if world == 1:
         lib = _lib.load()
         xh = x.cpu().pin_memory()

@@ -308,12 +308,21 @@ int bybycu_tile_gemm_host(int fmt, int M, int K, int N, const void* x_host, int 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int64_t xb = static_cast<int64_t>(M) * K * (x_dtype == BYBYCU_DT_BF16 ? 2 : 4);
     const int64_t ob = static_cast<int64_t>(M) * N * (out_dtype == BYBYCU_DT_BF16 ? 2 : 4);
+    // Page-locked, mapped host output: the kernel stores the result straight into it over
+    // PCIe (no device-to-host copy, no copy-engine latency); otherwise out_dev and a copy.
+    void* out_target = out_dev;
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, out_host) == cudaSuccess && pa.type == cudaMemoryTypeHost && pa.devicePointer)
+        out_target = pa.devicePointer;
+    else
+        cudaGetLastError();   // a pageable pointer is not an error here
     BYBYCU_CUDA_TRY(cudaMemcpyAsync(x_dev, x_host, static_cast<size_t>(xb), cudaMemcpyHostToDevice, s));
     if (int rc = tile_gemm_impl(fmt, M, K, N, x_dev, x_dtype, static_cast<int64_t>(M) * K, packed, packed_len,
-                                scale_base, lut, lut_len, lut_base, out_dev, out_dtype, static_cast<int64_t>(M) * N,
+                                scale_base, lut, lut_len, lut_base, out_target, out_dtype, static_cast<int64_t>(M) * N,
                                 route, s))
         return rc;
-    BYBYCU_CUDA_TRY(cudaMemcpyAsync(out_host, out_dev, static_cast<size_t>(ob), cudaMemcpyDeviceToHost, s));
+    if (out_target == out_dev)
+        BYBYCU_CUDA_TRY(cudaMemcpyAsync(out_host, out_dev, static_cast<size_t>(ob), cudaMemcpyDeviceToHost, s));
     BYBYCU_CUDA_TRY(cudaStreamSynchronize(s));
     return BYBYCU_OK;
 }

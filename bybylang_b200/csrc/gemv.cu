@@ -39,6 +39,8 @@
 
 #include "kernels.h"
 
+#include <mutex>
+
 namespace bybycu {
 
 namespace {
@@ -791,6 +793,67 @@ bool gemv_supports(const GemmArgs& a) {
     return true;
 }
 
+// The tensor maps of one weight slot and tiling.  Encoding six maps costs microseconds per
+// call, a large share of a decode step's host time, so encoded sets are kept per device in a
+// small direct-mapped cache keyed by everything the maps depend on (a map holds only the
+// address, the shape and the box; the same key always encodes the same maps).
+int gemv_maps(const GemmArgs& a, int tp, int kc, bool scale_tma, uint32_t s_pitch, GemvMaps* maps) {
+    struct Entry {
+        const void* packed = nullptr;
+        int64_t scale_base = 0;
+        int K = 0, N = 0, tp = 0, kc = 0, device = -1;
+        bool scale_tma = false;
+        GemvMaps maps;
+    };
+    constexpr int kEntries = 64;
+    static Entry cache[kEntries];
+    static std::mutex mu;
+    int device = 0;
+    BYBYCU_CUDA_TRY(cudaGetDevice(&device));
+    const uint64_t key = reinterpret_cast<uintptr_t>(a.packed) ^ (static_cast<uint64_t>(a.N) << 20) ^
+                         (static_cast<uint64_t>(a.K) << 40) ^ static_cast<uint64_t>(tp * 131 + kc + device * 7919);
+    const int slot = static_cast<int>((key ^ (key >> 17) ^ (key >> 33)) % kEntries);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        const Entry& e = cache[slot];
+        if (e.packed == a.packed && e.scale_base == a.scale_base && e.K == a.K && e.N == a.N && e.tp == tp &&
+            e.kc == kc && e.device == device && e.scale_tma == scale_tma) {
+            *maps = e.maps;
+            return BYBYCU_OK;
+        }
+    }
+    const uint8_t* scale_ptr = a.packed + a.scale_base;
+    const int G = a.K / 32;
+    const int box_rows[3] = {16 * tp, 16 * std::max(1, tp - 1), 16};
+    for (int i = 0; i < 3; ++i) {
+        if (int rc = encode_tensor_map_2d(&maps->w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.N, a.K / 2,
+                                          128, box_rows[i], CU_TENSOR_MAP_SWIZZLE_128B,
+                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+            return rc;
+        if (scale_tma) {
+            if (int rc = encode_tensor_map_2d(&maps->s[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, scale_ptr, G, a.N,
+                                              static_cast<uint64_t>(G) * 2, kc / 32, box_rows[i],
+                                              s_pitch == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
+                return rc;
+        } else {
+            maps->s[i] = maps->w[i];   // unused
+        }
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    Entry& e = cache[slot];
+    e.packed = a.packed;
+    e.scale_base = a.scale_base;
+    e.K = a.K;
+    e.N = a.N;
+    e.tp = tp;
+    e.kc = kc;
+    e.device = device;
+    e.scale_tma = scale_tma;
+    e.maps = *maps;
+    return BYBYCU_OK;
+}
+
 int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     DeviceInfo dev;
     if (int rc = current_device_info(&dev)) return rc;
@@ -874,22 +937,7 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     const size_t smem = 1024 + static_cast<size_t>(stages) * (stage_bytes + 16) + 16 + red_bytes;
 
     GemvMaps maps;
-    const int box_rows[3] = {16 * tp, 16 * std::max(1, tp - 1), 16};
-    for (int i = 0; i < 3; ++i) {
-        if (int rc = encode_tensor_map_2d(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.N, a.K / 2,
-                                          128, box_rows[i], CU_TENSOR_MAP_SWIZZLE_128B,
-                                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
-            return rc;
-        if (scale_tma) {
-            if (int rc = encode_tensor_map_2d(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, scale_ptr, G, a.N,
-                                              static_cast<uint64_t>(G) * 2, kc / 32, box_rows[i],
-                                              s_pitch == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-                                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
-                return rc;
-        } else {
-            maps.s[i] = maps.w[i];   // unused
-        }
-    }
+    if (int rc = gemv_maps(a, tp, kc, scale_tma, s_pitch, &maps)) return rc;
     const cudaStream_t st = a.stream;
     if (m1) {
         if (scale_tma) return tpl == 2 ? launch_m1<2, true>(maps, p, grid, smem, st) : launch_m1<5, true>(maps, p, grid, smem, st);

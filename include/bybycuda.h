@@ -121,8 +121,10 @@ BYBYCU_API int bybycu_tile_gemm(int fmt, int M, int K, int N,
                      int route, void* stream);
 
 /* The same op with HOST activations and output and DEVICE-resident weights: copies x in,
- * runs the op and copies out back, synchronising `stream` before it returns.  The
- * immediate-mode form of the path (gpuMatmulQ4, gpubackend.nim:806-843). */
+ * runs the op and copies out back, synchronising `stream` before it returns.  When out_host
+ * is page-locked, mapped host memory (cudaHostAlloc / cudaHostRegister) the kernel stores the
+ * result straight into it and out_dev is not used.  The immediate-mode form of the path
+ * (gpuMatmulQ4, gpubackend.nim:806-843). */
 BYBYCU_API int bybycu_tile_gemm_host(int fmt, int M, int K, int N,
                           const void* x_host, int x_dtype,
                           const void* packed, int64_t packed_len, int64_t scale_base,

@@ -36,7 +36,8 @@ constexpr int kTokCta = kBN / 2;    // token rows each CTA loads
 constexpr int kXK = 128;            // K per activation stage: two 128-byte swizzle rows of fp16
 constexpr int kXSub = 64;           // K per 128-byte swizzle row (one TMA box)
 constexpr int kWK = 256;            // K per weight stage: 128 packed bytes per row
-constexpr int kStages = 4;          // activation stages in shared memory = A slots in TMEM
+constexpr int kStages = 8;          // activation stages in shared memory
+constexpr int kASlots = 4;          // dequantized weight (A) slots in tensor memory
 constexpr int kWStages = 3;         // weight stages in shared memory
 constexpr int kSubs = kWK / kXK;    // activation stages per weight stage
 // 16 warps: 0 X TMA, 1 MMA (even CTA) + TMEM alloc, 2 W TMA, 3 X relay (odd CTA),
@@ -53,15 +54,16 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCols = kBN;                 // one accumulator buffer: a column per token
 constexpr uint32_t kAOff = 2 * kAccCols;           // A slots after the two accumulator buffers
 constexpr uint32_t kACols = kXK / 2;               // A slot: two fp16 per column
-static_assert(kAOff + kStages * kACols <= kTmemCols, "tensor memory budget");
+static_assert(kAOff + kASlots * kACols <= kTmemCols, "tensor memory budget");
+static_assert(kStages % kASlots == 0 && kASlots % 2 == 0, "stage i uses A slot i % kASlots; dequant groups alternate");
 
 constexpr uint32_t kOffX = 0;
 constexpr uint32_t kOffW = kOffX + kStages * kXStageBytes;
 constexpr uint32_t kOffS = kOffW + kWStages * kWStageBytes;
 constexpr uint32_t kOffBar = kOffS + kWStages * kSStageBytes;
-// barriers: full, stage_empty [kStages]; w_full, w_empty [kWStages]; d_full, d_empty [2];
-// done; then the TMEM base address and the abort flag
-constexpr uint32_t kNumBars = 2 * kStages + 2 * kWStages + 5;
+// barriers: full, x_empty [kStages]; a_empty [kASlots]; w_full, w_empty [kWStages];
+// d_full, d_empty [2]; done; then the TMEM base address and the abort flag
+constexpr uint32_t kNumBars = 2 * kStages + kASlots + 2 * kWStages + 5;
 // Arrivals that complete a stage on rank 0: its own TMA (with the bytes), the odd CTA's relay
 // and the eight dequant warps of the pair.  The MMA thread polls this one barrier per stage:
 // every shared-memory access of that thread stalls it for ~140 cycles while the tensor core
@@ -180,6 +182,35 @@ __device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint32_t a_tmem, uint6
         "setp.ne.b32 p, %4, 0;\n\t"
         "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+// One activation stage: eight 256 x 128 x 16 MMAs over K = 128 from one elected lane (the
+// first accumulating only when `accumulate` is set).  When `release` is set the previous
+// stage's two release commits (activation stage and A slot, both CTAs) follow the first MMA,
+// so a stage is freed as soon as possible without a commit between two queued MMAs.
+__device__ __forceinline__ void mma_pair_stage(uint32_t d_tmem, uint32_t a0, const uint64_t (&b)[8],
+                                               uint32_t accumulate, uint32_t release, uint32_t x_bar,
+                                               uint32_t a_bar) {
+    asm volatile(
+        "{\n\t.reg .pred e, p, q, r;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %2, 0;\n\t"
+        "setp.eq.b32 q, %2, %2;\n\t"
+        "setp.ne.and.b32 r, %19, 0, e;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %4, %3, p;\n\t"
+        "@r tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%20], %22;\n\t"
+        "@r tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%21], %22;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %6, %3, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %8, %3, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%9], %10, %3, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%11], %12, %3, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%13], %14, %3, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%15], %16, %3, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%17], %18, %3, q;\n\t}" ::"r"(d_tmem),
+        "r"(a0), "r"(accumulate), "r"(kIdesc), "l"(b[0]), "r"(a0 + 8), "l"(b[1]), "r"(a0 + 16), "l"(b[2]),
+        "r"(a0 + 24), "l"(b[3]), "r"(a0 + 32), "l"(b[4]), "r"(a0 + 40), "l"(b[5]), "r"(a0 + 48), "l"(b[6]),
+        "r"(a0 + 56), "l"(b[7]), "r"(release), "r"(x_bar), "r"(a_bar), "h"(static_cast<uint16_t>(0x3))
         : "memory");
 }
 
@@ -313,8 +344,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     // full[s]: on rank 0 the whole stage is ready (both activation halves, both A slots);
     // on rank 1 its own activation half landed (its relay forwards that to rank 0)
     uint64_t* full = bars;
-    uint64_t* stage_empty = bars + kStages;      // the pair's MMAs finished with the stage
-    uint64_t* w_full = bars + 2 * kStages;
+    uint64_t* x_empty = bars + kStages;          // the pair's MMAs finished with the activation stage
+    uint64_t* a_empty = bars + 2 * kStages;      // ... and with the A slot
+    uint64_t* w_full = a_empty + kASlots;
     uint64_t* w_empty = w_full + kWStages;
     uint64_t* d_full = w_empty + kWStages;       // [2] accumulator buffer complete
     uint64_t* d_empty = d_full + 2;              // [2] (rank 0) both epilogues read it
@@ -328,8 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&full[i], leader ? kFullArrivals : 1);
-            mbar_init(&stage_empty[i], 1);
+            mbar_init(&x_empty[i], 1);
         }
+        for (int i = 0; i < kASlots; ++i) mbar_init(&a_empty[i], 1);
         for (int i = 0; i < kWStages; ++i) {
             mbar_init(&w_full[i], 1);
             mbar_init(&w_empty[i], 8);       // both dequant groups
@@ -364,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 const int tok = (tile / p.tiles_n) * kBN + static_cast<int>(rank) * kTokCta;
                 for (int ks = 0; ks < n_ks; ++ks) {
                     const int s = issued % kStages, r = issued / kStages;
-                    if (r > 0 && !wait_bar(&stage_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
+                    if (r > 0 && !wait_bar(&x_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
                         *s_abort = 1;
                         break;
                     }
@@ -379,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             // rank 1 waits for its copies to land; rank 0's own full barrier also counts the
             // other arrivals, so it waits for the pair's MMAs to release the stages instead
             for (int it = issued > kStages ? issued - kStages : 0; it < issued; ++it) {
-                const bool landed = leader ? wait_bar(&stage_empty[it % kStages], (it / kStages) & 1, kDevErrDrainWait)
+                const bool landed = leader ? wait_bar(&x_empty[it % kStages], (it / kStages) & 1, kDevErrDrainWait)
                                            : wait_bar(&full[it % kStages], (it / kStages) & 1, kDevErrDrainWait);
                 if (!landed) break;
             }
@@ -429,6 +462,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // A stage's release (its commit) is issued after the next stage's first MMA, so the
         // commit never stands between two MMAs in the issue stream.
         if (leader) {
+            // stage i frees its activation stage and its A slot once its MMAs completed
+            auto release_stage = [&](int i) {
+                tc_commit_pair(&x_empty[i % kStages]);
+                tc_commit_pair(&a_empty[i % kASlots]);
+            };
             int consumed = 0, pending = -1;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
                 const int b = t & 1, u = t >> 1;
@@ -447,27 +485,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     }
                     tc_fence_after();
                     const uint64_t bdesc = sw128_desc(base + kOffX + s * kXStageBytes);
-                    const uint32_t a0 = tmem + kAOff + s * kACols;
+                    const uint32_t a0 = tmem + kAOff + (consumed % kASlots) * kACols;
+                    // 16-K steps advance 32 bytes inside a 128-byte swizzle row, then jump to
+                    // the next 64-K box
+                    uint64_t bk[8];
 #pragma unroll
-                    for (int k16 = 0; k16 < kXK / 16; ++k16) {
-                        // 16-K steps advance 32 bytes inside a 128-byte swizzle row, then jump
-                        // to the next 64-K box
-                        const uint64_t bk = bdesc + static_cast<uint64_t>((k16 >> 2) * (kXSubBytes >> 4) + (k16 & 3) * 2);
-                        mma_pair(d_tmem, a0 + k16 * 8, bk, (ks | k16) != 0);
-                        if (k16 == 0 && pending >= 0) tc_commit_pair(&stage_empty[pending]);
-                    }
-                    pending = s;
+                    for (int k16 = 0; k16 < kXK / 16; ++k16)
+                        bk[k16] = bdesc + static_cast<uint64_t>((k16 >> 2) * (kXSubBytes >> 4) + (k16 & 3) * 2);
+                    const int pv = pending >= 0 ? pending : 0;
+                    mma_pair_stage(d_tmem, a0, bk, ks != 0, pending >= 0, smem_u32(&x_empty[pv % kStages]),
+                                   smem_u32(&a_empty[pv % kASlots]));
+                    pending = consumed;
                     ++consumed;
                 }
                 if (!ok) {
                     *s_abort = 1;
                     break;
                 }
-                tc_commit_pair(&stage_empty[pending]);   // the tile's last stage
+                release_stage(pending);   // the tile's last stage
                 pending = -1;
                 tc_commit_pair(&d_full[b]);
             }
-            if (pending >= 0) tc_commit_pair(&stage_empty[pending]);
+            if (pending >= 0) release_stage(pending);
             // every MMA issued above has completed before the tensor memory is freed
             tc_commit_local(done_bar);
             __all_sync(0xffffffffu, wait_bar(done_bar, 0, kDevErrMmaWait));
@@ -499,8 +538,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 if (lane == 0) mbar_arrive(&w_empty[ws]);
                 ++w_used;
                 const int i = t * n_ks + kw * kSubs + grp;          // stage index; i % 2 == grp
-                const int s = i % kStages, r = i / kStages;
-                if (r > 0) ok = wait_bar(&stage_empty[s], (r - 1) & 1, kDevErrEmptyWait);
+                const int s = i % kStages;                          // its activation stage (full barrier)
+                const int slot = i % kASlots, r = i / kASlots;      // its A slot
+                if (r > 0) ok = wait_bar(&a_empty[slot], (r - 1) & 1, kDevErrEmptyWait);
                 ok = __all_sync(0xffffffffu, ok && !*s_abort);
                 if (!ok) break;
                 tc_fence_after();
@@ -520,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         dequant_word(u.z, sv, s16, &col[16 * h + 8]);
                         dequant_word(u.w, sv, s16, &col[16 * h + 12]);
                     }
-                    tmem_st32(tmem + lane_addr + kAOff + s * kACols + half * 32, col);
+                    tmem_st32(tmem + lane_addr + kAOff + slot * kACols + half * 32, col);
                 }
                 tc_wait_st();
                 tc_fence_before();

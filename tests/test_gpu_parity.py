@@ -303,3 +303,44 @@ def test_host_io_entry_point(oracle_mod):
                                      C.c_void_p(xd.data_ptr()), C.c_void_p(od.data_ptr()), _lib.ROUTE_AUTO, None)
     assert rc == 0, _lib.last_error()
     assert_close(O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, M, K, N, threads=8), oh.numpy())
+
+
+# ----------------------------------------------------------------------------------------
+# Failure detection without a GPU fault: a peer that never signals
+# ----------------------------------------------------------------------------------------
+
+def test_allgather_wait_for_a_silent_peer_times_out_and_reports():
+    """world = 2 with rank 1 absent: its output and signal arrays are local buffers that no
+    kernel ever signals.  The GEMV's bounded wait gives up after ~2 s, records device error 5
+    (peer wait) and returns; the context stays usable for the next call."""
+    import time
+    from bybylang_b200.formats import synthetic_q4b32, synthetic_x
+    M, K, N = 1, 1024, 256
+    n0, n1 = 0, 128
+    nib, sc = synthetic_q4b32(N, K, seed=3, device=DEV)
+    shard = gb.Q4B32Weights(nib[n0:n1], sc[n0:n1], device=DEV)
+    x = synthetic_x(M, K, seed=4, device=DEV)
+    out = torch.zeros(M, N, dtype=torch.float32, device=DEV)
+    absent_out = torch.zeros(M, N, dtype=torch.float32, device=DEV)
+    sig = [torch.zeros(16, dtype=torch.int32, device=DEV) for _ in range(2)]
+    peer_out = (C.c_void_p * 2)(out.data_ptr(), absent_out.data_ptr())
+    peer_sig = (C.POINTER(C.c_uint32) * 2)(*[C.cast(C.c_void_p(t.data_ptr()), C.POINTER(C.c_uint32)) for t in sig])
+    assert _lib.device_error() == 0
+    t0 = time.time()
+    rc = lib().bybycu_tile_gemm_allgather(2, M, K, N, n0, n1, C.c_void_p(x.data_ptr()), _lib.DT_BF16,
+                                          C.c_void_p(shard.packed.data_ptr()), shard.packed.numel(), shard.scale_base,
+                                          None, 0, 0, C.c_void_p(out.data_ptr()), peer_out, peer_sig, 2, 0, 1, None)
+    assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert _lib.device_error() == 5          # the peer wait ran out
+    assert 1.5 < waited < 30.0
+    # this rank's slice was computed and "sent" before the wait
+    ref = shard.matmul(x)
+    assert torch.equal(out[:, n0:n1], ref)
+    assert torch.equal(absent_out[:, n0:n1], ref)
+    # the context is healthy: an ordinary call still works
+    again = shard.matmul(x)
+    torch.cuda.synchronize()
+    assert torch.equal(again, ref)
+    assert _lib.device_error() == 0

@@ -126,6 +126,25 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], u
           "f"(c[3]));
 }
 
+// d += a * b  (m16n8k32, s8 inputs, s32 accumulators)
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Four bf16 activations (pairs e01, e23) -> one byte each of their fixed-point image
+// X = rint(x * up): the low byte when shift == 0 (as s8: X - 256 h), the high digit
+// h = (X + 128) >> 8 when bias == 128 and shift == 8, so that X = 256 h + sext8(X).
+__device__ __forceinline__ uint32_t digit4(uint32_t e01, uint32_t e23, float up, int bias, int shift) {
+    const int x0 = (__float2int_rn(__uint_as_float(e01 << 16) * up) + bias) >> shift;
+    const int x1 = (__float2int_rn(__uint_as_float(e01 & 0xFFFF0000u) * up) + bias) >> shift;
+    const int x2 = (__float2int_rn(__uint_as_float(e23 << 16) * up) + bias) >> shift;
+    const int x3 = (__float2int_rn(__uint_as_float(e23 & 0xFFFF0000u) * up) + bias) >> shift;
+    return prmt(prmt(x0, x1, 0x0040), prmt(x2, x3, 0x0040), 0x5410);
+}
+
 // fp16 dequantisation: the low nibbles (bits 0-3 / 16-19) become 1024 + (nibble ^ 8) =
 // 1032 + q, the high nibbles stay in place (bits 4-7 / 20-23, still mantissa in fp16) and
 // become 1024 + 16 (nibble ^ 8) = 1152 + 16 q; one LOP3 each.
@@ -484,6 +503,18 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
 // 8 / (kM1Warps / 4) blocks of the box.  The nibble dequantisation (one LOP3 per two weights,
 // after a shift) runs on the ALU pipe, the kernel's binding resource; the block-diagonal
 // selects are computed once per chunk and pinned in registers.
+//
+// The integer mode (the default) skips the dequantisation instead: a packed word already
+// holds eight signed nibbles, and one AND (after a 4-bit shift for the low nibbles) turns it
+// into four s8 values 16 q in exactly the K order of an m16n8k32 A fragment.  The activations
+// of each 32-block become a fixed-point image X = rint(x * 2^(140 - E)) (E = the block's
+// largest bf16 exponent, so |X| <= 2^14: exact for every element within 7 binades of the
+// block's largest, 2^-15 of it otherwise) split into two signed byte digits,
+// X = 256 h + sext8(X).  The four blocks of a warp share one accumulator: block j's low and
+// high digits occupy B columns 2j and 2j+1, so four s8 MMAs (K = 32 each) fill all eight
+// columns and lane (g, t) ends with block t's two digit sums for rows g and g + 8, exact in
+// int32.  The epilogue is one integer combine, one conversion and one FMA with
+// scale * 2^(E - 144) per row and block.
 // ----------------------------------------------------------------------------------------
 #ifndef BYBYCU_GEMV_M1_WARPS
 #define BYBYCU_GEMV_M1_WARPS 8
@@ -493,13 +524,88 @@ constexpr int kM1Threads = (kM1Warps + 1) * 32;
 constexpr int kM1KC = 1024;
 constexpr int kM1Parts = kM1Warps / 4;            // warps per box
 constexpr int kM1Blocks = 8 / kM1Parts;           // blocks per warp
+// operand modes of the M = 1 kernel
+constexpr int kM1Bf16 = 0;   // bf16 MMAs on 136 + q
+constexpr int kM1F16 = 1;    // fp16 MMAs on 1032 + q / 1152 + 16 q
+constexpr int kM1I8 = 2;     // s8 MMAs on 16 q and two-digit fixed-point activations
+
+// One 1024-value stage of the integer mode for one warp: blocks blk0 .. blk0 + 3 of box
+// `box` (c0 = the box's first block of K) for the pass's nt tiles.  Lane (g, t) builds digit
+// g % 2 of block g / 2 (its elements 4t..4t+3 and 16+4t..16+4t+3, the B fragment's k slots)
+// and accumulates block t of each tile into acc.
+template <int TP, bool STMA>
+__device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* smem, uint32_t st, int box, int blk0,
+                                            int c0, int g, int t, int t0, int nt, const uint32_t (&woff)[4],
+                                            float (&acc)[TP][2]) {
+    const int q = g >> 1;
+    const bool live = c0 + blk0 + q < p.G;
+    const uint32_t xr = st + p.x_off + (32 * (box * 8 + blk0 + q) + 4 * t) * 2;
+    uint2 lo = make_uint2(0u, 0u), hi = make_uint2(0u, 0u);
+    if (live) {
+        lo = sh_u64(smem, xr);
+        hi = sh_u64(smem, xr + 32);
+    }
+    // the block's largest exponent: the magnitudes' bit patterns order like the values
+    const uint32_t m2 = __vmaxu2(__vmaxu2(lo.x & 0x7FFF7FFFu, lo.y & 0x7FFF7FFFu),
+                                 __vmaxu2(hi.x & 0x7FFF7FFFu, hi.y & 0x7FFF7FFFu));
+    int e = static_cast<int>(max(m2 & 0xFFFFu, m2 >> 16) >> 7);
+    e = max(e, __shfl_xor_sync(0xffffffffu, e, 1));
+    e = max(e, __shfl_xor_sync(0xffffffffu, e, 2));
+    if (e == 255 && t == 0 && !(g & 1)) record_device_error(kDevErrActRange);   // inf or NaN
+    const int ec = max(e, 18);   // blocks below 2^-109 keep a normal fp32 factor
+    const float up = __int_as_float((267 - ec) << 23);   // 2^(140 - ec)
+    const int bias = (g & 1) ? 128 : 0, shift = (g & 1) ? 8 : 0;
+    const uint32_t b0 = digit4(lo.x, lo.y, up, bias, shift);   // k = 4t .. 4t+3
+    const uint32_t b1 = digit4(hi.x, hi.y, up, bias, shift);   // k = 16+4t .. 16+4t+3
+    uint32_t bq[4][2];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        bq[j][0] = q == j ? b0 : 0u;
+        bq[j][1] = q == j ? b1 : 0u;
+        asm volatile("" : "+r"(bq[j][0]), "+r"(bq[j][1]));   // keep them in registers
+    }
+    // lane (g, t) combines block t's digits: lane 8t built them
+    const int et = __shfl_sync(0xffffffffu, ec, 8 * t);
+    const float ft = __int_as_float((et - 17) << 23);   // 2^(et - 144): undoes up and the 16 of 16 q
+    const uint32_t wbox = st + box * p.w_box_bytes;
+#pragma unroll
+    for (int i = 0; i < TP; ++i) {
+        int d[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t wt = wbox + i * (kTileRows * 128) + woff[j];
+            const uint32_t w0 = sh_u32(smem, wt);
+            const uint32_t w8 = sh_u32(smem, wt + 1024);
+            const uint32_t a[4] = {(w0 << 4) & 0xF0F0F0F0u, (w8 << 4) & 0xF0F0F0F0u, w0 & 0xF0F0F0F0u,
+                                   w8 & 0xF0F0F0F0u};
+            mma_s8(d, a, bq[j][0], bq[j][1]);
+        }
+        const float v0 = static_cast<float>(d[0] + d[1] * 256), v8 = static_cast<float>(d[2] + d[3] * 256);
+        float sg, sg8;
+        if constexpr (STMA) {
+            const uint32_t sa = st + p.s_off + (i * kTileRows + g) * p.s_pitch + (box * 8 + blk0 + t) * 2;
+            sg = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(smem + sa)));
+            sg8 = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(smem + sa + 8 * p.s_pitch)));
+        } else {
+            const int64_t r0 = static_cast<int64_t>(t0 + i) * kTileRows + g;
+            const int ca = c0 + blk0 + t;
+            const bool ok0 = i < nt && r0 < p.N && ca < p.G, ok8 = i < nt && r0 + 8 < p.N && ca < p.G;
+            sg = ok0 ? __half2float(p.scales[r0 * p.G + ca]) : 0.0f;
+            sg8 = ok8 ? __half2float(p.scales[(r0 + 8) * p.G + ca]) : 0.0f;
+        }
+        acc[i][0] = fmaf(sg * ft, v0, acc[i][0]);
+        acc[i][1] = fmaf(sg8 * ft, v8, acc[i][1]);
+    }
+}
 
 // Two CTAs per SM: the register cap (96) lets the next launch's CTA sit beside the running
 // one, so its producer streams weights while this one computes (programmatic dependent launch).
-template <int TP, bool STMA, bool F16A>
+template <int TP, bool STMA, int MODE>
 __global__ void __launch_bounds__(kM1Threads, 2)
 gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
     constexpr int S = 2 * kM1Blocks;   // MMA steps per warp per box (low / high half per block)
+    constexpr bool F16A = MODE == kM1F16;
+    static_assert(MODE != kM1I8 || kM1Blocks == 4, "the integer mode fills 8 columns with 4 blocks x 2 digits");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -554,7 +660,11 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
             ok = false;
         }
         const int c0 = chunk * (kM1KC / 32) + box * 8;   // first block of this warp's box
-        if (ok && c0 + blk0 < p.G) {
+        if constexpr (MODE == kM1I8) {
+            if (ok && c0 + blk0 < p.G)
+                m1_i8_stage<TP, STMA>(p, smem, static_cast<uint32_t>(s) * p.stage_bytes, box, blk0, c0, g, t, t0,
+                                      min(p.tp, tile_begin + my_tiles - t0), woff, acc);
+        } else if (ok && c0 + blk0 < p.G) {
             const uint32_t st = static_cast<uint32_t>(s) * p.stage_bytes;   // offset of the stage in smem
             // ---- block g of the box: this lane's activation fragments (zero past K)
             const bool live = c0 + g < p.G;
@@ -736,23 +846,27 @@ int launch_t(const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, c
     return BYBYCU_OK;
 }
 
-// fp16 operands with the high nibbles dequantised in place (5 ALU ops per 8 weights instead
-// of 7); BYBY_CUDA_GEMV_F16=0 selects the bf16 operands (offset 136 instead of 1032/1152).
-bool m1_f16() {
-    static const int on = [] {
-        const char* e = getenv("BYBY_CUDA_GEMV_F16");
-        return (e && e[0] == '0') ? 0 : 1;
+// The operand mode of the M = 1 kernel: s8 MMAs on the raw nibbles (default), or, through
+// BYBY_CUDA_GEMV_M1=f16 / bf16, the dequantising fp16 / bf16 forms kept for comparison.
+int m1_mode() {
+    static const int mode = [] {
+        const char* e = getenv("BYBY_CUDA_GEMV_M1");
+        if (e && !strcmp(e, "f16")) return kM1F16;
+        if (e && !strcmp(e, "bf16")) return kM1Bf16;
+        return kM1I8;
     }();
-    return on != 0;
+    return mode;
 }
 
 template <int TP, bool STMA>
 int launch_m1(const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, cudaStream_t stream) {
-    auto kern = m1_f16() ? gemv_m1_kernel<TP, STMA, true> : gemv_m1_kernel<TP, STMA, false>;
-    static uint64_t configured[2] = {0, 0};
+    const int mode = m1_mode();
+    auto kern = mode == kM1I8 ? gemv_m1_kernel<TP, STMA, kM1I8>
+              : mode == kM1F16 ? gemv_m1_kernel<TP, STMA, kM1F16> : gemv_m1_kernel<TP, STMA, kM1Bf16>;
+    static uint64_t configured[3] = {0, 0, 0};
     int dev = 0;
     BYBYCU_CUDA_TRY(cudaGetDevice(&dev));
-    const int fi = m1_f16() ? 1 : 0;
+    const int fi = mode;
     if (!(configured[fi] >> (dev & 63) & 1)) {
         BYBYCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
         configured[fi] |= uint64_t(1) << (dev & 63);

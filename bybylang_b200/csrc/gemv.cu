@@ -68,6 +68,9 @@ struct GemvParams {
     uint32_t w_box_bytes;          // one nibble box: 16 * TP rows x 128 B
     uint32_t s_off, x_off;         // offsets inside a stage
     uint32_t s_pitch;              // bytes per row of the scale box
+    int x_whole;                   // M = 1 integer mode: the activation row arrives once per launch,
+    uint32_t xbar_off;             // one 1024-value chunk per barrier (then one "digits ready"
+    uint32_t x_all_off;            // barrier per chunk), at x_all_off; block factors after it
     const __half* scales;          // packed + scale_base
     const uint8_t* x;              // activations [M, K] (global)
     int x_elem;                    // 2 (bf16) or 4 (fp32)
@@ -132,17 +135,6 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint
         "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Four bf16 activations (pairs e01, e23) -> one byte each of their fixed-point image
-// X = rint(x * up): the low byte when shift == 0 (as s8: X - 256 h), the high digit
-// h = (X + 128) >> 8 when bias == 128 and shift == 8, so that X = 256 h + sext8(X).
-__device__ __forceinline__ uint32_t digit4(uint32_t e01, uint32_t e23, float up, int bias, int shift) {
-    const int x0 = (__float2int_rn(__uint_as_float(e01 << 16) * up) + bias) >> shift;
-    const int x1 = (__float2int_rn(__uint_as_float(e01 & 0xFFFF0000u) * up) + bias) >> shift;
-    const int x2 = (__float2int_rn(__uint_as_float(e23 << 16) * up) + bias) >> shift;
-    const int x3 = (__float2int_rn(__uint_as_float(e23 & 0xFFFF0000u) * up) + bias) >> shift;
-    return prmt(prmt(x0, x1, 0x0040), prmt(x2, x3, 0x0040), 0x5410);
 }
 
 // fp16 dequantisation: the low nibbles (bits 0-3 / 16-19) become 1024 + (nibble ^ 8) =
@@ -216,7 +208,7 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
             const int kn = min(p.kc, p.K - k0);
             const uint32_t rows = nt * kTileRows;
             const uint32_t bytes = wboxes * rows * 128 + (p.scale_tma ? rows * p.s_pitch : 0) +
-                                   p.M * static_cast<uint32_t>(kn) * p.x_elem;
+                                   (p.x_whole ? 0u : p.M * static_cast<uint32_t>(kn) * p.x_elem);
             uint8_t* st = smem + static_cast<size_t>(s) * p.stage_bytes;
             mbar_arrive_expect_tx(&full_bar[s], bytes);
             // one box per 16 * nt rows when nt is TP or TP - 1, else one per tile
@@ -234,6 +226,7 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
         };
         // Issues the activation rows of iteration `chunk` into stage s.
         auto issue_x = [&](int s, int chunk) {
+            if (p.x_whole) return;
             const int k0 = chunk * p.kc;
             const uint32_t x_row_bytes = static_cast<uint32_t>(min(p.kc, p.K - k0)) * p.x_elem;
             uint8_t* st = smem + static_cast<size_t>(s) * p.stage_bytes;
@@ -251,6 +244,15 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
                 if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
             }
             pdl_wait();
+            if (p.x_whole) {   // the whole row, chunk by chunk, each on its own barrier
+                uint64_t* x_bar = reinterpret_cast<uint64_t*>(smem + p.xbar_off);
+                for (int c = 0; c < p.n_chunks; ++c) {
+                    const uint32_t bytes = static_cast<uint32_t>(min(p.kc, p.K - c * p.kc)) * p.x_elem;
+                    mbar_arrive_expect_tx(&x_bar[c], bytes);
+                    bulk_load_1d(smem + p.x_all_off + static_cast<uint32_t>(c * p.kc) * p.x_elem,
+                                 p.x + static_cast<size_t>(c) * p.kc * p.x_elem, bytes, &x_bar[c]);
+                }
+            }
             chunk = 0;
             for (int it = 0; it < first; ++it) {
                 issue_x(it, chunk);
@@ -277,6 +279,9 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
             const int ds = it % p.stages;
             if (!mbar_wait_bounded(&full_bar[ds], (it / p.stages) & 1, kDevErrDrainWait)) break;
         }
+        if (p.x_whole)
+            for (int c = 0; c < p.n_chunks; ++c)
+                if (!mbar_wait_bounded(reinterpret_cast<uint64_t*>(smem + p.xbar_off) + c, 0, kDevErrDrainWait)) break;
     }
 }
 
@@ -520,7 +525,7 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
 #define BYBYCU_GEMV_M1_WARPS 8
 #endif
 constexpr int kM1Warps = BYBYCU_GEMV_M1_WARPS;   // 8 or 16
-constexpr int kM1Threads = (kM1Warps + 1) * 32;
+constexpr int kM1Threads = (kM1Warps + 2) * 32;   // + the producer and the digit warp
 constexpr int kM1KC = 1024;
 constexpr int kM1Parts = kM1Warps / 4;            // warps per box
 constexpr int kM1Blocks = 8 / kM1Parts;           // blocks per warp
@@ -533,40 +538,144 @@ constexpr int kM1I8 = 2;     // s8 MMAs on 16 q and two-digit fixed-point activa
 // `box` (c0 = the box's first block of K) for the pass's nt tiles.  Lane (g, t) builds digit
 // g % 2 of block g / 2 (its elements 4t..4t+3 and 16+4t..16+4t+3, the B fragment's k slots)
 // and accumulates block t of each tile into acc.
+// The integer mode's activation side, done by the digit warp once per launch: the resident
+// bf16 row is turned in place into B-fragment words.  Lane t of quad g converts blocks g,
+// g + 8, g + 16 and g + 24 of a chunk: in each it reads elements 4t..4t+3 (bytes 8t..8t+7 of
+// the block) and 16+4t..16+4t+3 (bytes 32+8t..) and writes back at exactly those bytes the
+// low and the high digits of the same elements, so block b's 64 bytes become
+// [digit][t][k 4t.. | k 16+4t..] in s8.  X = rint(x * 2^(140 - E)) comes from one FFMA with
+// 1.5 * 2^23, which leaves X, rounded to nearest even, in the float's low bits: its low byte
+// is the low digit, and the second byte of the same sum with 128 more is the high digit
+// (X + 128) >> 8.  The factor 2^(E - 144) of each block (it undoes the scaling and the 16 of
+// the 16 q operands) goes to the factor table.  All loads come before all stores, so the four
+// blocks' dependency chains overlap.
+__device__ __forceinline__ void m1_digits_chunk(const GemvParams& p, uint8_t* smem, int chunk, int g, int t) {
+    constexpr int J = 4;
+    uint2 lo[J], hi[J];
+    uint32_t xr[J];
+    bool live[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int blk = chunk * (kM1KC / 32) + 8 * j + g;
+        live[j] = blk < p.G;
+        xr[j] = p.x_all_off + blk * 64 + 8 * t;
+        lo[j] = live[j] ? sh_u64(smem, xr[j]) : make_uint2(0u, 0u);
+        hi[j] = live[j] ? sh_u64(smem, xr[j] + 32) : make_uint2(0u, 0u);
+    }
+    // each block's largest exponent: magnitude bit patterns order like the values, and inf /
+    // NaN sort above every finite value
+    int e[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const uint32_t m2 = __vmaxu2(__vmaxu2(lo[j].x & 0x7FFF7FFFu, lo[j].y & 0x7FFF7FFFu),
+                                     __vmaxu2(hi[j].x & 0x7FFF7FFFu, hi[j].y & 0x7FFF7FFFu));
+        e[j] = static_cast<int>(max(m2 & 0xFFFFu, m2 >> 16) >> 7);
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) e[j] = max(e[j], __shfl_xor_sync(0xffffffffu, e[j], 1));
+#pragma unroll
+    for (int j = 0; j < J; ++j) e[j] = max(e[j], __shfl_xor_sync(0xffffffffu, e[j], 2));
+    uint32_t out[J][4];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        if (live[j] && e[j] == 255 && t == 0) record_device_error(kDevErrActRange);   // inf or NaN
+        e[j] = max(e[j], 18);                                  // blocks below 2^-109: normal factors
+        const float up = __int_as_float((267 - e[j]) << 23);   // 2^(140 - E)
+        const uint32_t w[4] = {lo[j].x, lo[j].y, hi[j].x, hi[j].y};
+        uint32_t r[8], h[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float f0 = __uint_as_float(w[i] << 16), f1 = __uint_as_float(w[i] & 0xFFFF0000u);
+            r[2 * i] = __float_as_uint(fmaf(f0, up, 12582912.0f));       // 0x4B400000 + X
+            r[2 * i + 1] = __float_as_uint(fmaf(f1, up, 12582912.0f));
+            h[2 * i] = __float_as_uint(fmaf(f0, up, 12583040.0f));       // 0x4B400000 + X + 128
+            h[2 * i + 1] = __float_as_uint(fmaf(f1, up, 12583040.0f));
+        }
+        out[j][0] = prmt(prmt(r[0], r[1], 0x0040), prmt(r[2], r[3], 0x0040), 0x5410);
+        out[j][1] = prmt(prmt(r[4], r[5], 0x0040), prmt(r[6], r[7], 0x0040), 0x5410);
+        out[j][2] = prmt(prmt(h[0], h[1], 0x0051), prmt(h[2], h[3], 0x0051), 0x5410);
+        out[j][3] = prmt(prmt(h[4], h[5], 0x0051), prmt(h[6], h[7], 0x0051), 0x5410);
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        if (!live[j]) continue;
+        *reinterpret_cast<uint2*>(smem + xr[j]) = make_uint2(out[j][0], out[j][1]);
+        *reinterpret_cast<uint2*>(smem + xr[j] + 32) = make_uint2(out[j][2], out[j][3]);
+        if (t == 0)
+            *reinterpret_cast<float*>(smem + p.x_all_off + static_cast<uint32_t>(p.K) * 2 +
+                                      (chunk * (kM1KC / 32) + 8 * j + g) * 4) = __int_as_float((e[j] - 17) << 23);
+    }
+}
+
+// The digit warp: converts chunks 1, 2, ... as their activations land and marks each ready
+// (the consumers build chunk 0's operands themselves from the raw row, so that the first
+// MMAs wait for no conversion).  It always marks a chunk, after a timeout too, so that no
+// consumer waits for it in vain.
+__device__ __forceinline__ void m1_digit_warp(const GemvParams& p, uint8_t* smem, volatile int* s_abort, int lane) {
+    uint64_t* x_bar = reinterpret_cast<uint64_t*>(smem + p.xbar_off);
+    uint64_t* ready = x_bar + p.n_chunks;
+    for (int c = 1; c < p.n_chunks; ++c) {
+        if (!*s_abort && !mbar_wait_bounded(&x_bar[c], 0, kDevErrFullWait)) *s_abort = 1;
+        m1_digits_chunk(p, smem, c, lane >> 2, lane & 3);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[c]);   // release: the digits above before the arrival
+    }
+}
+
+// Four raw bf16 activations (pairs e01, e23) -> one digit byte each, as in m1_digits_chunk:
+// magic 1.5 * 2^23 and byte 0 for the low digit, magic + 128 and byte 1 for the high one.
+__device__ __forceinline__ uint32_t digit4(uint32_t e01, uint32_t e23, float up, float magic, uint32_t sel) {
+    const uint32_t r0 = __float_as_uint(fmaf(__uint_as_float(e01 << 16), up, magic));
+    const uint32_t r1 = __float_as_uint(fmaf(__uint_as_float(e01 & 0xFFFF0000u), up, magic));
+    const uint32_t r2 = __float_as_uint(fmaf(__uint_as_float(e23 << 16), up, magic));
+    const uint32_t r3 = __float_as_uint(fmaf(__uint_as_float(e23 & 0xFFFF0000u), up, magic));
+    return prmt(prmt(r0, r1, sel), prmt(r2, r3, sel), 0x5410);
+}
+
+// The weight side of one chunk in the integer mode for one warp: blocks blk0 .. blk0 + 3 of
+// box `box` (c0 = the box's first block of K) for the pass's nt tiles, accumulated into acc.
+// Lane (g, t) feeds B column g (digit g % 2 of block g / 2) and combines block t's two digit
+// sums for rows g and g + 8.
 template <int TP, bool STMA>
 __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* smem, uint32_t st, int box, int blk0,
                                             int c0, int g, int t, int t0, int nt, const uint32_t (&woff)[4],
-                                            float (&acc)[TP][2]) {
+                                            bool raw, float (&acc)[TP][2]) {
     const int q = g >> 1;
-    const bool live = c0 + blk0 + q < p.G;
-    const uint32_t xr = st + p.x_off + (32 * (box * 8 + blk0 + q) + 4 * t) * 2;
-    uint2 lo = make_uint2(0u, 0u), hi = make_uint2(0u, 0u);
-    if (live) {
-        lo = sh_u64(smem, xr);
-        hi = sh_u64(smem, xr + 32);
+    const int bb = c0 + blk0 + q, bt = c0 + blk0 + t;
+    uint2 dw;
+    float ft;
+    if (raw) {   // chunk 0: the digits from the raw row, here (the same arithmetic as m1_digits_chunk)
+        const uint32_t xr = p.x_all_off + (32 * bb + 4 * t) * 2;
+        uint2 lo = make_uint2(0u, 0u), hi = make_uint2(0u, 0u);
+        if (bb < p.G) {
+            lo = sh_u64(smem, xr);
+            hi = sh_u64(smem, xr + 32);
+        }
+        const uint32_t m2 = __vmaxu2(__vmaxu2(lo.x & 0x7FFF7FFFu, lo.y & 0x7FFF7FFFu),
+                                     __vmaxu2(hi.x & 0x7FFF7FFFu, hi.y & 0x7FFF7FFFu));
+        int e = static_cast<int>(max(m2 & 0xFFFFu, m2 >> 16) >> 7);
+        e = max(e, __shfl_xor_sync(0xffffffffu, e, 1));
+        e = max(e, __shfl_xor_sync(0xffffffffu, e, 2));
+        if (bb < p.G && e == 255 && t == 0 && !(g & 1)) record_device_error(kDevErrActRange);   // inf or NaN
+        e = max(e, 18);
+        const float up = __int_as_float((267 - e) << 23);
+        const float magic = (g & 1) ? 12583040.0f : 12582912.0f;
+        const uint32_t sel = (g & 1) ? 0x0051u : 0x0040u;
+        dw = make_uint2(digit4(lo.x, lo.y, up, magic, sel), digit4(hi.x, hi.y, up, magic, sel));
+        const int et = __shfl_sync(0xffffffffu, e, 8 * t);   // lane 8t built block t
+        ft = bt < p.G ? __int_as_float((et - 17) << 23) : 0.0f;
+    } else {
+        dw = bb < p.G ? sh_u64(smem, p.x_all_off + bb * 64 + (g & 1) * 32 + 8 * t) : make_uint2(0u, 0u);
+        ft = bt < p.G ? *reinterpret_cast<const float*>(smem + p.x_all_off + static_cast<uint32_t>(p.K) * 2 + bt * 4)
+                      : 0.0f;
     }
-    // the block's largest exponent: the magnitudes' bit patterns order like the values
-    const uint32_t m2 = __vmaxu2(__vmaxu2(lo.x & 0x7FFF7FFFu, lo.y & 0x7FFF7FFFu),
-                                 __vmaxu2(hi.x & 0x7FFF7FFFu, hi.y & 0x7FFF7FFFu));
-    int e = static_cast<int>(max(m2 & 0xFFFFu, m2 >> 16) >> 7);
-    e = max(e, __shfl_xor_sync(0xffffffffu, e, 1));
-    e = max(e, __shfl_xor_sync(0xffffffffu, e, 2));
-    if (e == 255 && t == 0 && !(g & 1)) record_device_error(kDevErrActRange);   // inf or NaN
-    const int ec = max(e, 18);   // blocks below 2^-109 keep a normal fp32 factor
-    const float up = __int_as_float((267 - ec) << 23);   // 2^(140 - ec)
-    const int bias = (g & 1) ? 128 : 0, shift = (g & 1) ? 8 : 0;
-    const uint32_t b0 = digit4(lo.x, lo.y, up, bias, shift);   // k = 4t .. 4t+3
-    const uint32_t b1 = digit4(hi.x, hi.y, up, bias, shift);   // k = 16+4t .. 16+4t+3
     uint32_t bq[4][2];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        bq[j][0] = q == j ? b0 : 0u;
-        bq[j][1] = q == j ? b1 : 0u;
+        bq[j][0] = q == j ? dw.x : 0u;
+        bq[j][1] = q == j ? dw.y : 0u;
         asm volatile("" : "+r"(bq[j][0]), "+r"(bq[j][1]));   // keep them in registers
     }
-    // lane (g, t) combines block t's digits: lane 8t built them
-    const int et = __shfl_sync(0xffffffffu, ec, 8 * t);
-    const float ft = __int_as_float((et - 17) << 23);   // 2^(et - 144): undoes up and the 16 of 16 q
     const uint32_t wbox = st + box * p.w_box_bytes;
 #pragma unroll
     for (int i = 0; i < TP; ++i) {
@@ -628,6 +737,8 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], kM1Warps);
         }
+        if (MODE == kM1I8)   // per chunk: activations landed, digits ready
+            for (int c = 0; c < 2 * p.n_chunks; ++c) mbar_init(reinterpret_cast<uint64_t*>(smem + p.xbar_off) + c, 1);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -635,6 +746,10 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
 
     if (warp == kM1Warps) {
         gemv_producer(maps, p, smem, full_bar, empty_bar, s_abort, lane, tile_begin, my_tiles, total_it);
+        return;
+    }
+    if (warp == kM1Warps + 1) {
+        if constexpr (MODE == kM1I8) m1_digit_warp(p, smem, s_abort, lane);
         return;
     }
 
@@ -661,9 +776,16 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
         }
         const int c0 = chunk * (kM1KC / 32) + box * 8;   // first block of this warp's box
         if constexpr (MODE == kM1I8) {
+            // chunk 0: its raw activations; later chunks: their digits (each completes once
+            // per launch, so later passes find them ready)
+            uint64_t* xb = reinterpret_cast<uint64_t*>(smem + p.xbar_off);
+            if (ok && !mbar_wait_bounded(chunk == 0 ? xb : xb + p.n_chunks + chunk, 0, kDevErrFullWait)) {
+                *s_abort = 1;
+                ok = false;
+            }
             if (ok && c0 + blk0 < p.G)
                 m1_i8_stage<TP, STMA>(p, smem, static_cast<uint32_t>(s) * p.stage_bytes, box, blk0, c0, g, t, t0,
-                                      min(p.tp, tile_begin + my_tiles - t0), woff, acc);
+                                      min(p.tp, tile_begin + my_tiles - t0), woff, chunk == 0, acc);
         } else if (ok && c0 + blk0 < p.G) {
             const uint32_t st = static_cast<uint32_t>(s) * p.stage_bytes;   // offset of the stage in smem
             // ---- block g of the box: this lane's activation fragments (zero past K)
@@ -859,8 +981,7 @@ int m1_mode() {
 }
 
 template <int TP, bool STMA>
-int launch_m1(const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, cudaStream_t stream) {
-    const int mode = m1_mode();
+int launch_m1(int mode, const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, cudaStream_t stream) {
     auto kern = mode == kM1I8 ? gemv_m1_kernel<TP, STMA, kM1I8>
               : mode == kM1F16 ? gemv_m1_kernel<TP, STMA, kM1F16> : gemv_m1_kernel<TP, STMA, kM1Bf16>;
     static uint64_t configured[3] = {0, 0, 0};
@@ -983,6 +1104,15 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     const size_t budget = static_cast<size_t>(dev.max_smem_optin) - 1024 - 64;
 
     const bool m1 = a.M == 1 && !xf32;
+    // The integer mode keeps the whole activation row resident (converted in place into
+    // digits, plus a factor per block and two barriers per 1024-value chunk) instead of a
+    // slice per stage; rows longer than 32768 values take the fp16 mode.
+    const int mode = m1_mode() == kM1I8 && a.K > 32768 ? kM1F16 : m1_mode();
+    const bool x_whole = m1 && mode == kM1I8;
+    const int n_xchunks = static_cast<int>(ceil_div(a.K, kM1KC));
+    const size_t x_all = x_whole ? static_cast<size_t>(n_xchunks) * 16 +
+                                       (static_cast<size_t>(a.K) * xe + static_cast<size_t>(G) * 4 + 15) / 16 * 16
+                                 : 0;
     // K chunk: 512 values (fine pipelining: compute starts after the first 1/(K/512) of the
     // data) with boxes spanning all rows of the pass; larger chunks only when M is large.
     int kc = 0, tp = 0, tpl = 0, stages = 0;
@@ -999,12 +1129,13 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
         const uint32_t so = (kc_try / 256) * wb;
         const uint32_t xo = static_cast<uint32_t>(so + round1k(scale_tma ? rows * sp : 0));
         const int xp = kc_try * xe + 32;
-        const size_t sb = round1k(xo + static_cast<size_t>(a.M) * xp);
+        const size_t sb = round1k(xo + (x_whole ? 0 : static_cast<size_t>(a.M) * xp));
         const size_t rb = m1 ? static_cast<size_t>(kM1Warps) * tpl_try * 16 * sizeof(float)
                              : static_cast<size_t>(kRedSlots) * tpl_try * ntn * 128 * sizeof(float);
         const int nch = static_cast<int>(ceil_div(a.K, kc_try));
         const int want = static_cast<int>(ceil_div(tiles_max, tp_try)) * nch;
-        const int st = static_cast<int>((budget - rb) / (sb + 16));
+        if (budget < rb + x_all + sb + 16) continue;
+        const int st = static_cast<int>((budget - rb - x_all) / (sb + 16));
         if (st >= std::min(m1 ? 2 : 4, want) && st >= 1) {
             kc = kc_try; tp = tp_try; tpl = tpl_try; stages = std::min(st, want);
             stage_bytes = sb; red_bytes = rb; s_pitch = sp; w_box = wb; s_off = so; x_off = xo; x_pitch = xp;
@@ -1048,14 +1179,20 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
         if (p.out_bf16) return set_error(BYBYCU_ERR_ARGS, "GEMV all-gather: the gathered output is fp32");
         p.pg = *pg;
     }
-    const size_t smem = 1024 + static_cast<size_t>(stages) * (stage_bytes + 16) + 16 + red_bytes;
+    const size_t smem = 1024 + static_cast<size_t>(stages) * (stage_bytes + 16) + 16 + red_bytes + x_all;
+    p.x_whole = x_whole ? 1 : 0;
+    p.xbar_off = static_cast<uint32_t>(static_cast<size_t>(stages) * (stage_bytes + 16) + 16 + red_bytes);
+    p.x_all_off = p.xbar_off + static_cast<uint32_t>(n_xchunks) * 16;
 
     GemvMaps maps;
     if (int rc = gemv_maps(a, tp, kc, scale_tma, s_pitch, &maps)) return rc;
     const cudaStream_t st = a.stream;
     if (m1) {
-        if (scale_tma) return tpl == 2 ? launch_m1<2, true>(maps, p, grid, smem, st) : launch_m1<5, true>(maps, p, grid, smem, st);
-        return tpl == 2 ? launch_m1<2, false>(maps, p, grid, smem, st) : launch_m1<5, false>(maps, p, grid, smem, st);
+        if (scale_tma)
+            return tpl == 2 ? launch_m1<2, true>(mode, maps, p, grid, smem, st)
+                            : launch_m1<5, true>(mode, maps, p, grid, smem, st);
+        return tpl == 2 ? launch_m1<2, false>(mode, maps, p, grid, smem, st)
+                        : launch_m1<5, false>(mode, maps, p, grid, smem, st);
     }
     if (ntn == 2) {
         return tpl == 2 ? dispatch_x<2, 2>(xf32, maps, p, grid, smem, st) : dispatch_x<5, 2>(xf32, maps, p, grid, smem, st);

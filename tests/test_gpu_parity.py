@@ -5,6 +5,10 @@ Tolerances (written here, per route):
 * GEMV route: the reference test's own check, max|diff| <= 1e-4 * max(1, max|ref|)
   (tests/t_fp4_tile_gemm.nim:54-67), and per element |diff| <= 1e-3 * max(1, |ref|) (the
   1e-3 relative bound of the path's parity gate, vulkan_driver.nim:2754).
+* GEMV route at M = 1 (the decode kernel's integer mode): the activations of each 32-block
+  become 15-bit fixed point on the block's largest exponent, so besides the bounds above,
+  on inputs of any dynamic range |diff| <= 2^-14 * sum_b max|x_b| * sum_{k in b} |w[n, k]|
+  plus fp32 slack (test_gemv_m1_activation_dynamic_range).
 * dequantisation: bit-exact for every format.
 """
 import ctypes as C
@@ -138,6 +142,60 @@ def test_gemv_ragged_shapes(M, K, N, oracle_mod):
     blob[p.size + 2:] = s.view(np.uint8).ravel()
     out = run(2, M, K, N, dev(xb).view(torch.bfloat16), dev(blob), scale_base=p.size + 2, route=_lib.ROUTE_GEMV)
     assert_close(want, out.cpu().numpy(), what=f"M={M} K={K} N={N} unaligned scales")
+
+
+def _bf16_bits(f):
+    """float32 -> bf16 bits, round to nearest even (finite inputs)."""
+    u = np.ascontiguousarray(f, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+@pytest.mark.parametrize("K,N", [(4096, 2048), (800, 300)])
+def test_gemv_m1_activation_dynamic_range(K, N, oracle_mod):
+    """Activations over 36 binades, zeros, a lone outlier over tiny values, all-tiny blocks:
+    the decode kernel stays inside its fixed-point error bound against the f64 reference."""
+    O = oracle_mod
+    rng = np.random.default_rng(K + N)
+    p, s = O.gen_q4b32(N, K, seed=77)
+    xf = (rng.choice([-1.0, 1.0], K) * np.exp2(rng.uniform(-24, 12, K))).astype(np.float32)
+    xf[rng.random(K) < 0.1] = 0.0
+    xf[3 * 32:4 * 32] = 0.0                         # an all-zero block
+    xf[5 * 32:6 * 32] = 1e-6
+    xf[5 * 32 + 7] = -3e4                           # one outlier over tiny values
+    xf[7 * 32:8 * 32] = 1e-30                       # a block of tiny values
+    xf[9 * 32:10 * 32] = -2.0                       # equal values
+    xb = _bf16_bits(xf).reshape(1, K)
+    x = O.bf16_to_f32(xb)
+    want = O.tile_gemm_q4b32_f64(x, p, s, 1, K, N)[0]
+    slot, sb = q4_slot(p, s)
+    got = run(2, 1, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb,
+              route=_lib.ROUTE_GEMV).cpu().numpy()[0].astype(np.float64)
+    w = np.abs(O.dequant_q4b32(p, s, N, K).astype(np.float64))   # |q| * |s|
+    xa = np.abs(x[0].astype(np.float64))
+    blk_max = xa.reshape(-1, 32).max(axis=1)
+    quant = 2.0 ** -14 * (w.reshape(N, -1, 32).sum(axis=2) * blk_max).sum(axis=1)
+    slack = 1e-5 * (w * xa).sum(axis=1) + 1e-30
+    err = np.abs(got - want)
+    assert np.isfinite(got).all()
+    assert (err <= quant + slack).all(), f"worst excess {(err - quant - slack).max():.3e}"
+    assert _lib.device_error() == 0
+
+
+def test_gemv_m1_nonfinite_activation_is_reported(oracle_mod):
+    """An inf activation has no fixed-point image: device error 7, no fault, and the
+    context stays usable."""
+    O = oracle_mod
+    K, N = 1024, 256
+    p, s = O.gen_q4b32(N, K)
+    xb = O.gen_x_bf16(1, K)
+    slot, sb = q4_slot(p, s)
+    x = dev(xb).view(torch.bfloat16).clone()
+    x[0, 100] = float("inf")
+    run(2, 1, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert _lib.device_error() == 7
+    assert _lib.device_error() == 0   # read-and-clear
+    out = run(2, 1, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert_close(O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, 1, K, N), out.cpu().numpy())
 
 
 def test_gemv_bf16_output(oracle_mod):

@@ -409,7 +409,10 @@ def main():
                 prefill = {"value": round(tf, 2), "unit": "TFLOP/s", "workload": "C3 M=2048 K=N=4096 Q4B32, x bf16, bf16 out",
                            "ms_per_call": round(t, 5), "calls": reps,
                            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tc_peak, "unit": "TFLOP/s",
-                                        "frac": round(tf / tc_peak, 4), "peak_kind": peak_kind},
+                                        "frac": round(tf / tc_peak, 4), "peak_kind": peak_kind,
+                                        "traffic": profiled_traffic("tc_gemm_prefill_c3.md"),
+                                        "traffic_source": "ncu --set full, one gemm_kernel launch: "
+                                                          "profiles/tc_gemm_prefill_c3.md"},
                            "includes": "fp16 staging pass + tcgen05 GEMM (2 launches per call)",
                            "l2": f"inputs larger than L2: {n_sets} rotating (W, x, out) sets ({n_sets * per_set >> 20} MiB), "
                                  "back-to-back calls, CUDA events on the launching stream"}

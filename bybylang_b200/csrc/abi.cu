@@ -323,7 +323,12 @@ int bybycu_tile_gemm_host(int fmt, int M, int K, int N, const void* x_host, int 
         return rc;
     if (out_target == out_dev)
         BYBYCU_CUDA_TRY(cudaMemcpyAsync(out_host, out_dev, static_cast<size_t>(ob), cudaMemcpyDeviceToHost, s));
-    BYBYCU_CUDA_TRY(cudaStreamSynchronize(s));
+    // Poll rather than block: a blocking wait can add the host thread's wake-up latency to
+    // every step of a latency-bound decode loop.
+    cudaError_t q;
+    while ((q = cudaStreamQuery(s)) == cudaErrorNotReady) {
+    }
+    BYBYCU_CUDA_TRY(q);
     return BYBYCU_OK;
 }
 

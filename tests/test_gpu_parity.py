@@ -345,22 +345,31 @@ def test_parity_gates():
     assert gb.sessionTileGemmReady(be, False, True, fmt=2)
 
 
-def test_host_io_entry_point(oracle_mod):
+@pytest.mark.parametrize("M,K,N,x_pinned,out_pinned", [
+    (1, 4096, 11008, True, True),     # decode: x fetched by the upload kernel, result stored to host
+    (1, 4096, 11008, False, True),    # pageable x: the copy engine
+    (1, 8192, 1000, True, False),     # pageable output: out_dev and a copy back
+    (3, 512, 300, True, True),        # M > 1 through the upload kernel
+    (16, 4096, 256, True, True),      # 128 KB of x: the copy engine
+])
+def test_host_io_entry_point(M, K, N, x_pinned, out_pinned, oracle_mod):
     """bybycu_tile_gemm_host: host activations in, host output back (the e2e form)."""
     O = oracle_mod
-    M, K, N = 1, 4096, 11008
-    p, s = O.gen_q4b32(N, K)
-    xb = O.gen_x_bf16(M, K)
+    p, s = O.gen_q4b32(N, K, seed=M + K)
+    xb = O.gen_x_bf16(M, K, seed=N)
     slot, sb = q4_slot(p, s)
-    xh = torch.from_numpy(xb).pin_memory()
-    oh = torch.zeros(M, N, dtype=torch.float32).pin_memory()
-    xd = torch.empty(M, K, dtype=torch.bfloat16, device=DEV)
+    xh = torch.from_numpy(xb).pin_memory() if x_pinned else torch.from_numpy(xb.copy())
+    oh = torch.zeros(M, N, dtype=torch.float32)
+    if out_pinned:
+        oh = oh.pin_memory()
+    xd = torch.full((M, K), 7.0, dtype=torch.bfloat16, device=DEV)   # a sentinel
     od = torch.empty(M, N, dtype=torch.float32, device=DEV)
     rc = lib().bybycu_tile_gemm_host(2, M, K, N, C.c_void_p(xh.data_ptr()), _lib.DT_BF16, C.c_void_p(slot.data_ptr()),
                                      slot.numel(), sb, None, 0, 0, C.c_void_p(oh.data_ptr()), _lib.DT_F32,
                                      C.c_void_p(xd.data_ptr()), C.c_void_p(od.data_ptr()), _lib.ROUTE_AUTO, None)
     assert rc == 0, _lib.last_error()
     assert_close(O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, M, K, N, threads=8), oh.numpy())
+    assert torch.equal(xd.cpu(), xh.view(torch.bfloat16))   # x_dev holds the row either way
 
 
 # ----------------------------------------------------------------------------------------

@@ -421,7 +421,7 @@ def main():
 
     if rank == 0:
         base = None
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:   # the host-core baseline: rank 0 at N = 1 only
             base = cpu_baseline(1, 5.0)
             base.pop("seconds_per_step", None)
         clocks = sampler.summary()

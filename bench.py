@@ -14,6 +14,9 @@ fp32 out - through libbybycuda's GEMV route.  Algorithmic bytes per step: 25,362
 * cpu_baseline  the reference's own CPU C (oracle/_ref: OP_TILE_GEMM through
               nimf_cpu_vm_run_slots, single-threaded as the reference is) on the same shape.
 * prefill     config C3 (M=2048, K=N=4096) TFLOP/s when the tensor-core route is present.
+* q4_asym_decode  the asymmetric Q4 data of the reference's matmul_q4 (interleaved nibbles, fp32
+              scales and zero points per 32-block, fp32 x) at the C2 shape through
+              bybycu_matmul_q4's decode kernel: GB/s of its 0.75 B/weight, rotating sets > 4x L2.
 
 N > 1 GPUs (torchrun, one process per GPU): weak scaling.  Each rank owns an 11008-column
 shard of a [11008*N, 4096] Q4B32 projection and every step ends with the device-side
@@ -203,6 +206,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-q4asym", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -419,6 +423,57 @@ def main():
         except _lib.BybyCudaError as e:
             prefill = {"error": str(e)}
 
+    # ---- asymmetric Q4 decode (the matmul_q4 data: interleaved nibbles, fp32 scales and zero
+    # points per 32-block, fp32 x) at the C2 shape, through bybycu_matmul_q4's decode kernel
+    q4asym = None
+    if world == 1 and not args.no_q4asym:
+        try:
+            G = K_DEC // 32
+            wbytes = N_DEC * K_DEC // 2 + N_DEC * G * 8
+            abytes = wbytes + K_DEC * 4 + N_DEC * 4
+            n_sets = max(2, -(-4 * L2_BYTES // wbytes))
+            gen = torch.Generator(device=dev).manual_seed(SEED + 31)
+            qsets = []
+            for c in range(n_sets):
+                wq = torch.randint(0, 256, (N_DEC, K_DEC // 2), dtype=torch.uint8, device=dev, generator=gen)
+                sc = torch.rand(N_DEC, G, device=dev, generator=gen) * 0.02 + 1e-4
+                zp = torch.rand(N_DEC, G, device=dev, generator=gen) * 15
+                qsets.append((gb.Q4AsymWeights(wq, sc, zp, K_DEC), torch.empty(1, N_DEC, device=dev)))
+            xa = torch.randn(1, K_DEC, device=dev, generator=gen)
+            with torch.cuda.stream(stream):
+                for wqs, o in qsets:
+                    wqs.matmul(xa, o, route=_lib.ROUTE_GEMV, stream=stream)
+            stream.synchronize()
+            qgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(qgraph, stream=stream):
+                for wqs, o in qsets:
+                    wqs.matmul(xa, o, route=_lib.ROUTE_GEMV, stream=stream)
+            reps = max(20, min(reps_t, 4000 // n_sets))
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    qgraph.replay()
+            stream.synchronize()
+            qa, qb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            qa.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(reps):
+                    qgraph.replay()
+            qb.record(stream)
+            stream.synchronize()
+            assert _lib.device_error() == 0
+            t_us = qa.elapsed_time(qb) * 1e3 / (reps * n_sets)
+            gbs = abytes / (t_us * 1e-6) / 1e9
+            q4asym = {"value": round(gbs, 2), "unit": "GB/s", "us_per_launch": round(t_us, 3),
+                      "workload": "asymmetric Q4 decode M=1 K=4096 N=11008 (nibbles, fp32 scales + zero "
+                                  "points per 32-block, x fp32, out fp32)",
+                      "algorithmic_bytes": abytes, "launches": reps * n_sets,
+                      "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
+                                   "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind},
+                      "l2": f"inputs larger than L2: {n_sets} rotating weight sets, CUDA graph replay"}
+            del qgraph
+        except _lib.BybyCudaError as e:
+            q4asym = {"error": str(e)}
+
     if rank == 0:
         base = None
         if not args.no_cpu_baseline and world == 1:   # the host-core baseline: rank 0 at N = 1 only
@@ -442,6 +497,7 @@ def main():
                          "algorithmic_bytes": STEP_BYTES, "peak_kind": peak_kind},
             "cpu_baseline": base, "e2e": e2e, "gpu_launches": steps * launches_per_step, "clocks": clocks,
             "prefill": prefill,
+            "q4_asym_decode": q4asym,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

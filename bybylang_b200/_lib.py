@@ -68,6 +68,8 @@ SIGNATURES = {
     "bybycu_route_for": [_i32, _i32, _i32, _i32, _i32, C.POINTER(_i32)],
     "bybycu_vm_run_slots": [C.POINTER(_u32), _i32, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _i32,
                             _i32, _i32, _i32, C.c_char_p, _i32, _vp],
+    "bybycu_matmul_q4": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp],
+    "bybycu_session_matmul_q4": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32],
     "bybycu_session_begin": [],
     "bybycu_session_end": [],
     "bybycu_session_upload": [_vp, _i64, C.POINTER(_vp)],

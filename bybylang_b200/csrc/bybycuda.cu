@@ -3,6 +3,7 @@
 #include "abi.cu"
 #include "simt.cu"
 #include "gemv.cu"
+#include "q4asym.cu"
 #include "tc.cu"
 #include "vm.cu"
 #include "session.cu"

@@ -47,7 +47,7 @@ enum DeviceErr : uint32_t {
     kDevErrMmaWait = 4,     // tensor-core commit never arrived
     kDevErrPeerWait = 5,    // a peer rank's signal never arrived
     kDevErrTmemAlloc = 6,   // tensor memory allocation failed
-    kDevErrActRange = 7,    // an activation is outside the fp16 range of the tensor-core route
+    kDevErrActRange = 7,    // an activation has no image in the route's operand format (out of range, inf, NaN)
 };
 
 __device__ uint32_t g_device_error = 0;

@@ -71,6 +71,8 @@ struct GemvParams {
     int x_whole;                   // M = 1 integer mode: the activation row arrives once per launch,
     uint32_t xbar_off;             // one 1024-value chunk per barrier (then one "digits ready"
     uint32_t x_all_off;            // barrier per chunk), at x_all_off; block factors after it
+    int zeros;                     // asymmetric Q4: a zero-point box beside each scale box ...
+    uint32_t z_off;                // ... at this offset inside the stage
     const __half* scales;          // packed + scale_base
     const uint8_t* x;              // activations [M, K] (global)
     int x_elem;                    // 2 (bf16) or 4 (fp32)
@@ -101,6 +103,7 @@ __device__ __forceinline__ void gemv_gather_end(const PeerGather& pg, uint32_t c
 struct GemvMaps {
     CUtensorMap w[3];
     CUtensorMap s[3];
+    CUtensorMap z[3];   // asymmetric Q4 only: the fp32 zero points, boxed like the scales
 };
 
 // The nibbles in bits 0-3 and 16-19 of `a` as two bf16 values 128 + (nibble ^ 8) = 136 + q:
@@ -199,6 +202,7 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
         for (int i = 0; i < 3; ++i) {
             prefetch_tensormap(&maps.w[i]);
             if (p.scale_tma) prefetch_tensormap(&maps.s[i]);
+            if (p.zeros) prefetch_tensormap(&maps.z[i]);
         }
         const uint64_t policy = l2_policy_evict_first();
         // Issues the weight part of iteration (chunk, t0) into stage s and arms its barrier.
@@ -208,6 +212,7 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
             const int kn = min(p.kc, p.K - k0);
             const uint32_t rows = nt * kTileRows;
             const uint32_t bytes = wboxes * rows * 128 + (p.scale_tma ? rows * p.s_pitch : 0) +
+                                   (p.zeros ? rows * p.s_pitch : 0) +
                                    (p.x_whole ? 0u : p.M * static_cast<uint32_t>(kn) * p.x_elem);
             uint8_t* st = smem + static_cast<size_t>(s) * p.stage_bytes;
             mbar_arrive_expect_tx(&full_bar[s], bytes);
@@ -222,6 +227,8 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
                                      row, policy);
                 if (p.scale_tma)
                     tma_load_2d(st + p.s_off + q * kTileRows * p.s_pitch, &maps.s[mi], &full_bar[s], k0 / 32, row);
+                if (p.zeros)
+                    tma_load_2d(st + p.z_off + q * kTileRows * p.s_pitch, &maps.z[mi], &full_bar[s], k0 / 32, row);
             }
         };
         // Issues the activation rows of iteration `chunk` into stage s.

@@ -280,6 +280,26 @@ int bybycu_session_q4b32_gemm(const void* a, const void* w, void* c, int M, int 
     return session_gemm(BYBYCU_FMT_Q4B32, a, w, nullptr, c, M, K, N, tensor_core);
 }
 
+// sessionMatmulQ4 (gpubackend.nim:3000-3060): the asymmetric-Q4 matmul of resident weights
+// (uploaded with sessionUpload, residentUploadQ4's form) into the open session.
+int bybycu_session_matmul_q4(const void* a, const void* wq, const void* scales, const void* zeros, void* c, int M,
+                             int K, int N, int group_size, int n_groups_per_row) {
+    if (!t_sess.active) return set_error(BYBYCU_ERR_SESSION, "no open session");
+    const int64_t ab = handle_bytes(a), wb = handle_bytes(wq), sb = handle_bytes(scales), zb = handle_bytes(zeros),
+                  cb = handle_bytes(c);
+    if (ab < 0 || wb < 0 || sb < 0 || zb < 0 || cb < 0) return set_error(BYBYCU_ERR_ARGS, "unknown session handle");
+    if (M <= 0 || K <= 0 || N <= 0 || n_groups_per_row <= 0)
+        return set_error(BYBYCU_ERR_SHAPE, "unsupported matmul_q4 shape M=%d K=%d N=%d", M, K, N);
+    const int64_t params = static_cast<int64_t>(N) * n_groups_per_row * 4;
+    if (ab < static_cast<int64_t>(M) * K * 4 || wb < static_cast<int64_t>(N) * ((K + 1) / 2) || sb < params ||
+        zb < params || cb < static_cast<int64_t>(M) * N * 4)
+        return session_note(set_error(BYBYCU_ERR_RANGE, "matmul_q4: a slot is smaller than M=%d K=%d N=%d needs", M, K, N));
+    return session_note(bybycu_matmul_q4(static_cast<const float*>(a), static_cast<const uint8_t*>(wq),
+                                         static_cast<const float*>(scales), static_cast<const float*>(zeros),
+                                         static_cast<float*>(c), M, K, N, group_size, n_groups_per_row,
+                                         BYBYCU_ROUTE_AUTO, t_sess.streams[t_sess.device]));
+}
+
 int bybycu_tile_gemm_ready(int fmt, int tensor_core, int* ready) {
     if (!ready) return set_error(BYBYCU_ERR_ARGS, "ready is NULL");
     if (fmt < 0 || fmt > 2) return set_error(BYBYCU_ERR_SHAPE, "tile GEMM weight format %d is not supported", fmt);

@@ -340,6 +340,126 @@ class Q4B32Weights:
                          scale_base=self.scale_base, route=route, stream=stream)
 
 
+# --------------------------------------------------------------------------------------
+# Asymmetric Q4 (matmul_q4: gpubackend.nim:806-843, 2871-3060; cpu_kernels_impl.inc:293-319)
+# --------------------------------------------------------------------------------------
+
+@dataclass
+class ResidentWeightHandle:
+    """gpubackend.nim's ResidentWeightHandle for the CUDA backend: the packed nibbles
+    [N, (K+1)/2] (even k in the low nibble) and the fp32 scales and zero points
+    [N, nGroupsPerRow], uploaded once as three session handles."""
+    kind: GpuBackend = GpuBackend.gbCuda
+    wq: SessionHandle = field(default_factory=SessionHandle)
+    scales: SessionHandle = field(default_factory=SessionHandle)
+    zeros: SessionHandle = field(default_factory=SessionHandle)
+    k: int = 0
+    n: int = 0
+    groupSize: int = 0
+    nGroupsPerRow: int = 0
+
+
+def _q4_shape_check(n_wq: int, n_scales: int, n_zeros: int, k: int, n: int, groupSize: int,
+                    nGroupsPerRow: int) -> None:
+    need = (k + groupSize - 1) // groupSize if groupSize > 0 else 1
+    if k <= 0 or n <= 0 or nGroupsPerRow < need:
+        raise BybyCudaError(_lib.ERR_SHAPE, f"unsupported matmul_q4 shape K={k} N={n} groups={nGroupsPerRow}")
+    if n_wq < n * ((k + 1) // 2) or n_scales < n * nGroupsPerRow or n_zeros < n * nGroupsPerRow:
+        raise BybyCudaError(_lib.ERR_RANGE, "matmul_q4: a weight slot is smaller than the shape needs")
+
+
+def _q4_check(wq, scales, zeros, k: int, n: int, groupSize: int, nGroupsPerRow: int):
+    wq = np.ascontiguousarray(wq, np.uint8).reshape(-1)
+    scales = np.ascontiguousarray(scales, np.float32).reshape(-1)
+    zeros = np.ascontiguousarray(zeros, np.float32).reshape(-1)
+    _q4_shape_check(wq.size, scales.size, zeros.size, k, n, groupSize, nGroupsPerRow)
+    return wq, scales, zeros
+
+
+def residentUploadQ4(backend: GpuBackend, wq, scales, zeros, k: int, n: int, groupSize: int,
+                     nGroupsPerRow: int) -> ResidentWeightHandle:
+    """gpubackend.nim:2883-2919: the weights on the device once, at model load."""
+    _chosen(backend)
+    if not _initialised:
+        ensureGpuInit(backend)
+    wq, scales, zeros = _q4_check(wq, scales, zeros, k, n, groupSize, nGroupsPerRow)
+    return ResidentWeightHandle(GpuBackend.gbCuda, sessionUpload(backend, wq), sessionUpload(backend, scales),
+                                sessionUpload(backend, zeros), k, n, groupSize, nGroupsPerRow)
+
+
+def residentPrepareQ4(w: ResidentWeightHandle, M: int = 1) -> bool:
+    """gpubackend.nim:2871: ready for M rows.  The CUDA kernels read the uploaded layout as it
+    is, so there is nothing to prepare."""
+    return w.kind == GpuBackend.gbCuda and w.wq.ptr != 0 and M > 0
+
+
+def residentFreeQ4(backend: GpuBackend, w: ResidentWeightHandle) -> None:
+    for h in (w.wq, w.scales, w.zeros):
+        if h.ptr:
+            sessionFree(backend, h)
+
+
+def sessionMatmulQ4(backend: GpuBackend, a: SessionHandle, w: ResidentWeightHandle, c: SessionHandle,
+                    M: int) -> bool:
+    """gpubackend.nim:3000-3060: C(M x N) = A(M x K) @ W into the open session; an empty c
+    gets a scratch buffer first (the reference's own fix for an unallocated output)."""
+    if not c.ptr:
+        c.cudaHandle = sessionAllocScratch(backend, M * w.n).cudaHandle
+    return _gemm("bybycu_session_matmul_q4", backend,
+                 (C.c_void_p(a.ptr), C.c_void_p(w.wq.ptr), C.c_void_p(w.scales.ptr), C.c_void_p(w.zeros.ptr),
+                  C.c_void_p(c.ptr), M, w.k, w.n, w.groupSize, w.nGroupsPerRow), c, M, w.n)
+
+
+def gpuMatmulQ4(backend: GpuBackend, a, wq, scales, zeros, m: int, k: int, n: int, groupSize: int,
+                nGroupsPerRow: int) -> np.ndarray:
+    """gpubackend.nim:806-843, immediate mode: host arrays in, the [m, n] fp32 product back."""
+    import torch
+    _chosen(backend)
+    if not _initialised:
+        ensureGpuInit(backend)
+    wq, scales, zeros = _q4_check(wq, scales, zeros, k, n, groupSize, nGroupsPerRow)
+    a = np.ascontiguousarray(a, np.float32).reshape(-1)
+    if m <= 0 or a.size < m * k:
+        raise BybyCudaError(_lib.ERR_RANGE, "matmul_q4: a is smaller than m * k")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    t = [torch.from_numpy(v).to(dev) for v in (a[:m * k], wq, scales, zeros)]
+    out = torch.empty(m, n, dtype=torch.float32, device=dev)
+    try:
+        call("bybycu_matmul_q4", *[_ptr(v) for v in t], _ptr(out), m, k, n, groupSize, nGroupsPerRow,
+             _lib.ROUTE_AUTO, _stream_ptr(None))
+    except BybyCudaError as e:
+        handleGpuFailure(backend, "matmul_q4", e)
+    return out.cpu().numpy()
+
+
+class Q4AsymWeights:
+    """Asymmetric Q4 weights resident on one device, for torch callers: nibbles [N, (K+1)/2]
+    (even k low), fp32 scales and zero points [N, groups] of ``group_size`` values."""
+
+    def __init__(self, wq, scales, zeros, K: int, group_size: int = 32, device=None):
+        import torch
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.wq = torch.as_tensor(wq).to(dev, torch.uint8).contiguous()
+        self.scales = torch.as_tensor(scales).to(dev, torch.float32).contiguous()
+        self.zeros = torch.as_tensor(zeros).to(dev, torch.float32).contiguous()
+        self.N = self.wq.shape[0]
+        self.K = K
+        self.group_size = group_size
+        self.n_groups = self.scales.shape[-1] if self.scales.dim() == 2 else self.scales.numel() // self.N
+        _q4_shape_check(self.wq.numel(), self.scales.numel(), self.zeros.numel(), K, self.N, group_size,
+                        self.n_groups)
+
+    def matmul(self, x, out=None, *, route: int = _lib.ROUTE_AUTO, stream=None):
+        """out[M, N] = x[M, K] . W^T, x fp32 on the device."""
+        import torch
+        M = x.shape[0]
+        if out is None:
+            out = torch.empty(M, self.N, dtype=torch.float32, device=x.device)
+        call("bybycu_matmul_q4", _ptr(x), _ptr(self.wq), _ptr(self.scales), _ptr(self.zeros), _ptr(out), M, self.K,
+             self.N, self.group_size, self.n_groups, int(route), _stream_ptr(stream))
+        return out
+
+
 __all__ = [
     "GpuBackend", "parseBackend", "normalizeBackend", "detectBackend", "ensureGpuInit",
     "setForbidCpuFallback", "gForbidCpuFallback", "handleGpuFailure", "SessionHandle",
@@ -347,4 +467,6 @@ __all__ = [
     "sessionRead", "sessionFree", "sessionFp4GemmTensorCore", "sessionFp4GemmTiledEnc",
     "sessionF16GemmTile", "sessionQ4B32Gemm", "sessionTileGemmReady", "sessionMicroVmEnc",
     "tile_gemm", "route_for", "dequant", "Q4B32Weights", "tileWeightBytes", "TileFormatQ4B32",
+    "ResidentWeightHandle", "residentUploadQ4", "residentPrepareQ4", "residentFreeQ4", "sessionMatmulQ4",
+    "gpuMatmulQ4", "Q4AsymWeights",
 ]

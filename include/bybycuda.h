@@ -163,6 +163,29 @@ BYBYCU_API int bybycu_dequant(int fmt, int K, int N, const void* packed, int64_t
 /* The route AUTO takes for a shape, after the same checks as bybycu_tile_gemm. */
 BYBYCU_API int bybycu_route_for(int fmt, int M, int K, int N, int x_dtype, int* route);
 
+/* Asymmetric Q4, the reference's matmul_q4 (gpuMatmulQ4 / sessionMatmulQ4,
+ * gpubackend.nim:806-843,3000-3060; nimf_cpu_matmul_q4, cpu_kernels_impl.inc:293-319):
+ *     c[M, N] = a[M, K] . W^T,  W[n, k] = (u[n, k] - zeros[n, g]) * scales[n, g],
+ * u the unsigned nibble k of wq[n, (K+1)/2] (even k in the low nibble), g = k / group_size
+ * (one group when group_size <= 0).  Every slot is a DEVICE pointer: fp32 a, fp32 scales and
+ * zeros [N, n_groups_per_row], fp32 c.
+ *   route  AUTO: the decode kernel when it applies (M = 1, group 32, K % 128 == 0, 16-byte
+ *          aligned slots: s8 tensor-core MMAs on the raw nibbles, activations in two-digit
+ *          fixed point per 32-block), SIMT otherwise; SIMT: one thread per output, fmaf in k
+ *          order (the CPU VM's OP_Q4_GEMV arithmetic); GEMV: the decode kernel, or
+ *          BYBYCU_ERR_SHAPE when it does not apply.
+ * Asynchronous on `stream`. */
+BYBYCU_API int bybycu_matmul_q4(const float* a, const uint8_t* wq, const float* scales, const float* zeros,
+                                float* c, int M, int K, int N, int group_size, int n_groups_per_row,
+                                int route, void* stream);
+
+/* sessionMatmulQ4 (gpubackend.nim:3000-3060): bybycu_matmul_q4 (route AUTO) into the open
+ * session, on its stream.  a, wq, scales, zeros and c are session handles (sessionUpload /
+ * sessionAllocScratch: residentUploadQ4 keeps the weights as three of them); each must hold
+ * what the shape needs. */
+BYBYCU_API int bybycu_session_matmul_q4(const void* a, const void* wq, const void* scales, const void* zeros,
+                                        void* c, int M, int K, int N, int group_size, int n_groups_per_row);
+
 /* Device-pointer twin of nimf_cpu_vm_run_slots (backends/cpu/cpu_kernels.h:118-121,
  * cpu_vm.c:178-182): runs a micro-VM program whose first op is OP_TILE_GEMM (formats
  * 0/1/2, followed by the canonical tile ops), OP_FP4_COOP_GEMM, OP_Q4_GEMV or

@@ -1,0 +1,191 @@
+"""Asymmetric Q4 (matmul_q4) on the GPU against the reference's own CPU kernel.
+
+The reference: nimf_cpu_matmul_q4 (backends/cpu/cpu_kernels_impl.inc:293-319), built unchanged
+into oracle/_ref, and its restatement in the oracle port.  Data: interleaved nibbles
+[N, (K+1)/2] (even k in the low nibble), fp32 scales and zero points [N, groups].
+
+Tolerances (written here):
+* decode kernel (route AUTO at M = 1, group 32): the reference test's max|diff| <= 1e-4 *
+  max(1, max|ref|), and per element its fixed-point bound against float64,
+  |diff| <= 2^-14 * sum_b max|x_b| * sum_{k in b} |w[n, k]| plus fp32 slack, on inputs of any
+  dynamic range.  (fp32 activations are rounded to 15-bit fixed point per 32-block, so the
+  1e-3 per-element bound of the bf16 decode path does not hold near zero outputs.)
+* exact kernel (route SIMT, and AUTO for every other shape): the same bounds against the
+  reference (its k-order fmaf differs from nimf_cpu_matmul_q4's evaluation order only by
+  fp32 rounding).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from bybylang_b200 import _lib  # noqa: E402
+from bybylang_b200 import gpubackend as gb  # noqa: E402
+
+from gpu_helpers import DEV, assert_close  # noqa: E402
+
+PEAK_TOL, ELEM_TOL = 1e-4, 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    gb.ensureGpuInit(gb.GpuBackend.gbCuda, 0)
+    yield
+    assert _lib.device_error() == 0
+
+
+def gen_q4(M, K, N, group=32, seed=0, integer_zeros=False):
+    rng = np.random.default_rng(seed)
+    groups = (K + group - 1) // group
+    wq = rng.integers(0, 256, size=(N, (K + 1) // 2), dtype=np.uint8)
+    scales = np.abs(rng.normal(0, 0.02, size=(N, groups))).astype(np.float32) + np.float32(1e-4)
+    zeros = (np.full((N, groups), 8.0, np.float32) if integer_zeros
+             else rng.uniform(0, 15, size=(N, groups)).astype(np.float32))
+    a = rng.normal(0, 1, size=(M, K)).astype(np.float32)
+    return a, wq, scales, zeros
+
+
+def run_q4(a, wq, scales, zeros, M, K, N, group, route=_lib.ROUTE_AUTO, n_groups=None):
+    n_groups = n_groups if n_groups is not None else scales.shape[1]
+    t = [torch.from_numpy(np.ascontiguousarray(v)).to(DEV) for v in (a, wq, scales, zeros)]
+    out = torch.full((M, N), float("nan"), dtype=torch.float32, device=DEV)
+    _lib.check(_lib.load().bybycu_matmul_q4(*[C.c_void_p(v.data_ptr()) for v in t], C.c_void_p(out.data_ptr()),
+                                            M, K, N, group, n_groups, route, None))
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def dequant_np(wq, scales, zeros, K, group):
+    """(u - z) * s per element, in float64."""
+    N = wq.shape[0]
+    u = np.empty((N, (K + 1) // 2 * 2), np.float64)
+    u[:, 0::2] = wq & 15
+    u[:, 1::2] = wq >> 4
+    u = u[:, :K]
+    g = np.arange(K) // group
+    return (u - zeros[:, g].astype(np.float64)) * scales[:, g].astype(np.float64)
+
+
+def assert_fixed_point_bound(x, wq, scales, zeros, K, got):
+    """Per element against float64: |diff| <= 2^-14 sum_b max|x_b| sum_{k in b} |w| + slack."""
+    N = wq.shape[0]
+    w = dequant_np(wq, scales, zeros, K, 32)
+    xd = x.astype(np.float64)
+    want = w @ xd
+    blk_max = np.abs(xd).reshape(-1, 32).max(axis=1)
+    quant = 2.0 ** -14 * (np.abs(w).reshape(N, -1, 32).sum(axis=2) * blk_max).sum(axis=1)
+    slack = 1e-5 * (np.abs(w) * np.abs(xd)).sum(axis=1) + 1e-30
+    err = np.abs(np.asarray(got, np.float64) - want)
+    assert np.isfinite(got).all()
+    assert (err <= quant + slack).all(), f"worst excess {(err - quant - slack).max():.3e}"
+
+
+@pytest.mark.parametrize("K,N", [(4096, 11008), (4096, 4096), (11008, 4096), (128, 1), (1152, 17), (2048, 300)])
+def test_decode_kernel_against_reference(K, N, oracle_mod):
+    O = oracle_mod
+    a, wq, scales, zeros = gen_q4(1, K, N, seed=K + N)
+    want = O.ref_matmul_q4(a, wq, scales, zeros, 1, K, N, 32, threads=8)
+    got = run_q4(a, wq, scales, zeros, 1, K, N, 32, route=_lib.ROUTE_GEMV)
+    assert_close(want, got, PEAK_TOL, None, f"K={K} N={N}")
+    assert_close(O.matmul_q4_asym(a, wq, scales, zeros, 1, K, N, 32), got, PEAK_TOL, None, "port")
+    assert_fixed_point_bound(a[0], wq, scales, zeros, K, got[0])
+
+
+def test_decode_kernel_integer_zero_points(oracle_mod):
+    O = oracle_mod
+    K, N = 4096, 2048
+    a, wq, scales, zeros = gen_q4(1, K, N, seed=3, integer_zeros=True)
+    got = run_q4(a, wq, scales, zeros, 1, K, N, 32)
+    assert_close(O.ref_matmul_q4(a, wq, scales, zeros, 1, K, N, 32, threads=8), got, PEAK_TOL, None)
+    assert_fixed_point_bound(a[0], wq, scales, zeros, K, got[0])
+
+
+def test_decode_kernel_dynamic_range():
+    """fp32 activations over 48 binades, zeros, a lone outlier, tiny blocks: inside the
+    fixed-point bound against float64."""
+    K, N = 4096, 1024
+    a, wq, scales, zeros = gen_q4(1, K, N, seed=11)
+    rng = np.random.default_rng(12)
+    x = (rng.choice([-1.0, 1.0], K) * np.exp2(rng.uniform(-30, 18, K))).astype(np.float32)
+    x[rng.random(K) < 0.1] = 0.0
+    x[64:96] = 0.0
+    x[160:192] = 1e-7
+    x[170] = 5e4
+    x[224:256] = 1e-35
+    a[0] = x
+    assert_fixed_point_bound(x, wq, scales, zeros, K, run_q4(a, wq, scales, zeros, 1, K, N, 32)[0])
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("M,K,N,group", [(3, 512, 300, 32), (1, 512, 100, 64), (16, 256, 40, 32), (1, 96, 7, 32)])
+def test_exact_kernel_shapes(M, K, N, group, oracle_mod):
+    """Shapes outside the decode kernel (M > 1, group 64, K % 128 != 0) take the exact kernel."""
+    O = oracle_mod
+    a, wq, scales, zeros = gen_q4(M, K, N, group=group, seed=M * K + N)
+    got = run_q4(a, wq, scales, zeros, M, K, N, group)
+    assert_close(O.ref_matmul_q4(a, wq, scales, zeros, M, K, N, group), got, PEAK_TOL, ELEM_TOL)
+
+
+def test_exact_kernel_odd_k_and_one_group():
+    """K odd (the last byte's high nibble unused) and group_size <= 0 (one group per row)."""
+    M, K, N = 2, 33, 9
+    a, wq, scales, zeros = gen_q4(M, K, N, group=32, seed=5)
+    want = a.astype(np.float64) @ dequant_np(wq, scales, zeros, K, 32).T
+    assert_close(want, run_q4(a, wq, scales, zeros, M, K, N, 32), PEAK_TOL, ELEM_TOL, "odd K")
+    s1, z1 = scales[:, :1].copy(), zeros[:, :1].copy()
+    want = a.astype(np.float64) @ dequant_np(wq, s1, z1, K, K + 1).T
+    assert_close(want, run_q4(a, wq, s1, z1, M, K, N, 0, n_groups=1), PEAK_TOL, ELEM_TOL, "group 0")
+
+
+def test_routes_and_errors(oracle_mod):
+    K, N = 1024, 64
+    a, wq, scales, zeros = gen_q4(1, K, N, seed=9)
+    fast = run_q4(a, wq, scales, zeros, 1, K, N, 32, route=_lib.ROUTE_GEMV)
+    exact = run_q4(a, wq, scales, zeros, 1, K, N, 32, route=_lib.ROUTE_SIMT)
+    assert_close(oracle_mod.ref_matmul_q4(a, wq, scales, zeros, 1, K, N, 32), exact, PEAK_TOL, ELEM_TOL, "exact")
+    assert_close(exact, fast, PEAK_TOL, None)
+    assert_fixed_point_bound(a[0], wq, scales, zeros, K, fast[0])
+    with pytest.raises(_lib.BybyCudaError):   # the decode route refuses M > 1
+        run_q4(np.vstack([a, a]), wq, scales, zeros, 2, K, N, 32, route=_lib.ROUTE_GEMV)
+    with pytest.raises(_lib.BybyCudaError):   # too few groups per row
+        run_q4(a, wq, scales, zeros, 1, K, N, 32, n_groups=8)
+
+
+def test_nonfinite_activation_is_reported():
+    K, N = 1024, 128
+    a, wq, scales, zeros = gen_q4(1, K, N, seed=13)
+    a[0, 77] = np.inf
+    run_q4(a, wq, scales, zeros, 1, K, N, 32)
+    assert _lib.device_error() == 7
+    assert _lib.device_error() == 0
+
+
+def test_session_resident_api_like_reference(oracle_mod):
+    """residentUploadQ4 + sessionMatmulQ4 inside a session, and gpuMatmulQ4 (immediate)."""
+    O = oracle_mod
+    be = gb.GpuBackend.gbCuda
+    M, K, N = 1, 2048, 512
+    a, wq, scales, zeros = gen_q4(M, K, N, seed=21)
+    want = O.ref_matmul_q4(a, wq, scales, zeros, M, K, N, 32)
+    w = gb.residentUploadQ4(be, wq, scales, zeros, K, N, 32, K // 32)
+    assert gb.residentPrepareQ4(w, M)
+    assert gb.sessionBegin(be)
+    ha = gb.sessionUpload(be, a)
+    hc = gb.SessionHandle()
+    assert gb.sessionMatmulQ4(be, ha, w, hc, M)
+    assert gb.sessionEnd(be)
+    assert_close(want, gb.sessionRead(be, hc, M * N).reshape(M, N), PEAK_TOL, None)
+    for h in (ha, hc):
+        gb.sessionFree(be, h)
+    gb.residentFreeQ4(be, w)
+    got = gb.gpuMatmulQ4(be, a, wq, scales, zeros, M, K, N, 32, K // 32)
+    assert_close(want, got, PEAK_TOL, None)
+    assert_fixed_point_bound(a[0], wq, scales, zeros, K, got[0])
+    W = gb.Q4AsymWeights(wq, scales, zeros, K)
+    out = W.matmul(torch.from_numpy(a).to(DEV))
+    torch.cuda.synchronize()
+    assert_close(want, out.cpu().numpy(), PEAK_TOL, None)

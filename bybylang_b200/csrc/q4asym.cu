@@ -23,7 +23,12 @@
 namespace bybycu {
 namespace {
 
-constexpr int kQ4aTP = 4;   // tiles of 16 rows per pass: two stages fit twice per SM
+// Tiles of 16 rows per pass, and the ring depth: one CTA per SM with three 64 KB stages.  Two
+// co-resident CTAs (4-tile passes, two stages each) measured 30% slower at the C2 shape: CTAs
+// with 5 tiles then need a second pass, while three stages keep enough of the 0.75 B/weight
+// stream in flight for one CTA.
+constexpr int kQ4aTP = 5;
+constexpr int kQ4aStages = 3;
 
 __global__ void __launch_bounds__(128) q4a_exact_kernel(int M, int K, int N, int group, int n_groups,
                                                         const uint8_t* __restrict__ wq,
@@ -235,8 +240,10 @@ int launch_q4a(int M, int K, int N, int group, int n_groups, const float* x, con
     const uint32_t z_off = s_off + rows * 128;      // 32 fp32 scales per row, then 32 zero points
     const uint32_t x_off = z_off + rows * 128;
     const uint32_t stage_bytes = (x_off + kM1KC * 4 + 1023) / 1024 * 1024;
-    const int stages = 2;
     const size_t red_bytes = static_cast<size_t>(kM1Warps) * kQ4aTP * 16 * sizeof(float);
+    const size_t budget = static_cast<size_t>(dev.max_smem_optin) - 1024 - 64 - red_bytes;
+    const int stages = std::min(kQ4aStages, static_cast<int>(budget / (stage_bytes + 16)));
+    if (stages < 2) return set_error(BYBYCU_ERR_SHAPE, "matmul_q4 decode: shared memory too small");
     const size_t smem = 1024 + static_cast<size_t>(stages) * (stage_bytes + 16) + 16 + red_bytes;
 
     GemvParams p{};

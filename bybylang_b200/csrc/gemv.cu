@@ -1150,11 +1150,13 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
         }
     }
     if (!kc) return set_error(BYBYCU_ERR_SHAPE, "GEMV: shared memory too small for M=%d", a.M);
-    // Ring depth.  The M = 1 kernel keeps two chunks in flight: all chunks requested at once
-    // complete together (the first one late), two let compute start on the first chunk early
-    // while the second streams.  BYBY_CUDA_GEMV_STAGES overrides (tuning).
+    // Ring depth of the M = 1 kernel.  One pass per CTA: two stages, so that two CTAs share an
+    // SM and the next launch's CTA streams its first stages while this one computes (C2: 6.4 us
+    // against 7.1 with three stages).  Several passes: three stages and one CTA per SM, whose
+    // deeper ring keeps the long stream in flight (1 x 32000 x 4096: 16.1 us against 17.9).
+    // BYBY_CUDA_GEMV_STAGES overrides (tuning).
     const int fit = stages;   // the most that fit in shared memory (and are useful)
-    if (m1) stages = std::min(fit, 2);
+    if (m1) stages = std::min(fit, tiles_max > tp ? 3 : 2);
     if (const char* e = getenv("BYBY_CUDA_GEMV_STAGES")) {
         const int want_stages = atoi(e);
         if (want_stages >= 1) stages = std::min(fit, want_stages);

@@ -70,6 +70,10 @@ SIGNATURES = {
                             _i32, _i32, _i32, C.c_char_p, _i32, _vp],
     "bybycu_matmul_q4": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp],
     "bybycu_session_matmul_q4": [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32],
+    "bybycu_matmul_q4_fused": [_i32, _vp, _i32, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_i32),
+                               C.POINTER(_vp), _vp, _vp, C.c_float, _i32, _i32, _i32, _vp],
+    "bybycu_session_matmul_q4_fused": [_i32, _vp, _i32, C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp),
+                                       C.POINTER(_i32), C.POINTER(_vp), _vp, _vp, C.c_float, _i32, _i32, _i32],
     "bybycu_session_begin": [],
     "bybycu_session_end": [],
     "bybycu_session_upload": [_vp, _i64, C.POINTER(_vp)],

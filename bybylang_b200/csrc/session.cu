@@ -300,6 +300,40 @@ int bybycu_session_matmul_q4(const void* a, const void* wq, const void* scales, 
                                          BYBYCU_ROUTE_AUTO, t_sess.streams[t_sess.device]));
 }
 
+// sessionMatmulQ4Fused (gpubackend.nim:3185-3231): the fused decode GEMV of resident
+// asymmetric-Q4 weights into the open session.  BYBYCU_ERR_SHAPE (not recorded as a session
+// error) means "unsupported here": the caller runs the unfused sequence, as the reference does.
+int bybycu_session_matmul_q4_fused(int mode, const void* a, int n_mats, const void* const* wq,
+                                   const void* const* scales, const void* const* zeros, const int* N,
+                                   void* const* outs, const void* res, const void* gamma, float eps, int K,
+                                   int group_size, int n_groups_per_row) {
+    if (!t_sess.active) return set_error(BYBYCU_ERR_SESSION, "no open session");
+    if (!a || !wq || !scales || !zeros || !N || !outs || n_mats < 1 || n_mats > 3 || K <= 0 || n_groups_per_row <= 0)
+        return set_error(BYBYCU_ERR_ARGS, "sessionMatmulQ4Fused: bad arguments");
+    auto fits = [](const void* h, int64_t need) { const int64_t b = handle_bytes(h); return b >= need; };
+    if (!fits(a, static_cast<int64_t>(K) * 4) || (res && !fits(res, static_cast<int64_t>(N[0]) * 4)) ||
+        (gamma && !fits(gamma, static_cast<int64_t>(K) * 4)))
+        return set_error(BYBYCU_ERR_RANGE, "sessionMatmulQ4Fused: a, res or gamma is not a large enough session handle");
+    const uint8_t* w8[3] = {};
+    const float* sc[3] = {};
+    const float* zr[3] = {};
+    float* out[3] = {};
+    for (int m = 0; m < n_mats; ++m) {
+        const int64_t params = static_cast<int64_t>(N[m]) * n_groups_per_row * 4;
+        if (N[m] <= 0 || !fits(wq[m], static_cast<int64_t>(N[m]) * ((K + 1) / 2)) || !fits(scales[m], params) ||
+            !fits(zeros[m], params) || !fits(outs[m], static_cast<int64_t>(N[m]) * 4))
+            return set_error(BYBYCU_ERR_RANGE, "sessionMatmulQ4Fused: matrix %d's handles are too small", m);
+        w8[m] = static_cast<const uint8_t*>(wq[m]);
+        sc[m] = static_cast<const float*>(scales[m]);
+        zr[m] = static_cast<const float*>(zeros[m]);
+        out[m] = static_cast<float*>(outs[m]);
+    }
+    const int rc = bybycu_matmul_q4_fused(mode, static_cast<const float*>(a), n_mats, w8, sc, zr, N, out,
+                                          static_cast<const float*>(res), static_cast<const float*>(gamma), eps, K,
+                                          group_size, n_groups_per_row, t_sess.streams[t_sess.device]);
+    return rc == BYBYCU_ERR_SHAPE ? rc : session_note(rc);
+}
+
 int bybycu_tile_gemm_ready(int fmt, int tensor_core, int* ready) {
     if (!ready) return set_error(BYBYCU_ERR_ARGS, "ready is NULL");
     if (fmt < 0 || fmt > 2) return set_error(BYBYCU_ERR_SHAPE, "tile GEMM weight format %d is not supported", fmt);

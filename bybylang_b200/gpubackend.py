@@ -432,6 +432,51 @@ def gpuMatmulQ4(backend: GpuBackend, a, wq, scales, zeros, m: int, k: int, n: in
     return out.cpu().numpy()
 
 
+def sessionMatmulQ4Fused(backend: GpuBackend, mode: int, a: SessionHandle, ws, outs, res: SessionHandle,
+                         hasRes: bool, gamma: SessionHandle | None = None, eps: float = 0.0,
+                         hasNorm: bool = False) -> bool:
+    """gpubackend.nim:3185-3231: the fused decode GEMV (M = 1) in one launch.  mode 0: 1-3
+    matrices share `a`, each into its own outs[i]; mode 1: ws = [gate, up] and outs[0] =
+    silu(gate) * up.  hasRes adds `res`; hasNorm RMS-normalises `a` with `gamma` and `eps`.
+    False when unsupported (the caller runs the unfused sequence); outputs must be allocated."""
+    _chosen(backend)
+    ws, outs = list(ws), list(outs)
+    if not 1 <= len(ws) <= 3 or len(outs) < len(ws) or (mode == 1 and len(ws) != 2):
+        return False
+    if (hasRes and not res.ptr) or (hasNorm and (gamma is None or not gamma.ptr)):
+        return False
+    w0 = ws[0]
+    for i, w in enumerate(ws):
+        if w.kind != GpuBackend.gbCuda or not outs[i].ptr:
+            return False
+        if w.k != w0.k or w.groupSize != w0.groupSize or w.nGroupsPerRow != w0.nGroupsPerRow:
+            return False
+    n = len(ws)
+    vp3 = C.c_void_p * n
+    rc = _lib.load().bybycu_session_matmul_q4_fused(
+        int(mode), C.c_void_p(a.ptr), n, vp3(*[w.wq.ptr for w in ws]), vp3(*[w.scales.ptr for w in ws]),
+        vp3(*[w.zeros.ptr for w in ws]), (C.c_int * n)(*[w.n for w in ws]), vp3(*[o.ptr for o in outs[:n]]),
+        C.c_void_p(res.ptr if hasRes else 0), C.c_void_p(gamma.ptr if hasNorm else 0), C.c_float(eps), w0.k,
+        w0.groupSize, w0.nGroupsPerRow)
+    if rc == _lib.ERR_SHAPE:
+        return False
+    if rc != 0:
+        handleGpuFailure(backend, "matmul_q4_fused", BybyCudaError(rc, _lib.last_error()[1]))
+    return True
+
+
+def matmul_q4_fused(mode: int, x, weights, outs, *, res=None, gamma=None, eps: float = 0.0, stream=None):
+    """The fused decode GEMV on torch tensors: x fp32 [1, K] (raw when gamma is given),
+    weights a list of Q4AsymWeights, outs fp32 [1, N] tensors; raises when unsupported."""
+    n = len(weights)
+    vp = C.c_void_p * n
+    call("bybycu_matmul_q4_fused", int(mode), _ptr(x), n, vp(*[w.wq.data_ptr() for w in weights]),
+         vp(*[w.scales.data_ptr() for w in weights]), vp(*[w.zeros.data_ptr() for w in weights]),
+         (C.c_int * n)(*[w.N for w in weights]), vp(*[o.data_ptr() for o in outs[:n]]), _ptr(res), _ptr(gamma),
+         C.c_float(eps), weights[0].K, weights[0].group_size, weights[0].n_groups, _stream_ptr(stream))
+    return outs
+
+
 class Q4AsymWeights:
     """Asymmetric Q4 weights resident on one device, for torch callers: nibbles [N, (K+1)/2]
     (even k low), fp32 scales and zero points [N, groups] of ``group_size`` values."""
@@ -468,5 +513,5 @@ __all__ = [
     "sessionF16GemmTile", "sessionQ4B32Gemm", "sessionTileGemmReady", "sessionMicroVmEnc",
     "tile_gemm", "route_for", "dequant", "Q4B32Weights", "tileWeightBytes", "TileFormatQ4B32",
     "ResidentWeightHandle", "residentUploadQ4", "residentPrepareQ4", "residentFreeQ4", "sessionMatmulQ4",
-    "gpuMatmulQ4", "Q4AsymWeights",
+    "gpuMatmulQ4", "Q4AsymWeights", "sessionMatmulQ4Fused", "matmul_q4_fused",
 ]

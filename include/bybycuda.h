@@ -186,6 +186,27 @@ BYBYCU_API int bybycu_matmul_q4(const float* a, const uint8_t* wq, const float* 
 BYBYCU_API int bybycu_session_matmul_q4(const void* a, const void* wq, const void* scales, const void* zeros,
                                         void* c, int M, int K, int N, int group_size, int n_groups_per_row);
 
+/* The fused decode GEMV of asymmetric-Q4 weights (sessionMatmulQ4Fused, gpubackend.nim:3185-3231;
+ * its shader q4_autotune.nim:194-325), one launch, M = 1:
+ *   mode 0: n_mats (1..3) matrices share `a`; outs[m][0 .. N[m]) = a . W_m^T;
+ *   mode 1: n_mats = 2 (gate, up; N[0] == N[1]); outs[0] = silu(a . Wg^T) * (a . Wu^T).
+ * With gamma != NULL, a is the raw vector and the product uses RMSNorm(a) = a * gamma /
+ * sqrt(mean(a^2) + eps); with res != NULL, res[0 .. N) is added to every output row.  wq, scales,
+ * zeros, outs are HOST arrays of n_mats DEVICE pointers; a, res, gamma are device pointers.  The
+ * decode kernel of bybycu_matmul_q4 (group 32, K % 128 == 0, 16-byte aligned slots); any other
+ * shape returns BYBYCU_ERR_SHAPE, for the caller to run the unfused sequence. */
+BYBYCU_API int bybycu_matmul_q4_fused(int mode, const float* a, int n_mats, const uint8_t* const* wq,
+                                      const float* const* scales, const float* const* zeros, const int* N,
+                                      float* const* outs, const float* res, const float* gamma, float eps,
+                                      int K, int group_size, int n_groups_per_row, void* stream);
+
+/* The same into the open session: every pointer is a session handle (wq / scales / zeros of
+ * residentUploadQ4); BYBYCU_ERR_SHAPE means unsupported and does not fail the session. */
+BYBYCU_API int bybycu_session_matmul_q4_fused(int mode, const void* a, int n_mats, const void* const* wq,
+                                              const void* const* scales, const void* const* zeros, const int* N,
+                                              void* const* outs, const void* res, const void* gamma, float eps,
+                                              int K, int group_size, int n_groups_per_row);
+
 /* Device-pointer twin of nimf_cpu_vm_run_slots (backends/cpu/cpu_kernels.h:118-121,
  * cpu_vm.c:178-182): runs a micro-VM program whose first op is OP_TILE_GEMM (formats
  * 0/1/2, followed by the canonical tile ops), OP_FP4_COOP_GEMM, OP_Q4_GEMV or

@@ -189,3 +189,97 @@ def test_session_resident_api_like_reference(oracle_mod):
     out = W.matmul(torch.from_numpy(a).to(DEV))
     torch.cuda.synchronize()
     assert_close(want, out.cpu().numpy(), PEAK_TOL, None)
+
+
+# ----------------------------------------------------------------------------------------
+# The fused decode GEMV (sessionMatmulQ4Fused, gpubackend.nim:3185-3231): one launch
+# ----------------------------------------------------------------------------------------
+
+def _bound(w, x):
+    """The decode kernel's per-element fixed-point bound for W . x (float64 arrays)."""
+    N = w.shape[0]
+    blk_max = np.abs(x).reshape(-1, 32).max(axis=1)
+    quant = 2.0 ** -14 * (np.abs(w).reshape(N, -1, 32).sum(axis=2) * blk_max).sum(axis=1)
+    return quant + 1e-5 * (np.abs(w) * np.abs(x)).sum(axis=1) + 1e-30
+
+
+def _fused_case(Ns, K, seed, norm, res):
+    rng = np.random.default_rng(seed)
+    mats = [gen_q4(1, K, N, seed=seed + 17 * i)[1:] for i, N in enumerate(Ns)]
+    x = rng.normal(0, 1, size=(1, K)).astype(np.float32)
+    gamma = (rng.uniform(0.5, 1.5, K).astype(np.float32) if norm else None)
+    r = rng.normal(0, 1, size=max(Ns)).astype(np.float32) if res else None
+    xe = (x[0] * gamma).astype(np.float32) if norm else x[0]          # x * gamma in fp32, as the kernel
+    inv = 1.0 / np.sqrt(np.mean(x[0].astype(np.float64) ** 2) + 1e-5) if norm else 1.0
+    return mats, x, gamma, r, xe.astype(np.float64), inv
+
+
+def _run_fused(mode, mats, x, gamma, r, K, eps=1e-5):
+    Ws = [gb.Q4AsymWeights(wq, sc, zp, K) for wq, sc, zp in mats]
+    outs = [torch.full((1, W.N), float("nan"), device=DEV) for W in Ws]
+    dev_t = lambda v: None if v is None else torch.from_numpy(v).to(DEV)  # noqa: E731
+    gb.matmul_q4_fused(mode, torch.from_numpy(x).to(DEV), Ws, outs, res=dev_t(r), gamma=dev_t(gamma), eps=eps)
+    torch.cuda.synchronize()
+    return [o.cpu().numpy()[0].astype(np.float64) for o in outs]
+
+
+@pytest.mark.parametrize("norm,res", [(False, False), (True, True), (True, False), (False, True)])
+def test_fused_mode0_shared_activations(norm, res):
+    """Three matrices (q, k, v shapes) from one x: each output within its bound."""
+    K, Ns = 4096, (4096, 1024, 1024)
+    mats, x, gamma, r, xe, inv = _fused_case(Ns, K, 31, norm, res)
+    got = _run_fused(0, mats, x, gamma, r, K)
+    for (wq, sc, zp), N, o in zip(mats, Ns, got):
+        w = dequant_np(wq, sc, zp, K, 32)
+        want = inv * (w @ xe) + (r[:N].astype(np.float64) if res else 0.0)
+        err = np.abs(o - want)
+        assert (err <= inv * _bound(w, xe) + 1e-5 * np.abs(want)).all(), f"N={N}: {err.max():.3e}"
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("N,norm,res", [(11008, True, True), (32000, False, False), (300, True, False)])
+def test_fused_mode1_silu_gate_up(N, norm, res):
+    """silu(gate) * up (+ residual), gate and up rows in the same CTA; N = 32000 takes several
+    gate / up pass pairs per CTA."""
+    K = 4096
+    mats, x, gamma, r, xe, inv = _fused_case((N, N), K, 41, norm, res)
+    got = _run_fused(1, mats, x, gamma, r, K)[0]
+    wg, wu = (dequant_np(*m, K, 32) for m in mats)
+    g, u = inv * (wg @ xe), inv * (wu @ xe)
+    sig = 1.0 / (1.0 + np.exp(-g))
+    want = g * sig * u + (r[:N].astype(np.float64) if res else 0.0)
+    dg, du = inv * _bound(wg, xe), inv * _bound(wu, xe)
+    dsilu = np.abs(sig * (1.0 + g * (1.0 - sig)))                    # |silu'(g)| <= 1.1
+    bound = (dsilu + 1e-3) * np.abs(u) * dg + np.abs(g * sig) * du + dg * du + 1e-5 * np.abs(want) + 1e-6
+    err = np.abs(got - want)
+    assert np.isfinite(got).all()
+    assert (err <= bound).all(), f"worst excess {(err - bound).max():.3e}"
+
+
+def test_fused_session_api_and_unsupported():
+    be = gb.GpuBackend.gbCuda
+    K, N = 2048, 512
+    mats, x, gamma, r, xe, inv = _fused_case((N, N), K, 51, True, True)
+    ws = [gb.residentUploadQ4(be, wq, sc, zp, K, N, 32, K // 32) for wq, sc, zp in mats]
+    assert gb.sessionBegin(be)
+    ha, hg, hr = gb.sessionUpload(be, x), gb.sessionUpload(be, gamma), gb.sessionUpload(be, r)
+    outs = [gb.sessionAllocScratch(be, N), gb.sessionAllocScratch(be, N)]
+    assert gb.sessionMatmulQ4Fused(be, 1, ha, ws, outs, hr, True, hg, 1e-5, True)
+    # unsupported forms return False and leave the session usable
+    assert not gb.sessionMatmulQ4Fused(be, 1, ha, ws[:1], outs, hr, True, hg, 1e-5, True)   # mode 1 needs 2
+    assert not gb.sessionMatmulQ4Fused(be, 0, ha, ws, [outs[0]], hr, False)                 # too few outputs
+    assert gb.sessionEnd(be)
+    got = gb.sessionRead(be, outs[0], N).astype(np.float64)
+    wg, wu = (dequant_np(*m, K, 32) for m in mats)
+    g, u = inv * (wg @ xe), inv * (wu @ xe)
+    want = g / (1.0 + np.exp(-g)) * u + r.astype(np.float64)
+    assert np.abs(got - want).max() <= 1e-3 * max(1.0, np.abs(want).max())
+    for h in (ha, hg, hr, *outs):
+        gb.sessionFree(be, h)
+    for w in ws:
+        gb.residentFreeQ4(be, w)
+    # a K the fused kernel cannot tile: BYBYCU_ERR_SHAPE for the caller's unfused fallback
+    Ws = [gb.Q4AsymWeights(*gen_q4(1, 96, 16, seed=3)[1:], 96)]
+    with pytest.raises(_lib.BybyCudaError) as ei:
+        gb.matmul_q4_fused(0, torch.zeros(1, 96, device=DEV), Ws, [torch.empty(1, 16, device=DEV)])
+    assert ei.value.code == _lib.ERR_SHAPE

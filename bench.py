@@ -470,7 +470,43 @@ def main():
                       "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": hbm_peak, "unit": "GB/s",
                                    "frac": round(gbs / hbm_peak, 4), "peak_kind": peak_kind},
                       "l2": f"inputs larger than L2: {n_sets} rotating weight sets, CUDA graph replay"}
-            del qgraph
+            # the fused gate/up form of the same data (a Llama FFN's first half): RMSNorm of x,
+            # silu(gate) * up, residual, one launch over two 11008 x 4096 matrices per step
+            gamma = torch.rand(1, K_DEC, device=dev, generator=gen) + 0.5
+            resid = torch.randn(1, N_DEC, device=dev, generator=gen)
+            pairs = [(qsets[2 * i][0], qsets[2 * i + 1][0], torch.empty(1, N_DEC, device=dev),
+                      torch.empty(1, N_DEC, device=dev)) for i in range(n_sets // 2)]
+            fgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                for wg, wu, o0, o1 in pairs:
+                    gb.matmul_q4_fused(1, xa, [wg, wu], [o0, o1], res=resid, gamma=gamma, eps=1e-5, stream=stream)
+            stream.synchronize()
+            with torch.cuda.graph(fgraph, stream=stream):
+                for wg, wu, o0, o1 in pairs:
+                    gb.matmul_q4_fused(1, xa, [wg, wu], [o0, o1], res=resid, gamma=gamma, eps=1e-5, stream=stream)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    fgraph.replay()
+            stream.synchronize()
+            fa, fb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            fa.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(reps):
+                    fgraph.replay()
+            fb.record(stream)
+            stream.synchronize()
+            assert _lib.device_error() == 0
+            f_us = fa.elapsed_time(fb) * 1e3 / (reps * len(pairs))
+            fbytes = 2 * wbytes + 2 * K_DEC * 4 + 2 * N_DEC * 4
+            q4asym["fused_gate_up"] = {
+                "value": round(fbytes / (f_us * 1e-6) / 1e9, 2), "unit": "GB/s", "us_per_launch": round(f_us, 3),
+                "workload": "fused decode GEMV mode 1: RMSNorm(x), silu(x.Wg) * (x.Wu) + residual, "
+                            "Wg, Wu 11008 x 4096 asymmetric Q4, one launch",
+                "algorithmic_bytes": fbytes,
+                "roofline": {"bound": "hbm", "achieved": round(fbytes / (f_us * 1e-6) / 1e9, 2), "peak": hbm_peak,
+                             "unit": "GB/s", "frac": round(fbytes / (f_us * 1e-6) / 1e9 / hbm_peak, 4),
+                             "peak_kind": peak_kind}}
+            del qgraph, fgraph
         except _lib.BybyCudaError as e:
             q4asym = {"error": str(e)}
 

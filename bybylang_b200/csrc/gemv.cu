@@ -90,8 +90,8 @@ __device__ __forceinline__ void store_to_peers(const PeerGather& pg, int64_t oi,
 }
 
 // End of a GEMV launch that gathers: the barrier orders every consumer thread's stores before
-// thread 0's system-scope fence (fences are cumulative), then the last CTA signals the ranks
-// and waits for theirs.  One fence per CTA: a fence per thread cost microseconds per step.
+// thread 0's release (cumulative), then the last CTA signals the ranks and waits for theirs.
+// One release per CTA: a system fence per thread cost microseconds per step.
 __device__ __forceinline__ void gemv_gather_end(const PeerGather& pg, uint32_t consumer_threads) {
     if (pg.world <= 1) return;
     named_barrier(2, consumer_threads);

@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(256) exchange_kernel(const float* __restrict__
                 if (r < pg.world && r != pg.rank) pg.out[r][off] = v;
         }
     }
-    __syncthreads();   // every thread's stores before thread 0's system-scope fence
+    __syncthreads();   // every thread's stores before thread 0's release (peer_gather_finish)
     if (threadIdx.x == 0) peer_gather_finish(pg);
 }
 

@@ -57,7 +57,9 @@ constexpr uint32_t kOnesBf16x2 = 0x3F803F80u;
 
 struct GemvParams {
     int M, K, N, G;
-    int tiles_base, tiles_extra;   // contiguous tile split over the grid
+    int tiles_base, tiles_extra;   // contiguous split over the grid: tiles, or rows with row_split
+    int row_split;                 // M = 1: every CTA takes 74 or 75 rows (say), not 4 or 5 tiles
+    int rem_rows;                  // row_split: rows of the short last pass of a base-size CTA
     int kc;                        // K values per chunk (512, 1024 or 2048)
     int n_chunks;
     int stages;
@@ -197,7 +199,9 @@ __device__ __forceinline__ void split_f32(const float4 v, uint32_t& h0, uint32_t
 __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvParams& p, uint8_t* smem,
                                               uint64_t* full_bar, uint64_t* empty_bar, volatile int* s_abort,
                                               int lane, int tile_begin, int my_tiles, int total_it) {
+    // units: tiles, or rows with row_split; a pass covers `upass` of them
     const int wboxes = p.kc / 256;
+    const int upass = p.row_split ? p.tp * kTileRows : p.tp;
     if (lane == 0) {
         for (int i = 0; i < 3; ++i) {
             prefetch_tensormap(&maps.w[i]);
@@ -207,15 +211,24 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
         const uint64_t policy = l2_policy_evict_first();
         // Issues the weight part of iteration (chunk, t0) into stage s and arms its barrier.
         auto issue_weights = [&](int s, int chunk, int t0) {
-            const int nt = min(p.tp, tile_begin + my_tiles - t0);
+            const int nu = min(upass, tile_begin + my_tiles - t0);
+            const int nt = p.row_split ? (nu + kTileRows - 1) / kTileRows : nu;
             const int k0 = chunk * p.kc;
             const int kn = min(p.kc, p.K - k0);
-            const uint32_t rows = nt * kTileRows;
+            const uint32_t rows = p.row_split ? nu : nt * kTileRows;
             const uint32_t bytes = wboxes * rows * 128 + (p.scale_tma ? rows * p.s_pitch : 0) +
                                    (p.zeros ? rows * p.s_pitch : 0) +
                                    (p.x_whole ? 0u : p.M * static_cast<uint32_t>(kn) * p.x_elem);
             uint8_t* st = smem + static_cast<size_t>(s) * p.stage_bytes;
             mbar_arrive_expect_tx(&full_bar[s], bytes);
+            if (p.row_split) {   // one box of exactly the pass's rows: full, or one of two short heights
+                const int mi = nu == upass ? 0 : (nu == p.rem_rows ? 1 : 2);
+                for (int bx = 0; bx < wboxes; ++bx)
+                    tma_load_2d_hint(st + bx * p.w_box_bytes, &maps.w[mi], &full_bar[s], k0 / 2 + bx * 128, t0,
+                                     policy);
+                if (p.scale_tma) tma_load_2d(st + p.s_off, &maps.s[mi], &full_bar[s], k0 / 32, t0);
+                return;
+            }
             // one box per 16 * nt rows when nt is TP or TP - 1, else one per tile
             const int mi = nt == p.tp ? 0 : (nt == p.tp - 1 ? 1 : 2);
             const int pieces = mi == 2 ? nt : 1;
@@ -248,7 +261,7 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
             int chunk = 0, t0 = tile_begin;
             for (int it = 0; it < first; ++it) {
                 issue_weights(it, chunk, t0);
-                if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
+                if (++chunk == p.n_chunks) { chunk = 0; t0 += upass; }
             }
             pdl_wait();
             if (p.x_whole) {   // the whole row, chunk by chunk, each on its own barrier
@@ -268,7 +281,7 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
         }
         int issued = first;
         int s = first % p.stages, round = first / p.stages;
-        int chunk = first % p.n_chunks, t0 = tile_begin + (first / p.n_chunks) * p.tp;
+        int chunk = first % p.n_chunks, t0 = tile_begin + (first / p.n_chunks) * upass;
         for (int it = first; it < total_it; ++it) {
             if (*s_abort) break;
             if (!mbar_wait_bounded(&empty_bar[s], (round - 1) & 1, kDevErrEmptyWait)) {
@@ -279,7 +292,7 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
             issue_x(s, chunk);
             issued = it + 1;
             if (++s == p.stages) { s = 0; ++round; }
-            if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
+            if (++chunk == p.n_chunks) { chunk = 0; t0 += upass; }
         }
         // Before the CTA may exit, every copy it issued must have landed.
         for (int it = max(0, issued - p.stages); it < issued; ++it) {
@@ -645,8 +658,8 @@ __device__ __forceinline__ uint32_t digit4(uint32_t e01, uint32_t e23, float up,
 // sums for rows g and g + 8.
 template <int TP, bool STMA>
 __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* smem, uint32_t st, int box, int blk0,
-                                            int c0, int g, int t, int t0, int nt, const uint32_t (&woff)[4],
-                                            bool raw, float (&acc)[TP][2]) {
+                                            int c0, int g, int t, int64_t row0, int64_t row_end,
+                                            const uint32_t (&woff)[4], bool raw, float (&acc)[TP][2]) {
     const int q = g >> 1;
     const int bb = c0 + blk0 + q, bt = c0 + blk0 + t;
     uint2 dw;
@@ -703,9 +716,9 @@ __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* 
             sg = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(smem + sa)));
             sg8 = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(smem + sa + 8 * p.s_pitch)));
         } else {
-            const int64_t r0 = static_cast<int64_t>(t0 + i) * kTileRows + g;
+            const int64_t r0 = row0 + i * kTileRows + g;
             const int ca = c0 + blk0 + t;
-            const bool ok0 = i < nt && r0 < p.N && ca < p.G, ok8 = i < nt && r0 + 8 < p.N && ca < p.G;
+            const bool ok0 = r0 < row_end && ca < p.G, ok8 = r0 + 8 < row_end && ca < p.G;
             sg = ok0 ? __half2float(p.scales[r0 * p.G + ca]) : 0.0f;
             sg8 = ok8 ? __half2float(p.scales[(r0 + 8) * p.G + ca]) : 0.0f;
         }
@@ -734,9 +747,10 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
     pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.x;
-    const int my_tiles = p.tiles_base + (b < p.tiles_extra ? 1 : 0);
+    const int my_tiles = p.tiles_base + (b < p.tiles_extra ? 1 : 0);            // units: rows when row_split
     const int tile_begin = b * p.tiles_base + min(b, p.tiles_extra);
-    const int passes = (my_tiles + p.tp - 1) / p.tp;
+    const int upass = p.row_split ? p.tp * kTileRows : p.tp;
+    const int passes = (my_tiles + upass - 1) / upass;
     const int total_it = passes * p.n_chunks;
 
     if (threadIdx.x == 0) {
@@ -775,7 +789,11 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
 
     int s = 0, round = 0, chunk = 0, t0 = tile_begin;
     for (int it = 0; it < total_it; ++it) {
-        const int nt = min(p.tp, tile_begin + my_tiles - t0);
+        // this pass: tiles nt, rows [row0, row_end)
+        const int nu = min(upass, tile_begin + my_tiles - t0);
+        const int nt = p.row_split ? (nu + kTileRows - 1) / kTileRows : nu;
+        const int64_t row0 = p.row_split ? t0 : static_cast<int64_t>(t0) * kTileRows;
+        const int64_t row_end = min(static_cast<int64_t>(p.N), row0 + (p.row_split ? nu : nu * kTileRows));
         bool ok = !*s_abort;
         if (ok && !mbar_wait_bounded(&full_bar[s], round & 1, kDevErrFullWait)) {
             *s_abort = 1;
@@ -791,8 +809,8 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
                 ok = false;
             }
             if (ok && c0 + blk0 < p.G)
-                m1_i8_stage<TP, STMA>(p, smem, static_cast<uint32_t>(s) * p.stage_bytes, box, blk0, c0, g, t, t0,
-                                      min(p.tp, tile_begin + my_tiles - t0), woff, chunk == 0, acc);
+                m1_i8_stage<TP, STMA>(p, smem, static_cast<uint32_t>(s) * p.stage_bytes, box, blk0, c0, g, t, row0,
+                                      row_end, woff, chunk == 0, acc);
         } else if (ok && c0 + blk0 < p.G) {
             const uint32_t st = static_cast<uint32_t>(s) * p.stage_bytes;   // offset of the stage in smem
             // ---- block g of the box: this lane's activation fragments (zero past K)
@@ -885,9 +903,9 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
                     sg = half2_bits_to_float2(sh_u32(smem, sa));
                     sg8 = half2_bits_to_float2(sh_u32(smem, sa + 8 * p.s_pitch));
                 } else {
-                    const int64_t r0 = static_cast<int64_t>(t0 + i) * kTileRows + g;
+                    const int64_t r0 = row0 + i * kTileRows + g;
                     const int ca = c0 + 2 * t, cc = ca + 1;
-                    const bool v0 = i < nt && r0 < p.N, v8 = i < nt && r0 + 8 < p.N;
+                    const bool v0 = r0 < row_end, v8 = r0 + 8 < row_end;
                     sg.x = (v0 && ca < p.G) ? __half2float(p.scales[r0 * p.G + ca]) : 0.0f;
                     sg.y = (v0 && cc < p.G) ? __half2float(p.scales[r0 * p.G + cc]) : 0.0f;
                     sg8.x = (v8 && ca < p.G) ? __half2float(p.scales[(r0 + 8) * p.G + ca]) : 0.0f;
@@ -927,8 +945,8 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
                 float sum = 0.0f;
 #pragma unroll
                 for (int w = 0; w < kM1Warps; ++w) sum += lds_f32(red + ((w * TP) * 16 + e) * 4);
-                const int64_t n = static_cast<int64_t>(t0) * kTileRows + e;
-                if (n < p.N) {
+                const int64_t n = row0 + e;
+                if (n < row_end) {
                     const int64_t oi = p.out_col0 + n;
                     if (p.out_bf16) reinterpret_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(sum);
                     else reinterpret_cast<float*>(p.out)[oi] = sum;
@@ -937,7 +955,7 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
             }
             named_barrier(1, kM1Warps * 32);
         }
-        if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
+        if (++chunk == p.n_chunks) { chunk = 0; t0 += upass; }
     }
     gemv_gather_end(p.pg, kM1Warps * 32);
 }
@@ -1039,14 +1057,15 @@ bool gemv_supports(const GemmArgs& a) {
 // call, a large share of a decode step's host time, so encoded sets are kept per device in a
 // small direct-mapped cache keyed by everything the maps depend on (a map holds only the
 // address, the shape and the box; the same key always encodes the same maps).
-int gemv_maps(const GemmArgs& a, int tp, int kc, bool scale_tma, uint32_t s_pitch, GemvMaps* maps) {
+int gemv_maps(const GemmArgs& a, const int (&box_rows)[3], int kc, bool scale_tma, uint32_t s_pitch, GemvMaps* maps) {
     struct Entry {
         const void* packed = nullptr;
         int64_t scale_base = 0;
-        int K = 0, N = 0, tp = 0, kc = 0, device = -1;
+        int K = 0, N = 0, rows[3] = {0, 0, 0}, kc = 0, device = -1;
         bool scale_tma = false;
         GemvMaps maps;
     };
+    const int tp = box_rows[0] * 131 + box_rows[1] * 7 + box_rows[2];   // the box heights, hashed
     constexpr int kEntries = 64;
     static Entry cache[kEntries];
     static std::mutex mu;
@@ -1058,15 +1077,15 @@ int gemv_maps(const GemmArgs& a, int tp, int kc, bool scale_tma, uint32_t s_pitc
     {
         std::lock_guard<std::mutex> lock(mu);
         const Entry& e = cache[slot];
-        if (e.packed == a.packed && e.scale_base == a.scale_base && e.K == a.K && e.N == a.N && e.tp == tp &&
-            e.kc == kc && e.device == device && e.scale_tma == scale_tma) {
+        if (e.packed == a.packed && e.scale_base == a.scale_base && e.K == a.K && e.N == a.N &&
+            e.rows[0] == box_rows[0] && e.rows[1] == box_rows[1] && e.rows[2] == box_rows[2] && e.kc == kc &&
+            e.device == device && e.scale_tma == scale_tma) {
             *maps = e.maps;
             return BYBYCU_OK;
         }
     }
     const uint8_t* scale_ptr = a.packed + a.scale_base;
     const int G = a.K / 32;
-    const int box_rows[3] = {16 * tp, 16 * std::max(1, tp - 1), 16};
     for (int i = 0; i < 3; ++i) {
         if (int rc = encode_tensor_map_2d(&maps->w[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.N, a.K / 2,
                                           128, box_rows[i], CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1088,7 +1107,7 @@ int gemv_maps(const GemmArgs& a, int tp, int kc, bool scale_tma, uint32_t s_pitc
     e.scale_base = a.scale_base;
     e.K = a.K;
     e.N = a.N;
-    e.tp = tp;
+    for (int i = 0; i < 3; ++i) e.rows[i] = box_rows[i];
     e.kc = kc;
     e.device = device;
     e.scale_tma = scale_tma;
@@ -1104,13 +1123,17 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     const int xe = xf32 ? 4 : 2;
     const int n_tiles = static_cast<int>(ceil_div(a.N, kTileRows));
     const int grid = std::min(n_tiles, dev.sm_count);
-    const int tiles_max = static_cast<int>(ceil_div(n_tiles, grid));
+    const bool m1 = a.M == 1 && !xf32;
+    // M = 1 splits rows, not tiles: 11008 rows over 148 CTAs is 74 or 75 rows each instead of 4
+    // or 5 tiles (64 or 80 rows), so no CTA streams 6% more than its share and all end together
+    const int rows_base = a.N / grid, rows_extra = a.N % grid;
+    const int tiles_max = m1 ? static_cast<int>(ceil_div(rows_base + (rows_extra ? 1 : 0), kTileRows))
+                             : static_cast<int>(ceil_div(n_tiles, grid));
     const uint8_t* scale_ptr = a.packed + a.scale_base;
     const int G = a.K / 32;
     const bool scale_tma = (G % 8 == 0) && ((reinterpret_cast<uintptr_t>(scale_ptr) & 15u) == 0);
     const size_t budget = static_cast<size_t>(dev.max_smem_optin) - 1024 - 64;
 
-    const bool m1 = a.M == 1 && !xf32;
     // The integer mode keeps the whole activation row resident (converted in place into
     // digits, plus a factor per block and two barriers per 1024-value chunk) instead of a
     // slice per stage; rows longer than 32768 values take the fp16 mode.
@@ -1164,8 +1187,10 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
 
     GemvParams p{};
     p.M = a.M; p.K = a.K; p.N = a.N; p.G = G;
-    p.tiles_base = n_tiles / grid;
-    p.tiles_extra = n_tiles % grid;
+    p.tiles_base = m1 ? rows_base : n_tiles / grid;
+    p.tiles_extra = m1 ? rows_extra : n_tiles % grid;
+    p.row_split = m1 ? 1 : 0;
+    p.rem_rows = rows_base % (tp * kTileRows);
     p.kc = kc;
     p.n_chunks = static_cast<int>(ceil_div(a.K, kc));
     p.stages = stages;
@@ -1194,7 +1219,14 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     p.x_all_off = p.xbar_off + static_cast<uint32_t>(n_xchunks) * 16;
 
     GemvMaps maps;
-    if (int rc = gemv_maps(a, tp, kc, scale_tma, s_pitch, &maps)) return rc;
+    int box_rows[3] = {kTileRows * tp, kTileRows * std::max(1, tp - 1), kTileRows};
+    if (m1) {   // a full pass, and the short last passes of the two CTA sizes (unused slots: full)
+        const int full = kTileRows * tp;
+        const int ra = rows_base % full, rb = (rows_base + 1) % full;
+        box_rows[1] = ra ? ra : full;
+        box_rows[2] = rb ? rb : full;
+    }
+    if (int rc = gemv_maps(a, box_rows, kc, scale_tma, s_pitch, &maps)) return rc;
     const cudaStream_t st = a.stream;
     if (m1) {
         if (scale_tma)

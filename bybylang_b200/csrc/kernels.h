@@ -42,15 +42,17 @@ struct PeerGather {
 __device__ __forceinline__ bool peer_gather_finish(const PeerGather& pg) {
     // The CTA's completion count is an acq_rel atomic at GPU scope: a release of every store
     // this CTA made (the caller's barrier makes the other threads' stores this thread's), and,
-    // for the last CTA, an acquire of every other CTA's.  The last CTA's signals are releases
-    // at system scope, which carry all of those stores to the peers' acquire loads.
+    // for the last CTA, an acquire of every other CTA's.  The last CTA's system-scope release
+    // fence then carries all of those stores before its signals, to the peers' acquire loads.
     uint32_t* mine = pg.sig[pg.rank];
     uint32_t prev;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(mine + kMaxRanks + 1) : "memory");
     if (prev != gridDim.x * gridDim.y * gridDim.z - 1) return true;
     mine[kMaxRanks + 1] = 0;   // every CTA of this launch has counted
+    // one system-scope release fence covers the signals to every rank
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
     for (int r = 0; r < pg.world; ++r)
-        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(pg.sig[r] + pg.rank) : "memory");
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(pg.sig[r] + pg.rank) : "memory");
     const uint32_t target = pg.epoch ? pg.epoch : mine[kMaxRanks] + 1;
     bool ok = true;
     for (int r = 0; r < pg.world && ok; ++r) {

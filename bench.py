@@ -14,6 +14,7 @@ fp32 out - through libbybycuda's GEMV route.  Algorithmic bytes per step: 25,362
 * cpu_baseline  the reference's own CPU C (oracle/_ref: OP_TILE_GEMM through
               nimf_cpu_vm_run_slots, single-threaded as the reference is) on the same shape.
 * prefill     config C3 (M=2048, K=N=4096) TFLOP/s when the tensor-core route is present.
+* f16_decode  format 1 (fp16 weights) at the C2 shape through the tile GEMM's decode route.
 * q4_asym_decode  the asymmetric Q4 data of the reference's matmul_q4 (interleaved nibbles, fp32
               scales and zero points per 32-block, fp32 x) at the C2 shape through
               bybycu_matmul_q4's decode kernel: GB/s of its 0.75 B/weight, rotating sets > 4x L2.
@@ -510,6 +511,54 @@ def main():
         except _lib.BybyCudaError as e:
             q4asym = {"error": str(e)}
 
+    # ---- format 1 (fp16 weights, 2 B per weight) decode at the C2 shape, through the tile GEMM's
+    # decode route
+    f16dec = None
+    if world == 1 and not args.no_q4asym:
+        try:
+            fbytes = N_DEC * K_DEC * 2
+            n_sets = max(2, -(-4 * L2_BYTES // fbytes))
+            gen = torch.Generator(device=dev).manual_seed(SEED + 41)
+            hsets = [((torch.randn(N_DEC, K_DEC, device=dev, generator=gen) * 0.05).half().view(torch.uint8),
+                      torch.empty(1, N_DEC, device=dev)) for _ in range(n_sets)]
+
+            def f16_launch(i):
+                wh, o = hsets[i % n_sets]
+                gb.tile_gemm(1, x, wh, o, M=1, K=K_DEC, N=N_DEC, route=_lib.ROUTE_GEMV, stream=stream)
+            with torch.cuda.stream(stream):
+                for i in range(n_sets):
+                    f16_launch(i)
+            stream.synchronize()
+            hgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(hgraph, stream=stream):
+                for i in range(n_sets):
+                    f16_launch(i)
+            reps = max(20, min(reps_t, 2000 // n_sets))
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    hgraph.replay()
+            stream.synchronize()
+            ha, hb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ha.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(reps):
+                    hgraph.replay()
+            hb.record(stream)
+            stream.synchronize()
+            assert _lib.device_error() == 0
+            h_us = ha.elapsed_time(hb) * 1e3 / (reps * n_sets)
+            hbytes = fbytes + K_DEC * 2 + N_DEC * 4
+            f16dec = {"value": round(hbytes / (h_us * 1e-6) / 1e9, 2), "unit": "GB/s", "us_per_launch": round(h_us, 3),
+                      "workload": "format 1 (fp16 weights) decode M=1 K=4096 N=11008, x bf16, out fp32",
+                      "algorithmic_bytes": hbytes,
+                      "roofline": {"bound": "hbm", "achieved": round(hbytes / (h_us * 1e-6) / 1e9, 2),
+                                   "peak": hbm_peak, "unit": "GB/s",
+                                   "frac": round(hbytes / (h_us * 1e-6) / 1e9 / hbm_peak, 4), "peak_kind": peak_kind},
+                      "l2": f"inputs larger than L2: {n_sets} rotating weight sets, CUDA graph replay"}
+            del hgraph, hsets
+        except _lib.BybyCudaError as e:
+            f16dec = {"error": str(e)}
+
     if rank == 0:
         base = None
         if not args.no_cpu_baseline and world == 1:   # the host-core baseline: rank 0 at N = 1 only
@@ -534,6 +583,7 @@ def main():
             "cpu_baseline": base, "e2e": e2e, "gpu_launches": steps * launches_per_step, "clocks": clocks,
             "prefill": prefill,
             "q4_asym_decode": q4asym,
+            "f16_decode": f16dec,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

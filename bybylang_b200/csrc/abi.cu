@@ -119,7 +119,8 @@ int choose_route(const GemmArgs& a, int requested, int* route) {
     if (requested == BYBYCU_ROUTE_SIMT) { *route = BYBYCU_ROUTE_SIMT; return BYBYCU_OK; }
     if (requested == BYBYCU_ROUTE_GEMV) {
         if (!gemv_supports(a))
-            return set_error(BYBYCU_ERR_SHAPE, "GEMV route needs format 2, M <= 16 and 16-byte aligned slots");
+            return set_error(BYBYCU_ERR_SHAPE, "GEMV route needs format 2 (M <= 16) or format 1 (M <= 8) and "
+                                               "16-byte aligned slots");
         *route = BYBYCU_ROUTE_GEMV;
         return BYBYCU_OK;
     }

@@ -4,6 +4,7 @@
 #include "simt.cu"
 #include "gemv.cu"
 #include "q4asym.cu"
+#include "f16gemv.cu"
 #include "tc.cu"
 #include "vm.cu"
 #include "session.cu"

@@ -1044,6 +1044,7 @@ size_t round1k(size_t v) { return (v + 1023) / 1024 * 1024; }
 }  // namespace
 
 bool gemv_supports(const GemmArgs& a) {
+    if (a.fmt == BYBYCU_FMT_F16) return f16_gemv_supports(a);   // f16gemv.cu
     if (a.fmt != BYBYCU_FMT_Q4B32) return false;
     if (a.M < 1 || a.M > 16 || a.K % 32 != 0 || a.N < 1) return false;
     if (a.x_dtype != BYBYCU_DT_BF16 && a.x_dtype != BYBYCU_DT_F32) return false;
@@ -1116,6 +1117,10 @@ int gemv_maps(const GemmArgs& a, const int (&box_rows)[3], int kc, bool scale_tm
 }
 
 int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
+    if (a.fmt == BYBYCU_FMT_F16) {
+        if (pg) return set_error(BYBYCU_ERR_ARGS, "the format-1 GEMV does not store to peers");
+        return launch_f16_gemv(a);
+    }
     DeviceInfo dev;
     if (int rc = current_device_info(&dev)) return rc;
     const bool xf32 = a.x_dtype == BYBYCU_DT_F32;

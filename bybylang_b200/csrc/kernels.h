@@ -77,6 +77,9 @@ int launch_simt(const GemmArgs& a);
 // Decode GEMV route (format 2, M <= 16): TMA-streamed weights, bf16 mma.sync reductions with
 // exact per-block fp32 scaling.
 bool gemv_supports(const GemmArgs& a);
+// Format 1 (fp16 weights) decode GEMV, M <= 8: 16-byte weight streams, fp32 FMAs.
+bool f16_gemv_supports(const GemmArgs& a);
+int launch_f16_gemv(const GemmArgs& a);
 int launch_gemv(const GemmArgs& a, const PeerGather* pg = nullptr);
 // Prefill GEMM route: tcgen05 MMAs from shared-memory fp16 tiles, fp32 accumulators in TMEM.
 bool tc_supports(const GemmArgs& a);

@@ -221,6 +221,49 @@ def test_auto_route_small_m_is_gemv(oracle_mod):
 
 
 # ----------------------------------------------------------------------------------------
+# Format 1 (fp16 weights) on the decode route (M <= 8): the GEMV tolerances
+# ----------------------------------------------------------------------------------------
+
+def test_f16_gemv_reference_cases(golden):
+    g = golden["ref_tile_cases"]
+    ran = 0
+    for i in range(5):
+        M, K, N = (int(v) for v in g[f"f16_{i}_shape"])
+        if M > 8:
+            continue
+        out = run(1, M, K, N, dev(g[f"f16_{i}_x"]), dev(g[f"f16_{i}_halves"].view(np.uint8)), route=_lib.ROUTE_GEMV)
+        assert_close(g[f"f16_{i}_dyn"], out.cpu().numpy(), what=f"case {i}")
+        ran += 1
+    assert ran >= 1
+
+
+@pytest.mark.parametrize("M,K,N,xbf16", [(1, 4096, 11008, True), (1, 4096, 11008, False), (3, 512, 300, True),
+                                         (8, 1024, 77, False), (1, 32, 1, True), (5, 2048, 1000, True)])
+def test_f16_gemv_against_oracle(M, K, N, xbf16, oracle_mod):
+    O = oracle_mod
+    rng = np.random.default_rng(M * K + N)
+    halves = (rng.normal(0, 0.05, size=(N, K))).astype(np.float16)
+    if xbf16:
+        xb = O.gen_x_bf16(M, K, seed=N)
+        x = dev(xb).view(torch.bfloat16)
+        xf = O.bf16_to_f32(xb)
+    else:
+        xf = rng.normal(0, 1, size=(M, K)).astype(np.float32)
+        x = dev(xf)
+    want = O.tile_gemm_f16(xf, halves.view(np.uint16), M, K, N)
+    out = run(1, M, K, N, x, dev(halves.view(np.uint8)), route=_lib.ROUTE_GEMV)
+    assert_close(want, out.cpu().numpy(), what=f"M={M} K={K} N={N}")
+    b16 = run(1, M, K, N, x, dev(halves.view(np.uint8)), route=_lib.ROUTE_GEMV, out_dtype=torch.bfloat16)
+    assert torch.equal(out.to(torch.bfloat16), b16)
+
+
+def test_auto_route_f16_decode_is_gemv():
+    assert gb.route_for(1, 1, 4096, 4096) == _lib.ROUTE_GEMV
+    assert gb.route_for(1, 8, 4096, 4096) == _lib.ROUTE_GEMV
+    assert gb.route_for(1, 9, 4096, 4096) == _lib.ROUTE_SIMT
+
+
+# ----------------------------------------------------------------------------------------
 # Dequantisation: bit-exact
 # ----------------------------------------------------------------------------------------
 

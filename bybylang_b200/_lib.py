@@ -36,6 +36,20 @@ ROUTE_SIMT = 3
 ROUTE_NAMES = {ROUTE_AUTO: "auto", ROUTE_GEMV: "gemv", ROUTE_TC: "tc", ROUTE_SIMT: "simt"}
 
 
+OP_TILE_GEMM = 0
+OP_MATMUL_Q4 = 1
+
+
+class Plan(C.Structure):
+    """bybycu_plan: a tuned route and its launch knobs."""
+    _fields_ = [("route", C.c_int32), ("variant", C.c_int32), ("stages", C.c_int32), ("ms", C.c_float),
+                ("name", C.c_char * 32)]
+
+    def __repr__(self) -> str:
+        return (f"Plan({self.name.decode()!r}, route={ROUTE_NAMES.get(self.route, self.route)}, "
+                f"variant={self.variant}, stages={self.stages}, ms={self.ms:.4f})")
+
+
 class BybyCudaError(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"[cuda] {message} (status {code})")
@@ -91,6 +105,13 @@ SIGNATURES = {
     "bybycu_tile_gemm_allgather": [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _vp, _i64, _i64,
                                    _vp, _i64, _i64, _vp, C.POINTER(_vp), C.POINTER(C.POINTER(_u32)),
                                    _i32, _i32, _u32, _vp],
+    "bybycu_prepare_q4_tuned": [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, C.POINTER(_i32)],
+    "bybycu_prepare_tile_gemm_tuned": [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _i64, C.POINTER(_i32)],
+    "bybycu_plan_get": [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, C.POINTER(Plan), C.POINTER(_i32)],
+    "bybycu_plan_set": [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, C.POINTER(Plan)],
+    "bybycu_plan_clear": [],
+    "bybycu_tuning_stats": [C.POINTER(_i32), C.POINTER(_i64)],
+    "bybycu_tune_cache_path": [C.c_char_p, _i32],
 }
 
 _lib = None

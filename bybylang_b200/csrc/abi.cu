@@ -166,6 +166,7 @@ int tile_gemm_impl(int fmt, int M, int K, int N, const void* x, int x_dtype, int
     a.out = out; a.out_dtype = out_dtype;
     a.out_ld = N; a.out_col0 = 0;
     a.stream = stream;
+    if (route == BYBYCU_ROUTE_AUTO) apply_tile_gemm_plan(&a, &route);
     int r = 0;
     if (int rc = choose_route(a, route, &r)) return rc;
     return run_gemm(a, r);
@@ -348,7 +349,9 @@ int bybycu_route_for(int fmt, int M, int K, int N, int x_dtype, int* route) {
     a.fmt = fmt; a.M = M; a.K = K; a.N = N; a.x_dtype = x_dtype;
     static const uint8_t* const aligned = reinterpret_cast<const uint8_t*>(uintptr_t(1) << 20);
     a.packed = aligned; a.x = aligned; a.out = const_cast<uint8_t*>(aligned);
-    return choose_route(a, BYBYCU_ROUTE_AUTO, route);
+    int requested = BYBYCU_ROUTE_AUTO;
+    apply_tile_gemm_plan(&a, &requested);
+    return choose_route(a, requested, route);
 }
 
 }  // extern "C"

@@ -9,3 +9,4 @@
 #include "vm.cu"
 #include "session.cu"
 #include "shard.cu"
+#include "tune.cu"

@@ -138,8 +138,10 @@ int launch_f16_gemv(const GemmArgs& a) {
     DeviceInfo dev;
     if (int rc = current_device_info(&dev)) return rc;
     const size_t smem = static_cast<size_t>(a.M) * a.K * 4;
-    // CTAs per SM: as many as the activation copy and 48 warps allow, and no more than the rows need
-    const int per_sm = std::max(1, std::min(3, static_cast<int>(dev.max_smem_optin / std::max<size_t>(smem, 1))));
+    // CTAs per SM: as many as the activation copy and 48 warps allow (or a tuned plan's count,
+    // a.variant, within that), and no more than the rows need
+    int per_sm = std::max(1, std::min(3, static_cast<int>(dev.max_smem_optin / std::max<size_t>(smem, 1))));
+    if (a.variant >= 1) per_sm = std::min(per_sm, a.variant);
     const int groups = static_cast<int>(ceil_div(a.N, kF16Rows));
     const int grid = std::max(1, std::min(dev.sm_count * per_sm, static_cast<int>(ceil_div(groups, kF16Warps))));
     if (a.M == 1) return launch_f16_m<1>(a, grid, smem);

@@ -173,6 +173,9 @@ __device__ __forceinline__ uint32_t sh_u32(const uint8_t* smem, uint32_t off) {
 __device__ __forceinline__ uint2 sh_u64(const uint8_t* smem, uint32_t off) {
     return *reinterpret_cast<const uint2*>(smem + off);
 }
+__device__ __forceinline__ uint4 sh_u128(const uint8_t* smem, uint32_t off) {
+    return *reinterpret_cast<const uint4*>(smem + off);
+}
 
 __device__ __forceinline__ float2 half2_bits_to_float2(uint32_t v) {
     __half2 h;
@@ -559,7 +562,7 @@ constexpr int kM1I8 = 2;     // s8 MMAs on 16 q and two-digit fixed-point activa
 // g % 2 of block g / 2 (its elements 4t..4t+3 and 16+4t..16+4t+3, the B fragment's k slots)
 // and accumulates block t of each tile into acc.
 // The integer mode's activation side, done by the digit warp once per launch: the resident
-// bf16 row is turned in place into B-fragment words.  Lane t of quad g converts blocks g,
+// bf16 (or fp32) row is turned in place into B-fragment words.  Lane t of quad g converts blocks g,
 // g + 8, g + 16 and g + 24 of a chunk: in each it reads elements 4t..4t+3 (bytes 8t..8t+7 of
 // the block) and 16+4t..16+4t+3 (bytes 32+8t..) and writes back at exactly those bytes the
 // low and the high digits of the same elements, so block b's 64 bytes become
@@ -568,29 +571,60 @@ constexpr int kM1I8 = 2;     // s8 MMAs on 16 q and two-digit fixed-point activa
 // is the low digit, and the second byte of the same sum with 128 more is the high digit
 // (X + 128) >> 8.  The factor 2^(E - 144) of each block (it undoes the scaling and the 16 of
 // the 16 q operands) goes to the factor table.  All loads come before all stores, so the four
-// blocks' dependency chains overlap.
+// blocks' dependency chains overlap.  An fp32 row keeps 128 bytes per block; its digits take
+// the first 64 of them (lane t's loads at bytes 16t.. and 64+16t.. feed the block's exponent,
+// which the quad shuffles before any lane stores, so no store lands on bytes still unread).
+template <bool XF32>
+__device__ __forceinline__ float m1_x_elem(const uint2& lo, const uint2& hi, const uint4& lo4, const uint4& hi4, int i) {
+    if constexpr (XF32) {
+        const uint32_t w[8] = {lo4.x, lo4.y, lo4.z, lo4.w, hi4.x, hi4.y, hi4.z, hi4.w};
+        return __uint_as_float(w[i]);
+    } else {
+        const uint32_t w[4] = {lo.x, lo.y, hi.x, hi.y};
+        return __uint_as_float((i & 1) ? (w[i >> 1] & 0xFFFF0000u) : (w[i >> 1] << 16));
+    }
+}
+
+// The biased exponent of the largest magnitude among a lane's 8 raw activations:
+// magnitude bit patterns order like the values, and inf / NaN sort above every finite value.
+template <bool XF32>
+__device__ __forceinline__ int m1_max_exp(const uint2& lo, const uint2& hi, const uint4& lo4, const uint4& hi4) {
+    if constexpr (XF32) {
+        const uint32_t m = max(max(max(lo4.x & 0x7FFFFFFFu, lo4.y & 0x7FFFFFFFu), max(lo4.z & 0x7FFFFFFFu, lo4.w & 0x7FFFFFFFu)),
+                               max(max(hi4.x & 0x7FFFFFFFu, hi4.y & 0x7FFFFFFFu), max(hi4.z & 0x7FFFFFFFu, hi4.w & 0x7FFFFFFFu)));
+        return static_cast<int>(m >> 23);
+    } else {
+        const uint32_t m2 = __vmaxu2(__vmaxu2(lo.x & 0x7FFF7FFFu, lo.y & 0x7FFF7FFFu),
+                                     __vmaxu2(hi.x & 0x7FFF7FFFu, hi.y & 0x7FFF7FFFu));
+        return static_cast<int>(max(m2 & 0xFFFFu, m2 >> 16) >> 7);
+    }
+}
+
+template <bool XF32>
 __device__ __forceinline__ void m1_digits_chunk(const GemvParams& p, uint8_t* smem, int chunk, int g, int t) {
     constexpr int J = 4;
+    constexpr uint32_t kPitch = XF32 ? 128u : 64u;   // bytes of one block of the resident row
+    constexpr uint32_t kElem = XF32 ? 4u : 2u;
     uint2 lo[J], hi[J];
+    uint4 lo4[J], hi4[J];
     uint32_t xr[J];
     bool live[J];
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         const int blk = chunk * (kM1KC / 32) + 8 * j + g;
         live[j] = blk < p.G;
-        xr[j] = p.x_all_off + blk * 64 + 8 * t;
-        lo[j] = live[j] ? sh_u64(smem, xr[j]) : make_uint2(0u, 0u);
-        hi[j] = live[j] ? sh_u64(smem, xr[j] + 32) : make_uint2(0u, 0u);
+        xr[j] = p.x_all_off + blk * kPitch;
+        if constexpr (XF32) {
+            lo4[j] = live[j] ? sh_u128(smem, xr[j] + 16 * t) : make_uint4(0u, 0u, 0u, 0u);
+            hi4[j] = live[j] ? sh_u128(smem, xr[j] + 64 + 16 * t) : make_uint4(0u, 0u, 0u, 0u);
+        } else {
+            lo[j] = live[j] ? sh_u64(smem, xr[j] + 8 * t) : make_uint2(0u, 0u);
+            hi[j] = live[j] ? sh_u64(smem, xr[j] + 32 + 8 * t) : make_uint2(0u, 0u);
+        }
     }
-    // each block's largest exponent: magnitude bit patterns order like the values, and inf /
-    // NaN sort above every finite value
     int e[J];
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-        const uint32_t m2 = __vmaxu2(__vmaxu2(lo[j].x & 0x7FFF7FFFu, lo[j].y & 0x7FFF7FFFu),
-                                     __vmaxu2(hi[j].x & 0x7FFF7FFFu, hi[j].y & 0x7FFF7FFFu));
-        e[j] = static_cast<int>(max(m2 & 0xFFFFu, m2 >> 16) >> 7);
-    }
+    for (int j = 0; j < J; ++j) e[j] = m1_max_exp<XF32>(lo[j], hi[j], lo4[j], hi4[j]);
 #pragma unroll
     for (int j = 0; j < J; ++j) e[j] = max(e[j], __shfl_xor_sync(0xffffffffu, e[j], 1));
 #pragma unroll
@@ -601,15 +635,12 @@ __device__ __forceinline__ void m1_digits_chunk(const GemvParams& p, uint8_t* sm
         if (live[j] && e[j] == 255 && t == 0) record_device_error(kDevErrActRange);   // inf or NaN
         e[j] = max(e[j], 18);                                  // blocks below 2^-109: normal factors
         const float up = __int_as_float((267 - e[j]) << 23);   // 2^(140 - E)
-        const uint32_t w[4] = {lo[j].x, lo[j].y, hi[j].x, hi[j].y};
         uint32_t r[8], h[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float f0 = __uint_as_float(w[i] << 16), f1 = __uint_as_float(w[i] & 0xFFFF0000u);
-            r[2 * i] = __float_as_uint(fmaf(f0, up, 12582912.0f));       // 0x4B400000 + X
-            r[2 * i + 1] = __float_as_uint(fmaf(f1, up, 12582912.0f));
-            h[2 * i] = __float_as_uint(fmaf(f0, up, 12583040.0f));       // 0x4B400000 + X + 128
-            h[2 * i + 1] = __float_as_uint(fmaf(f1, up, 12583040.0f));
+        for (int i = 0; i < 8; ++i) {
+            const float f = m1_x_elem<XF32>(lo[j], hi[j], lo4[j], hi4[j], i);
+            r[i] = __float_as_uint(fmaf(f, up, 12582912.0f));   // 0x4B400000 + X
+            h[i] = __float_as_uint(fmaf(f, up, 12583040.0f));   // 0x4B400000 + X + 128
         }
         out[j][0] = prmt(prmt(r[0], r[1], 0x0040), prmt(r[2], r[3], 0x0040), 0x5410);
         out[j][1] = prmt(prmt(r[4], r[5], 0x0040), prmt(r[6], r[7], 0x0040), 0x5410);
@@ -619,10 +650,10 @@ __device__ __forceinline__ void m1_digits_chunk(const GemvParams& p, uint8_t* sm
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         if (!live[j]) continue;
-        *reinterpret_cast<uint2*>(smem + xr[j]) = make_uint2(out[j][0], out[j][1]);
-        *reinterpret_cast<uint2*>(smem + xr[j] + 32) = make_uint2(out[j][2], out[j][3]);
+        *reinterpret_cast<uint2*>(smem + xr[j] + 8 * t) = make_uint2(out[j][0], out[j][1]);
+        *reinterpret_cast<uint2*>(smem + xr[j] + 32 + 8 * t) = make_uint2(out[j][2], out[j][3]);
         if (t == 0)
-            *reinterpret_cast<float*>(smem + p.x_all_off + static_cast<uint32_t>(p.K) * 2 +
+            *reinterpret_cast<float*>(smem + p.x_all_off + static_cast<uint32_t>(p.K) * kElem +
                                       (chunk * (kM1KC / 32) + 8 * j + g) * 4) = __int_as_float((e[j] - 17) << 23);
     }
 }
@@ -631,12 +662,13 @@ __device__ __forceinline__ void m1_digits_chunk(const GemvParams& p, uint8_t* sm
 // (the consumers build chunk 0's operands themselves from the raw row, so that the first
 // MMAs wait for no conversion).  It always marks a chunk, after a timeout too, so that no
 // consumer waits for it in vain.
+template <bool XF32>
 __device__ __forceinline__ void m1_digit_warp(const GemvParams& p, uint8_t* smem, volatile int* s_abort, int lane) {
     uint64_t* x_bar = reinterpret_cast<uint64_t*>(smem + p.xbar_off);
     uint64_t* ready = x_bar + p.n_chunks;
     for (int c = 1; c < p.n_chunks; ++c) {
         if (!*s_abort && !mbar_wait_bounded(&x_bar[c], 0, kDevErrFullWait)) *s_abort = 1;
-        m1_digits_chunk(p, smem, c, lane >> 2, lane & 3);
+        m1_digits_chunk<XF32>(p, smem, c, lane >> 2, lane & 3);
         __syncwarp();
         if (lane == 0) mbar_arrive(&ready[c]);   // release: the digits above before the arrival
     }
@@ -651,29 +683,43 @@ __device__ __forceinline__ uint32_t digit4(uint32_t e01, uint32_t e23, float up,
     const uint32_t r3 = __float_as_uint(fmaf(__uint_as_float(e23 & 0xFFFF0000u), up, magic));
     return prmt(prmt(r0, r1, sel), prmt(r2, r3, sel), 0x5410);
 }
+// The same for four raw fp32 activations.
+__device__ __forceinline__ uint32_t digit4f(uint4 v, float up, float magic, uint32_t sel) {
+    const uint32_t r0 = __float_as_uint(fmaf(__uint_as_float(v.x), up, magic));
+    const uint32_t r1 = __float_as_uint(fmaf(__uint_as_float(v.y), up, magic));
+    const uint32_t r2 = __float_as_uint(fmaf(__uint_as_float(v.z), up, magic));
+    const uint32_t r3 = __float_as_uint(fmaf(__uint_as_float(v.w), up, magic));
+    return prmt(prmt(r0, r1, sel), prmt(r2, r3, sel), 0x5410);
+}
 
 // The weight side of one chunk in the integer mode for one warp: blocks blk0 .. blk0 + 3 of
 // box `box` (c0 = the box's first block of K) for the pass's nt tiles, accumulated into acc.
 // Lane (g, t) feeds B column g (digit g % 2 of block g / 2) and combines block t's two digit
 // sums for rows g and g + 8.
-template <int TP, bool STMA>
+template <int TP, bool STMA, bool XF32>
 __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* smem, uint32_t st, int box, int blk0,
                                             int c0, int g, int t, int64_t row0, int64_t row_end,
                                             const uint32_t (&woff)[4], bool raw, float (&acc)[TP][2]) {
+    constexpr uint32_t kPitch = XF32 ? 128u : 64u;   // bytes of one block of the resident row
+    constexpr uint32_t kElem = XF32 ? 4u : 2u;
     const int q = g >> 1;
     const int bb = c0 + blk0 + q, bt = c0 + blk0 + t;
     uint2 dw;
     float ft;
     if (raw) {   // chunk 0: the digits from the raw row, here (the same arithmetic as m1_digits_chunk)
-        const uint32_t xr = p.x_all_off + (32 * bb + 4 * t) * 2;
+        const uint32_t xr = p.x_all_off + bb * kPitch + 4 * t * kElem;
         uint2 lo = make_uint2(0u, 0u), hi = make_uint2(0u, 0u);
+        uint4 lo4 = make_uint4(0u, 0u, 0u, 0u), hi4 = make_uint4(0u, 0u, 0u, 0u);
         if (bb < p.G) {
-            lo = sh_u64(smem, xr);
-            hi = sh_u64(smem, xr + 32);
+            if constexpr (XF32) {
+                lo4 = sh_u128(smem, xr);
+                hi4 = sh_u128(smem, xr + 64);
+            } else {
+                lo = sh_u64(smem, xr);
+                hi = sh_u64(smem, xr + 32);
+            }
         }
-        const uint32_t m2 = __vmaxu2(__vmaxu2(lo.x & 0x7FFF7FFFu, lo.y & 0x7FFF7FFFu),
-                                     __vmaxu2(hi.x & 0x7FFF7FFFu, hi.y & 0x7FFF7FFFu));
-        int e = static_cast<int>(max(m2 & 0xFFFFu, m2 >> 16) >> 7);
+        int e = m1_max_exp<XF32>(lo, hi, lo4, hi4);
         e = max(e, __shfl_xor_sync(0xffffffffu, e, 1));
         e = max(e, __shfl_xor_sync(0xffffffffu, e, 2));
         if (bb < p.G && e == 255 && t == 0 && !(g & 1)) record_device_error(kDevErrActRange);   // inf or NaN
@@ -681,12 +727,13 @@ __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* 
         const float up = __int_as_float((267 - e) << 23);
         const float magic = (g & 1) ? 12583040.0f : 12582912.0f;
         const uint32_t sel = (g & 1) ? 0x0051u : 0x0040u;
-        dw = make_uint2(digit4(lo.x, lo.y, up, magic, sel), digit4(hi.x, hi.y, up, magic, sel));
+        if constexpr (XF32) dw = make_uint2(digit4f(lo4, up, magic, sel), digit4f(hi4, up, magic, sel));
+        else dw = make_uint2(digit4(lo.x, lo.y, up, magic, sel), digit4(hi.x, hi.y, up, magic, sel));
         const int et = __shfl_sync(0xffffffffu, e, 8 * t);   // lane 8t built block t
         ft = bt < p.G ? __int_as_float((et - 17) << 23) : 0.0f;
     } else {
-        dw = bb < p.G ? sh_u64(smem, p.x_all_off + bb * 64 + (g & 1) * 32 + 8 * t) : make_uint2(0u, 0u);
-        ft = bt < p.G ? *reinterpret_cast<const float*>(smem + p.x_all_off + static_cast<uint32_t>(p.K) * 2 + bt * 4)
+        dw = bb < p.G ? sh_u64(smem, p.x_all_off + bb * kPitch + (g & 1) * 32 + 8 * t) : make_uint2(0u, 0u);
+        ft = bt < p.G ? *reinterpret_cast<const float*>(smem + p.x_all_off + static_cast<uint32_t>(p.K) * kElem + bt * 4)
                       : 0.0f;
     }
     uint32_t bq[4][2];
@@ -729,9 +776,10 @@ __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* 
 
 // Two CTAs per SM: the register cap (96) lets the next launch's CTA sit beside the running
 // one, so its producer streams weights while this one computes (programmatic dependent launch).
-template <int TP, bool STMA, int MODE>
+template <int TP, bool STMA, int MODE, bool XF32 = false>
 __global__ void __launch_bounds__(kM1Threads, 2)
 gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
+    static_assert(!XF32 || MODE == kM1I8, "fp32 activations: the integer mode only");
     constexpr int S = 2 * kM1Blocks;   // MMA steps per warp per box (low / high half per block)
     constexpr bool F16A = MODE == kM1F16;
     static_assert(MODE != kM1I8 || kM1Blocks == 4, "the integer mode fills 8 columns with 4 blocks x 2 digits");
@@ -770,7 +818,7 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
         return;
     }
     if (warp == kM1Warps + 1) {
-        if constexpr (MODE == kM1I8) m1_digit_warp(p, smem, s_abort, lane);
+        if constexpr (MODE == kM1I8) m1_digit_warp<XF32>(p, smem, s_abort, lane);
         return;
     }
 
@@ -809,8 +857,8 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
                 ok = false;
             }
             if (ok && c0 + blk0 < p.G)
-                m1_i8_stage<TP, STMA>(p, smem, static_cast<uint32_t>(s) * p.stage_bytes, box, blk0, c0, g, t, row0,
-                                      row_end, woff, chunk == 0, acc);
+                m1_i8_stage<TP, STMA, XF32>(p, smem, static_cast<uint32_t>(s) * p.stage_bytes, box, blk0, c0, g, t,
+                                            row0, row_end, woff, chunk == 0, acc);
         } else if (ok && c0 + blk0 < p.G) {
             const uint32_t st = static_cast<uint32_t>(s) * p.stage_bytes;   // offset of the stage in smem
             // ---- block g of the box: this lane's activation fragments (zero past K)
@@ -1006,13 +1054,14 @@ int m1_mode() {
 }
 
 template <int TP, bool STMA>
-int launch_m1(int mode, const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, cudaStream_t stream) {
-    auto kern = mode == kM1I8 ? gemv_m1_kernel<TP, STMA, kM1I8>
+int launch_m1(int mode, bool xf32, const GemvMaps& maps, const GemvParams& p, int grid, size_t smem,
+              cudaStream_t stream) {
+    auto kern = mode == kM1I8 ? (xf32 ? gemv_m1_kernel<TP, STMA, kM1I8, true> : gemv_m1_kernel<TP, STMA, kM1I8>)
               : mode == kM1F16 ? gemv_m1_kernel<TP, STMA, kM1F16> : gemv_m1_kernel<TP, STMA, kM1Bf16>;
-    static uint64_t configured[3] = {0, 0, 0};
+    static uint64_t configured[4] = {0, 0, 0, 0};
     int dev = 0;
     BYBYCU_CUDA_TRY(cudaGetDevice(&dev));
-    const int fi = mode;
+    const int fi = xf32 ? 3 : mode;
     if (!(configured[fi] >> (dev & 63) & 1)) {
         BYBYCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
         configured[fi] |= uint64_t(1) << (dev & 63);
@@ -1128,7 +1177,11 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     const int xe = xf32 ? 4 : 2;
     const int n_tiles = static_cast<int>(ceil_div(a.N, kTileRows));
     const int grid = std::min(n_tiles, dev.sm_count);
-    const bool m1 = a.M == 1 && !xf32;
+    // the M = 1 kernel: bf16 rows in every operand mode, fp32 rows in the integer mode (the
+    // other modes take fp32 rows through the general kernel's two-term split)
+    const int want_mode = a.variant >= kM1Bf16 && a.variant <= kM1I8 ? a.variant : m1_mode();
+    const int mode = want_mode == kM1I8 && a.K > 32768 ? kM1F16 : want_mode;
+    const bool m1 = a.M == 1 && (!xf32 || mode == kM1I8);
     // M = 1 splits rows, not tiles: 11008 rows over 148 CTAs is 74 or 75 rows each instead of 4
     // or 5 tiles (64 or 80 rows), so no CTA streams 6% more than its share and all end together
     const int rows_base = a.N / grid, rows_extra = a.N % grid;
@@ -1142,7 +1195,6 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     // The integer mode keeps the whole activation row resident (converted in place into
     // digits, plus a factor per block and two barriers per 1024-value chunk) instead of a
     // slice per stage; rows longer than 32768 values take the fp16 mode.
-    const int mode = m1_mode() == kM1I8 && a.K > 32768 ? kM1F16 : m1_mode();
     const bool x_whole = m1 && mode == kM1I8;
     const int n_xchunks = static_cast<int>(ceil_div(a.K, kM1KC));
     const size_t x_all = x_whole ? static_cast<size_t>(n_xchunks) * 16 +
@@ -1182,9 +1234,10 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     // SM and the next launch's CTA streams its first stages while this one computes (C2: 6.4 us
     // against 7.1 with three stages).  Several passes: three stages and one CTA per SM, whose
     // deeper ring keeps the long stream in flight (1 x 32000 x 4096: 16.1 us against 17.9).
-    // BYBY_CUDA_GEMV_STAGES overrides (tuning).
+    // A tuned plan's depth (a.stages), then BYBY_CUDA_GEMV_STAGES, override.
     const int fit = stages;   // the most that fit in shared memory (and are useful)
     if (m1) stages = std::min(fit, tiles_max > tp ? 3 : 2);
+    if (a.stages >= 1) stages = std::min(fit, a.stages);
     if (const char* e = getenv("BYBY_CUDA_GEMV_STAGES")) {
         const int want_stages = atoi(e);
         if (want_stages >= 1) stages = std::min(fit, want_stages);
@@ -1235,10 +1288,10 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     const cudaStream_t st = a.stream;
     if (m1) {
         if (scale_tma)
-            return tpl == 2 ? launch_m1<2, true>(mode, maps, p, grid, smem, st)
-                            : launch_m1<5, true>(mode, maps, p, grid, smem, st);
-        return tpl == 2 ? launch_m1<2, false>(mode, maps, p, grid, smem, st)
-                        : launch_m1<5, false>(mode, maps, p, grid, smem, st);
+            return tpl == 2 ? launch_m1<2, true>(mode, xf32, maps, p, grid, smem, st)
+                            : launch_m1<5, true>(mode, xf32, maps, p, grid, smem, st);
+        return tpl == 2 ? launch_m1<2, false>(mode, xf32, maps, p, grid, smem, st)
+                        : launch_m1<5, false>(mode, xf32, maps, p, grid, smem, st);
     }
     if (ntn == 2) {
         return tpl == 2 ? dispatch_x<2, 2>(xf32, maps, p, grid, smem, st) : dispatch_x<5, 2>(xf32, maps, p, grid, smem, st);

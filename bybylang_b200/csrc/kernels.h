@@ -22,6 +22,11 @@ struct GemmArgs {
     int64_t out_ld = 0;
     int64_t out_col0 = 0;
     cudaStream_t stream = nullptr;
+    // Launch knobs of a tuned plan (tune.cu); the defaults leave each route's own choice.
+    // variant: the M = 1 Q4B32 GEMV's operand form (kM1*), or the format-1 GEMV's CTAs per SM.
+    // stages: the ring depth of the streamed weights (GEMV routes).
+    int variant = -1;
+    int stages = 0;
 };
 
 // Ranks of a column-sharded GEMM whose output slices are gathered over NVLink peer
@@ -89,5 +94,11 @@ int launch_tc_static_scratch(const GemmArgs& a);
 
 int launch_dequant(int fmt, int K, int N, const uint8_t* packed, int64_t scale_base,
                    const float* lut, float* w, cudaStream_t stream);
+
+// Tuned plans (tune.cu).  When the caller asked for the automatic route and a plan was
+// prepared for the shape on this device, the plan's route and knobs replace the built-in
+// choice - if that route can run these exact arguments; otherwise nothing changes.
+void apply_tile_gemm_plan(GemmArgs* a, int* route);
+void apply_q4_plan(int M, int K, int N, int group, int groups, bool fast, int* route, int* stages);
 
 }  // namespace bybycu

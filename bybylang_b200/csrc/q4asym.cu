@@ -394,6 +394,7 @@ struct Q4aFused {
     const float* res = nullptr;
     const float* gamma = nullptr;
     float eps = 0.0f;
+    int stages = 0;   // ring depth; 0 = the default (three, as many as fit)
 };
 
 int launch_q4a_fused(const Q4aFused& f, cudaStream_t stream) {
@@ -458,7 +459,7 @@ int launch_q4a_fused(const Q4aFused& f, cudaStream_t stream) {
     p.stage_bytes = (p.g_off + (p.has_norm ? kM1KC * 4 : 0) + 1023) / 1024 * 1024;
     const size_t tail = static_cast<size_t>(kM1Warps) * kQ4aTP * 16 * 4 + kM1Warps * 4 + rows * 4;   // red, sq, gate
     const size_t budget = static_cast<size_t>(dev.max_smem_optin) - 1024 - 64 - tail;
-    p.stages = std::min(kQ4aStages, static_cast<int>(budget / (p.stage_bytes + 16)));
+    p.stages = std::min(f.stages >= 2 ? f.stages : kQ4aStages, static_cast<int>(budget / (p.stage_bytes + 16)));
     if (p.stages < 2) return set_error(BYBYCU_ERR_SHAPE, "matmul_q4 decode: shared memory too small");
     const size_t smem = 1024 + static_cast<size_t>(p.stages) * (p.stage_bytes + 16) + 16 + tail;
 
@@ -518,8 +519,9 @@ int launch_q4a_fused(const Q4aFused& f, cudaStream_t stream) {
 }
 
 int launch_q4a(int K, int N, const float* x, const uint8_t* wq, const float* scales, const float* zeros, float* out,
-               cudaStream_t stream) {
+               cudaStream_t stream, int stages = 0) {
     Q4aFused f;
+    f.stages = stages;
     f.K = K;
     f.x = x;
     f.wq[0] = wq;
@@ -545,6 +547,8 @@ extern "C" int bybycu_matmul_q4(const float* a, const uint8_t* wq, const float* 
     if (route != BYBYCU_ROUTE_AUTO && route != BYBYCU_ROUTE_SIMT && route != BYBYCU_ROUTE_GEMV)
         return set_error(BYBYCU_ERR_ARGS, "matmul_q4: route %d (AUTO, SIMT or GEMV)", route);
     const bool fast = q4a_fast_supports(M, K, N, group_size, n_groups_per_row, a, wq, scales, zeros);
+    int stages = 0;
+    if (route == BYBYCU_ROUTE_AUTO) apply_q4_plan(M, K, N, group_size, n_groups_per_row, fast, &route, &stages);
     if (route == BYBYCU_ROUTE_GEMV && !fast)
         return set_error(BYBYCU_ERR_SHAPE, "matmul_q4: the decode route needs M=1, group 32, K %% 128 == 0 and "
                                            "16-byte aligned slots");
@@ -555,7 +559,7 @@ extern "C" int bybycu_matmul_q4(const float* a, const uint8_t* wq, const float* 
         BYBYCU_LAUNCH_CHECK("q4a_exact_kernel");
         return BYBYCU_OK;
     }
-    return launch_q4a(K, N, a, wq, scales, zeros, c, s);
+    return launch_q4a(K, N, a, wq, scales, zeros, c, s, stages);
 }
 
 extern "C" int bybycu_matmul_q4_fused(int mode, const float* a, int n_mats, const uint8_t* const* wq,

@@ -339,6 +339,12 @@ class Q4B32Weights:
         return tile_gemm(TileFormatQ4B32, x, self.packed, out, M=M, K=self.K, N=self.N,
                          scale_base=self.scale_base, route=route, stream=stream)
 
+    def prepare(self, M: int = 1, x_dtype: int = _lib.DT_BF16) -> bool:
+        """Autotunes the automatic route for M rows of x_dtype activations (residentPrepareQ4's
+        role)."""
+        return prepareTileGemmTuned(TileFormatQ4B32, self.packed, M=M, K=self.K, N=self.N,
+                                    scale_base=self.scale_base, x_dtype=x_dtype)
+
 
 # --------------------------------------------------------------------------------------
 # Asymmetric Q4 (matmul_q4: gpubackend.nim:806-843, 2871-3060; cpu_kernels_impl.inc:293-319)
@@ -388,9 +394,53 @@ def residentUploadQ4(backend: GpuBackend, wq, scales, zeros, k: int, n: int, gro
 
 
 def residentPrepareQ4(w: ResidentWeightHandle, M: int = 1) -> bool:
-    """gpubackend.nim:2871: ready for M rows.  The CUDA kernels read the uploaded layout as it
-    is, so there is nothing to prepare."""
-    return w.kind == GpuBackend.gbCuda and w.wq.ptr != 0 and M > 0
+    """gpubackend.nim:2871-2881 -> vulkanPrepareQ4Tuned (q4_autotune.nim:387-543): autotunes
+    the plan that sessionMatmulQ4 / gpuMatmulQ4 use for these weights at M rows (M = 1 the
+    decode plan, M > 1 the plan of M's power-of-two class), through the library's
+    parity-gated candidate timing and its JSON plan cache.  True when a plan is installed;
+    False when there is nothing to choose, tuning is switched off (BYBY_Q4_TUNED=0 or
+    BYBY_GPU_AUTOTUNE=0) or the handle is not a CUDA one."""
+    if w.kind != GpuBackend.gbCuda or not w.wq.ptr or M <= 0:
+        return False
+    prepared = C.c_int(0)
+    call("bybycu_prepare_q4_tuned", C.c_void_p(w.wq.ptr), C.c_void_p(w.scales.ptr), C.c_void_p(w.zeros.ptr),
+         int(M), w.k, w.n, w.groupSize, w.nGroupsPerRow, C.byref(prepared))
+    return bool(prepared.value)
+
+
+def prepareTileGemmTuned(fmt: int, packed, *, M: int, K: int, N: int, scale_base: int = 0,
+                         x_dtype: int = _lib.DT_BF16) -> bool:
+    """The tuner for the tile GEMM on resident `packed` weights (a torch device tensor):
+    installs the fastest parity-checked route and knobs for format `fmt` at M rows of
+    activations of type x_dtype (plans are kept per type)."""
+    prepared = C.c_int(0)
+    call("bybycu_prepare_tile_gemm_tuned", int(fmt), int(x_dtype), int(M), int(K), int(N), _ptr(packed),
+         packed.numel() * packed.element_size(), int(scale_base), C.byref(prepared))
+    return bool(prepared.value)
+
+
+def tunedPlan(op: int, *, M: int, K: int, N: int, fmt: int = 0, x_dtype: int = _lib.DT_BF16,
+              groupSize: int = 0, nGroupsPerRow: int = 0) -> "_lib.Plan | None":
+    """The plan installed for a shape on the current device, or None."""
+    plan, found = _lib.Plan(), C.c_int(0)
+    call("bybycu_plan_get", int(op), int(fmt), int(x_dtype), int(M), int(K), int(N), int(groupSize),
+         int(nGroupsPerRow), C.byref(plan), C.byref(found))
+    return plan if found.value else None
+
+
+def q4TuningStats() -> tuple[int, int]:
+    """vulkanQ4TuningStats (q4_autotune.nim:545-546): (installed plans, ROUTE_AUTO launches
+    that followed one)."""
+    n, d = C.c_int(0), C.c_int64(0)
+    call("bybycu_tuning_stats", C.byref(n), C.byref(d))
+    return n.value, d.value
+
+
+def tuneCachePath() -> str:
+    """The plan cache file of the current device ('' when caching is off)."""
+    buf = C.create_string_buffer(1024)
+    call("bybycu_tune_cache_path", buf, 1024)
+    return buf.value.decode()
 
 
 def residentFreeQ4(backend: GpuBackend, w: ResidentWeightHandle) -> None:
@@ -504,6 +554,13 @@ class Q4AsymWeights:
              self.N, self.group_size, self.n_groups, int(route), _stream_ptr(stream))
         return out
 
+    def prepare(self, M: int = 1) -> bool:
+        """Autotunes the automatic route for M rows (residentPrepareQ4's role)."""
+        prepared = C.c_int(0)
+        call("bybycu_prepare_q4_tuned", _ptr(self.wq), _ptr(self.scales), _ptr(self.zeros), int(M), self.K, self.N,
+             self.group_size, self.n_groups, C.byref(prepared))
+        return bool(prepared.value)
+
 
 __all__ = [
     "GpuBackend", "parseBackend", "normalizeBackend", "detectBackend", "ensureGpuInit",
@@ -513,5 +570,6 @@ __all__ = [
     "sessionF16GemmTile", "sessionQ4B32Gemm", "sessionTileGemmReady", "sessionMicroVmEnc",
     "tile_gemm", "route_for", "dequant", "Q4B32Weights", "tileWeightBytes", "TileFormatQ4B32",
     "ResidentWeightHandle", "residentUploadQ4", "residentPrepareQ4", "residentFreeQ4", "sessionMatmulQ4",
-    "gpuMatmulQ4", "Q4AsymWeights", "sessionMatmulQ4Fused", "matmul_q4_fused",
+    "gpuMatmulQ4", "Q4AsymWeights", "sessionMatmulQ4Fused", "matmul_q4_fused", "prepareTileGemmTuned",
+    "tunedPlan", "q4TuningStats", "tuneCachePath",
 ]

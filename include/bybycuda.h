@@ -207,6 +207,64 @@ BYBYCU_API int bybycu_session_matmul_q4_fused(int mode, const void* a, int n_mat
                                               void* const* outs, const void* res, const void* gamma, float eps,
                                               int K, int group_size, int n_groups_per_row);
 
+/* ---- tuned plans (the Q4 autotuner and its plan cache) ------------------------------ */
+
+/* A launch plan: the route and its knobs.  variant: the operand form of the M = 1 Q4B32 GEMV
+ * (0 bf16, 1 fp16, 2 s8 fixed point) or the CTAs per SM of the format-1 GEMV, -1 for the
+ * route's default; stages: the ring depth of a GEMV's weight stream, 0 for the default.
+ * Replaces VkQ4Plan (backends/vulkan/q4_autotune.nim:2-7). */
+typedef struct bybycu_plan {
+    int32_t route;     /* BYBYCU_ROUTE_SIMT, _GEMV or _TC */
+    int32_t variant;
+    int32_t stages;
+    float ms;          /* the tuner's median time per launch (0 when set by hand) */
+    char name[32];     /* the candidate's name, e.g. "gemv-s8-st2" */
+} bybycu_plan;
+
+#define BYBYCU_OP_TILE_GEMM 0   /* bybycu_tile_gemm, plans keyed by format, K, N and M class */
+#define BYBYCU_OP_MATMUL_Q4 1   /* bybycu_matmul_q4, keyed by K, N, group, groups and M class */
+
+/* Autotunes the asymmetric-Q4 matmul for these resident weights: every route and ring depth
+ * the device supports runs on the weights and the input x[i] = ((17 i) mod 101 - 50) / 64;
+ * candidates whose output differs from the exact kernel's by more than max(1e-5, 3e-3 of its
+ * peak) are dropped, the rest are timed (three rounds, median; a candidate must be 3% faster
+ * to win) and the winner becomes the plan of ROUTE_AUTO calls of this shape on this device.
+ * M = 1 tunes the decode plan; M > 1 the plan of M's power-of-two class (2 .. 128, larger M
+ * sharing the 128 plan).  Plans persist in <dir>/q4-plans-<hash of device, driver, library
+ * build and route switches>.json, dir = BYBY_CUDA_TUNE_DIR (0: no file), else
+ * $XDG_CACHE_HOME/bybylang_b200, else ~/.cache/bybylang_b200; a later process reads the plan
+ * back instead of tuning.  *prepared = 1 when a plan is installed, 0 when there is nothing to
+ * choose or BYBY_Q4_TUNED=0 / BYBY_GPU_AUTOTUNE=0.  Synchronous; allocates scratch (up to
+ * ~256 MiB of weight copies that keep the timing out of L2).  Replaces vulkanPrepareQ4Tuned
+ * (q4_autotune.nim:387-543), called by residentPrepareQ4 (gpubackend.nim:2871-2881). */
+BYBYCU_API int bybycu_prepare_q4_tuned(const uint8_t* wq, const float* scales, const float* zeros,
+                                       int M, int K, int N, int group_size, int n_groups_per_row,
+                                       int* prepared);
+
+/* The same for the tile GEMM of format `fmt` on device-resident `packed` weights, for
+ * activations of type x_dtype (BYBYCU_DT_F32 or _BF16: plans are kept per type).  Format 2:
+ * the routes SIMT, GEMV with each operand form and ring depth, TC; format 1: SIMT and the
+ * fp16 GEMV with 1-3 CTAs per SM; format 0 has one route and is never prepared. */
+BYBYCU_API int bybycu_prepare_tile_gemm_tuned(int fmt, int x_dtype, int M, int K, int N, const void* packed,
+                                              int64_t packed_len, int64_t scale_base, int* prepared);
+
+/* The installed plan of a shape on the current device (*found = 0 when none); group_size
+ * and n_groups_per_row matter for BYBYCU_OP_MATMUL_Q4 only, fmt and x_dtype for
+ * BYBYCU_OP_TILE_GEMM only. */
+BYBYCU_API int bybycu_plan_get(int op, int fmt, int x_dtype, int M, int K, int N, int group_size,
+                               int n_groups_per_row, bybycu_plan* plan, int* found);
+/* Installs `plan` for a shape by hand (NULL removes it); ROUTE_AUTO calls then use it where
+ * its route can run the call's arguments. */
+BYBYCU_API int bybycu_plan_set(int op, int fmt, int x_dtype, int M, int K, int N, int group_size,
+                               int n_groups_per_row, const bybycu_plan* plan);
+/* Drops every installed plan (the cache file stays) and zeroes the dispatch count. */
+BYBYCU_API int bybycu_plan_clear(void);
+/* Installed plans and the ROUTE_AUTO launches that followed one (vulkanQ4TuningStats,
+ * q4_autotune.nim:545-546). */
+BYBYCU_API int bybycu_tuning_stats(int* prepared_plans, int64_t* tuned_dispatches);
+/* The plan cache file of the current device ("" when caching is off). */
+BYBYCU_API int bybycu_tune_cache_path(char* buf, int buf_len);
+
 /* Device-pointer twin of nimf_cpu_vm_run_slots (backends/cpu/cpu_kernels.h:118-121,
  * cpu_vm.c:178-182): runs a micro-VM program whose first op is OP_TILE_GEMM (formats
  * 0/1/2, followed by the canonical tile ops), OP_FP4_COOP_GEMM, OP_Q4_GEMV or

@@ -119,3 +119,35 @@ def test_session_order_errors():
     lib = _lib.load()
     assert lib.bybycu_session_end() == _lib.ERR_SESSION
     assert lib.bybycu_session_q4b32_gemm(None, None, None, 1, 64, 16, 1) == _lib.ERR_SESSION
+
+
+def test_tuned_plan_table_host_checks(monkeypatch):
+    """The plan table and the tuner's argument checks answer before any device call."""
+    lib = _lib.load()
+    assert lib.bybycu_plan_clear() == 0
+    n, d = C.c_int(-1), C.c_int64(-1)
+    assert lib.bybycu_tuning_stats(C.byref(n), C.byref(d)) == 0 and (n.value, d.value) == (0, 0)
+    good = _lib.Plan(route=_lib.ROUTE_GEMV, variant=-1, stages=0, ms=0.0, name=b"x")
+    assert lib.bybycu_plan_set(7, 2, 0, 1, 64, 16, 0, 0, good) == _lib.ERR_ARGS
+    assert lib.bybycu_plan_set(_lib.OP_TILE_GEMM, 2, 0, 0, 64, 16, 0, 0, good) == _lib.ERR_SHAPE
+    for bad in (dict(route=_lib.ROUTE_AUTO), dict(variant=-2), dict(stages=9)):
+        p = _lib.Plan(route=bad.get("route", _lib.ROUTE_GEMV), variant=bad.get("variant", -1),
+                      stages=bad.get("stages", 0), ms=0.0, name=b"bad")
+        assert lib.bybycu_plan_set(_lib.OP_TILE_GEMM, 2, 0, 1, 64, 16, 0, 0, p) == _lib.ERR_ARGS, bad
+    tc = _lib.Plan(route=_lib.ROUTE_TC, variant=-1, stages=0, ms=0.0, name=b"tc")
+    assert lib.bybycu_plan_set(_lib.OP_MATMUL_Q4, 0, 0, 1, 64, 16, 32, 2, tc) == _lib.ERR_ARGS
+    prepared = C.c_int(-1)
+    vp = C.c_void_p(1 << 20)
+    assert lib.bybycu_prepare_q4_tuned(vp, vp, vp, 1, 64, 16, 32, 2, None) == _lib.ERR_ARGS
+    assert lib.bybycu_prepare_q4_tuned(vp, vp, vp, 1, 64, 16, 32, 1, C.byref(prepared)) == _lib.ERR_SHAPE
+    assert prepared.value == 0
+    assert lib.bybycu_prepare_tile_gemm_tuned(5, 0, 1, 64, 16, vp, 1 << 20, 512, C.byref(prepared)) == _lib.ERR_ARGS
+    assert lib.bybycu_prepare_tile_gemm_tuned(2, 7, 1, 64, 16, vp, 1 << 20, 512, C.byref(prepared)) == _lib.ERR_ARGS
+    assert lib.bybycu_prepare_tile_gemm_tuned(2, 0, 1, 64, 16, vp, 100, 512, C.byref(prepared)) == _lib.ERR_RANGE
+    # switched off: answered without a device
+    monkeypatch.setenv("BYBY_Q4_TUNED", "0")
+    prepared.value = -1
+    assert lib.bybycu_prepare_q4_tuned(vp, vp, vp, 1, 64, 16, 32, 2, C.byref(prepared)) == 0
+    assert prepared.value == 0
+    assert lib.bybycu_prepare_tile_gemm_tuned(2, 1, 1, 64, 16, vp, 1 << 20, 512, C.byref(prepared)) == 0
+    assert prepared.value == 0

@@ -150,10 +150,12 @@ def _bf16_bits(f):
     return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
 
 
+@pytest.mark.parametrize("xdt", ["bf16", "f32"])
 @pytest.mark.parametrize("K,N", [(4096, 2048), (800, 300)])
-def test_gemv_m1_activation_dynamic_range(K, N, oracle_mod):
+def test_gemv_m1_activation_dynamic_range(K, N, xdt, oracle_mod):
     """Activations over 36 binades, zeros, a lone outlier over tiny values, all-tiny blocks:
-    the decode kernel stays inside its fixed-point error bound against the f64 reference."""
+    the decode kernel stays inside its fixed-point error bound against the f64 reference,
+    for bf16 rows and for full-precision fp32 rows."""
     O = oracle_mod
     rng = np.random.default_rng(K + N)
     p, s = O.gen_q4b32(N, K, seed=77)
@@ -165,11 +167,11 @@ def test_gemv_m1_activation_dynamic_range(K, N, oracle_mod):
     xf[7 * 32:8 * 32] = 1e-30                       # a block of tiny values
     xf[9 * 32:10 * 32] = -2.0                       # equal values
     xb = _bf16_bits(xf).reshape(1, K)
-    x = O.bf16_to_f32(xb)
+    x = O.bf16_to_f32(xb) if xdt == "bf16" else xf.reshape(1, K)
     want = O.tile_gemm_q4b32_f64(x, p, s, 1, K, N)[0]
     slot, sb = q4_slot(p, s)
-    got = run(2, 1, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb,
-              route=_lib.ROUTE_GEMV).cpu().numpy()[0].astype(np.float64)
+    xd = dev(xb).view(torch.bfloat16) if xdt == "bf16" else dev(x)
+    got = run(2, 1, K, N, xd, slot, scale_base=sb, route=_lib.ROUTE_GEMV).cpu().numpy()[0].astype(np.float64)
     w = np.abs(O.dequant_q4b32(p, s, N, K).astype(np.float64))   # |q| * |s|
     xa = np.abs(x[0].astype(np.float64))
     blk_max = xa.reshape(-1, 32).max(axis=1)
@@ -179,6 +181,34 @@ def test_gemv_m1_activation_dynamic_range(K, N, oracle_mod):
     assert np.isfinite(got).all()
     assert (err <= quant + slack).all(), f"worst excess {(err - quant - slack).max():.3e}"
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("K,N", [(4096, 11008), (4192, 300), (1024, 64)])
+def test_gemv_m1_f32_rows_match_bf16_rows(K, N, oracle_mod):
+    """fp32 rows take the decode kernel's integer mode directly: a row of bf16 values gives
+    bit-identical outputs as fp32 and as bf16 (same exponents, same fixed-point digits)."""
+    O = oracle_mod
+    p, s = O.gen_q4b32(N, K, seed=K + 3)
+    xb = O.gen_x_bf16(1, K, seed=N)
+    slot, sb = q4_slot(p, s)
+    a = run(2, 1, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    b = run(2, 1, K, N, dev(O.bf16_to_f32(xb)), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert torch.equal(a, b)
+    assert_close(O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, 1, K, N), b.cpu().numpy(), what=f"K={K} N={N}")
+
+
+def test_gemv_m1_nonfinite_f32_activation_is_reported(oracle_mod):
+    O = oracle_mod
+    K, N = 2048, 256
+    p, s = O.gen_q4b32(N, K)
+    xf = O.gen_x_f32(1, K)
+    slot, sb = q4_slot(p, s)
+    x = dev(xf).clone()
+    x[0, 1500] = float("nan")
+    run(2, 1, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert _lib.device_error() == 7
+    out = run(2, 1, K, N, dev(xf), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert_close(O.tile_gemm_q4b32(xf, p, s, 1, K, N), out.cpu().numpy())
 
 
 def test_gemv_m1_nonfinite_activation_is_reported(oracle_mod):

@@ -50,6 +50,14 @@ class Plan(C.Structure):
                 f"variant={self.variant}, stages={self.stages}, ms={self.ms:.4f})")
 
 
+class TensorInfo(C.Structure):
+    """bybycu_tensor_info: one tensor of a checkpoint index."""
+    _fields_ = [("name", C.c_char * 256), ("name_len", C.c_int32), ("kind", C.c_int32), ("rank", C.c_int32),
+                ("scales", C.c_int32), ("shape", C.c_int64 * 8), ("offset", C.c_int64), ("bytes", C.c_int64),
+                ("scale_offset", C.c_int64), ("group_size", C.c_int32), ("eb", C.c_int32), ("mb", C.c_int32),
+                ("dtype", C.c_char * 16)]
+
+
 class BybyCudaError(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"[cuda] {message} (status {code})")
@@ -112,6 +120,12 @@ SIGNATURES = {
     "bybycu_plan_clear": [],
     "bybycu_tuning_stats": [C.POINTER(_i32), C.POINTER(_i64)],
     "bybycu_tune_cache_path": [C.c_char_p, _i32],
+    "bybycu_map_file": [C.c_char_p, C.POINTER(_vp), C.POINTER(_i64), C.POINTER(_vp)],
+    "bybycu_unmap_file": [_vp],
+    "bybycu_upload_host_range": [_vp, _vp, _i64],
+    "bybycu_session_upload_ptr": [_vp, _i64, C.POINTER(_vp)],
+    "bybycu_fingerprint": [_vp, _i64, C.c_char_p, _i32],
+    "bybycu_checkpoint_index": [C.c_char_p, C.POINTER(TensorInfo), _i32, C.POINTER(_i32)],
 }
 
 _lib = None

@@ -10,3 +10,4 @@
 #include "session.cu"
 #include "shard.cu"
 #include "tune.cu"
+#include "ingest.cu"

@@ -95,6 +95,10 @@ int launch_tc_static_scratch(const GemmArgs& a);
 int launch_dequant(int fmt, int K, int N, const uint8_t* packed, int64_t scale_base,
                    const float* lut, float* w, cudaStream_t stream);
 
+// Host -> device copy of a pageable (e.g. file-mapped) range through the staging engine of
+// ingest.cu; synchronous.
+int upload_host_range(void* dst, const void* src, int64_t bytes);
+
 // Tuned plans (tune.cu).  When the caller asked for the automatic route and a plan was
 // prepared for the shape on this device, the plan's route and knobs replace the built-in
 // choice - if that route can run these exact arguments; otherwise nothing changes.

@@ -217,10 +217,9 @@ int bybycu_session_upload(const void* host, int64_t bytes, void** handle) {
     if (!handle || bytes <= 0 || !host) return set_error(BYBYCU_ERR_ARGS, "sessionUpload: bad arguments");
     void* d = nullptr;
     BYBYCU_CUDA_TRY(cudaMalloc(&d, static_cast<size_t>(bytes)));
-    const cudaError_t e = cudaMemcpy(d, host, static_cast<size_t>(bytes), cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
+    if (int rc = upload_host_range(d, host, bytes)) {
         cudaFree(d);
-        return cuda_fail(e, "sessionUpload");
+        return rc;
     }
     {
         std::lock_guard<std::mutex> lock(g_handles_mu);
@@ -228,6 +227,10 @@ int bybycu_session_upload(const void* host, int64_t bytes, void** handle) {
     }
     *handle = d;
     return BYBYCU_OK;
+}
+
+int bybycu_session_upload_ptr(const void* host, int64_t bytes, void** handle) {
+    return bybycu_session_upload(host, bytes, handle);
 }
 
 int bybycu_session_alloc_scratch(int64_t n_floats, void** handle) {

@@ -45,6 +45,7 @@
 #include <tuple>
 #include <vector>
 
+#include "json.cuh"
 #include "kernels.h"
 
 #ifndef BYBYCU_SOURCE_HASH
@@ -176,108 +177,6 @@ int cache_path(int device, std::string* path) {
     return BYBYCU_OK;
 }
 
-// A JSON reader for the cache file: objects, strings, numbers and literals (arrays are
-// parsed and dropped).  Anything malformed makes the whole file count as absent.
-struct JVal {
-    enum Type { kNull, kNum, kStr, kObj, kOther } type = kNull;
-    double num = 0;
-    std::string str;
-    std::vector<std::pair<std::string, JVal>> obj;
-    const JVal* get(const char* k) const {
-        for (const auto& kv : obj)
-            if (kv.first == k) return &kv.second;
-        return nullptr;
-    }
-};
-
-struct JParser {
-    const char* p;
-    const char* end;
-    void ws() {
-        while (p < end && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p;
-    }
-    bool str(std::string* s) {
-        if (p >= end || *p != '"') return false;
-        ++p;
-        while (p < end && *p != '"') {
-            char c = *p++;
-            if (c == '\\') {
-                if (p >= end) return false;
-                const char e = *p++;
-                switch (e) {
-                    case 'n': c = '\n'; break;
-                    case 't': c = '\t'; break;
-                    case 'r': c = '\r'; break;
-                    case 'b': c = '\b'; break;
-                    case 'f': c = '\f'; break;
-                    case 'u':
-                        if (end - p < 4) return false;
-                        p += 4;
-                        c = '?';
-                        break;
-                    default: c = e;   // \" \\ \/
-                }
-            }
-            s->push_back(c);
-        }
-        if (p >= end) return false;
-        ++p;
-        return true;
-    }
-    bool value(JVal* v, int depth) {
-        if (depth > 16) return false;
-        ws();
-        if (p >= end) return false;
-        if (*p == '"') {
-            v->type = JVal::kStr;
-            return str(&v->str);
-        }
-        if (*p == '{' || *p == '[') {
-            const bool is_obj = *p == '{';
-            const char close = is_obj ? '}' : ']';
-            v->type = is_obj ? JVal::kObj : JVal::kOther;
-            ++p;
-            ws();
-            if (p < end && *p == close) { ++p; return true; }
-            for (;;) {
-                std::string k;
-                if (is_obj) {
-                    ws();
-                    if (!str(&k)) return false;
-                    ws();
-                    if (p >= end || *p != ':') return false;
-                    ++p;
-                }
-                JVal child;
-                if (!value(&child, depth + 1)) return false;
-                if (is_obj) v->obj.emplace_back(std::move(k), std::move(child));
-                ws();
-                if (p < end && *p == ',') { ++p; continue; }
-                if (p < end && *p == close) { ++p; return true; }
-                return false;
-            }
-        }
-        if (*p == '-' || (*p >= '0' && *p <= '9')) {
-            char* q = nullptr;
-            std::string tok(p, static_cast<size_t>(std::min<ptrdiff_t>(end - p, 64)));
-            v->num = strtod(tok.c_str(), &q);
-            if (q == tok.c_str()) return false;
-            p += q - tok.c_str();
-            v->type = JVal::kNum;
-            return true;
-        }
-        for (const char* lit : {"true", "false", "null"}) {
-            const size_t n = strlen(lit);
-            if (static_cast<size_t>(end - p) >= n && !strncmp(p, lit, n)) {
-                p += n;
-                v->type = JVal::kOther;
-                return true;
-            }
-        }
-        return false;
-    }
-};
-
 std::string json_escape(const std::string& s) {
     std::string o;
     for (char c : s) {
@@ -303,9 +202,8 @@ std::map<std::string, bybycu_plan>& cache_for(const std::string& path, const std
     size_t n;
     while ((n = fread(buf, 1, sizeof buf, f)) > 0 && text.size() < (size_t(8) << 20)) text.append(buf, n);
     fclose(f);
-    JParser jp{text.data(), text.data() + text.size()};
     JVal root;
-    if (!jp.value(&root, 0) || root.type != JVal::kObj) return plans;
+    if (!json_parse(text, &root) || root.type != JVal::kObj) return plans;
     const JVal* ver = root.get("version");
     const JVal* s = root.get("signature");
     const JVal* ps = root.get("plans");

@@ -443,6 +443,43 @@ def tuneCachePath() -> str:
     return buf.value.decode()
 
 
+def sessionUploadPrivatePtr(backend: GpuBackend, data: int, nbytes: int) -> SessionHandle:
+    """gpubackend.nim:2940-2959: a device copy of `nbytes` at host address `data` (a model
+    mapping or any host range), straight from there through the library's staging engine."""
+    _chosen(backend)
+    h = C.c_void_p()
+    call("bybycu_session_upload_ptr", C.c_void_p(data), int(nbytes), C.byref(h))
+    return SessionHandle(GpuBackend.gbCuda, CudaResidentTensor(h.value, int(nbytes)))
+
+
+def sessionWrapHostRange(backend: GpuBackend, data: int, nbytes: int) -> tuple[SessionHandle, int]:
+    """gpubackend.nim:2920-2938.  Wrapping host pages as a device buffer is for GPUs that share
+    system memory; a B200 reads HBM, so the handle is always empty (callers then copy with
+    sessionUploadPrivatePtr)."""
+    _chosen(backend)
+    return SessionHandle(GpuBackend.gbCuda, CudaResidentTensor()), 0
+
+
+def residentUploadQ4Mapped(backend: GpuBackend, wq: int, wqBytes: int, scales, zeros, k: int, n: int,
+                           groupSize: int, nGroupsPerRow: int) -> tuple[ResidentWeightHandle, bool]:
+    """gpubackend.nim:2961-2998: residentUploadQ4 for packed nibbles that live in a model
+    mapping at host address `wq`.  On a B200 (a dGPU) the nibbles are copied straight from the
+    mapping into HBM, never through an intermediate host buffer, so zeroCopy is False and the
+    mapping may be closed after the call.  Scales and zeros are small and copied."""
+    _chosen(backend)
+    if not _initialised:
+        ensureGpuInit(backend)
+    scales = np.ascontiguousarray(scales, np.float32).reshape(-1)
+    zeros = np.ascontiguousarray(zeros, np.float32).reshape(-1)
+    _q4_shape_check(int(wqBytes), scales.size, zeros.size, k, n, groupSize, nGroupsPerRow)
+    if not wq:
+        raise BybyCudaError(_lib.ERR_ARGS, "residentUploadQ4Mapped: wq is NULL")
+    w = ResidentWeightHandle(GpuBackend.gbCuda, sessionUploadPrivatePtr(backend, wq, wqBytes),
+                             sessionUpload(backend, scales), sessionUpload(backend, zeros), k, n, groupSize,
+                             nGroupsPerRow)
+    return w, False
+
+
 def residentFreeQ4(backend: GpuBackend, w: ResidentWeightHandle) -> None:
     for h in (w.wq, w.scales, w.zeros):
         if h.ptr:
@@ -571,5 +608,6 @@ __all__ = [
     "tile_gemm", "route_for", "dequant", "Q4B32Weights", "tileWeightBytes", "TileFormatQ4B32",
     "ResidentWeightHandle", "residentUploadQ4", "residentPrepareQ4", "residentFreeQ4", "sessionMatmulQ4",
     "gpuMatmulQ4", "Q4AsymWeights", "sessionMatmulQ4Fused", "matmul_q4_fused", "prepareTileGemmTuned",
-    "tunedPlan", "q4TuningStats", "tuneCachePath",
+    "tunedPlan", "q4TuningStats", "tuneCachePath", "sessionUploadPrivatePtr", "sessionWrapHostRange",
+    "residentUploadQ4Mapped",
 ]

@@ -207,6 +207,52 @@ BYBYCU_API int bybycu_session_matmul_q4_fused(int mode, const void* a, int n_mat
                                               void* const* outs, const void* res, const void* gamma, float eps,
                                               int K, int group_size, int n_groups_per_row);
 
+/* ---- weight ingestion ---------------------------------------------------------------- */
+
+/* Maps a checkpoint file read-only (openReadOnlyMapping, mapped_file.nim:10-13): *data and
+ * *size describe the whole file, *mapping is the handle for bybycu_unmap_file
+ * (unmapReadOnlyFile, mapped_file.nim:15-19).  The mapping outlives nothing it does not own:
+ * device copies made from it stay valid after the unmap. */
+BYBYCU_API int bybycu_map_file(const char* path, void** data, int64_t* size, void** mapping);
+BYBYCU_API int bybycu_unmap_file(void* mapping);
+
+/* Copies `bytes` of host memory - a file mapping or any pageable range - to device memory at
+ * dst, and returns when they have landed.  Pageable ranges of 4 MiB and more go through the
+ * library's pinned staging slots, several host threads at once (BYBY_CUDA_INGEST_THREADS,
+ * default one per host thread, at most 16), so page faults, memcpy and DMA overlap; BYBY_CUDA_INGEST=register pins the
+ * range in place instead where the OS allows.  The dGPU branch of residentUploadQ4Mapped
+ * (gpubackend.nim:2961-2998): "copied straight from the mapping, never through an
+ * intermediate" buffer of the caller's. */
+BYBYCU_API int bybycu_upload_host_range(void* dst, const void* src, int64_t bytes);
+
+/* sessionUploadPrivatePtr (gpubackend.nim:2940-2959): a new session handle holding a copy of
+ * `bytes` of host memory, by the same engine. */
+BYBYCU_API int bybycu_session_upload_ptr(const void* host, int64_t bytes, void** handle);
+
+/* The sampled content identity of fingerprint (probe_data.nim:11-17): "sample1-" and 16 hex
+ * digits of FNV-1a over the byte count and five 64-byte runs; out_len >= 25. */
+BYBYCU_API int bybycu_fingerprint(const void* data, int64_t bytes, char* out, int out_len);
+
+/* One tensor of a checkpoint index (ProbeTensor, probe_weights.nim:5-9). */
+typedef struct bybycu_tensor_info {
+    char name[256];          /* truncated when name_len >= 256 */
+    int32_t name_len;
+    int32_t kind;            /* NIMQ: the tensor's kind byte; NIMBIN: 0; safetensors: 0 for F32, else -1 */
+    int32_t rank;            /* <= 8 */
+    int32_t scales;          /* NIMQ: number of 8-byte scale entries at scale_offset */
+    int64_t shape[8];
+    int64_t offset, bytes;   /* the payload's byte range in the file */
+    int64_t scale_offset;
+    int32_t group_size, eb, mb;   /* NIMQ quantisation fields */
+    char dtype[16];          /* safetensors dtype ("F32", "BF16", "U8", ...); "" otherwise */
+} bybycu_tensor_info;
+
+/* The tensor index of a NIMQ2, NIMQ3, NIMBIN or .safetensors checkpoint from its headers
+ * alone (probeTensorIndex, probe_weights.nim:29-104, with its checks and messages; a
+ * safetensors shape of more than 8 dimensions is rejected).  Fills up to cap entries and
+ * sets *count to the number of tensors, so a caller may ask with cap = 0 first. */
+BYBYCU_API int bybycu_checkpoint_index(const char* path, bybycu_tensor_info* out, int cap, int* count);
+
 /* ---- tuned plans (the Q4 autotuner and its plan cache) ------------------------------ */
 
 /* A launch plan: the route and its knobs.  variant: the operand form of the M = 1 Q4B32 GEMV

@@ -18,6 +18,9 @@ fp32 out - through libbybycuda's GEMV route.  Algorithmic bytes per step: 25,362
 * q4_asym_decode  the asymmetric Q4 data of the reference's matmul_q4 (interleaved nibbles, fp32
               scales and zero points per 32-block, fp32 x) at the C2 shape through
               bybycu_matmul_q4's decode kernel: GB/s of its 0.75 B/weight, rotating sets > 4x L2.
+* decode_x_f32  the headline step with fp32 activations (the session API's type).
+* ingest      GB/s of a 1 GiB file mapping copied into HBM by bybycu_upload_host_range (the copy
+              of residentUploadQ4Mapped), host clock, beside a plain pageable copy.
 
 N > 1 GPUs (torchrun, one process per GPU): weak scaling.  Each rank owns an 11008-column
 shard of a [11008*N, 4096] Q4B32 projection and every step ends with the device-side
@@ -559,6 +562,85 @@ def main():
         except _lib.BybyCudaError as e:
             f16dec = {"error": str(e)}
 
+    # ---- the C2 decode with fp32 activation rows (the reference's own activation type)
+    dec32 = None
+    if world == 1 and not args.no_q4asym:
+        try:
+            x32 = x.float().contiguous()
+
+            def launch32(i):
+                w = weights[i % copies]
+                gb.tile_gemm(2, x32, w.packed, outs[i % copies], M=M_DEC, K=K_DEC, N=N_DEC,
+                             scale_base=w.scale_base, route=_lib.ROUTE_GEMV, stream=stream)
+            g32 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g32, stream=stream):
+                for i in range(copies):
+                    launch32(i)
+            reps = max(20, min(reps_t, 4000 // copies))
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    g32.replay()
+            stream.synchronize()
+            da, db = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            da.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(reps):
+                    g32.replay()
+            db.record(stream)
+            stream.synchronize()
+            assert _lib.device_error() == 0
+            d_us = da.elapsed_time(db) * 1e3 / (reps * copies)
+            dbytes = W_BYTES + K_DEC * 4 + N_DEC * 4
+            dec32 = {"value": round(dbytes / (d_us * 1e-6) / 1e9, 2), "unit": "GB/s", "us_per_launch": round(d_us, 3),
+                     "workload": "decode GEMV C2 with x fp32 (the session API's activation type), out fp32",
+                     "algorithmic_bytes": dbytes,
+                     "frac": round(dbytes / (d_us * 1e-6) / 1e9 / hbm_peak, 4), "peak_kind": peak_kind}
+            del g32
+        except _lib.BybyCudaError as e:
+            dec32 = {"error": str(e)}
+
+    # ---- weight ingestion: a checkpoint mapping copied into HBM (residentUploadQ4Mapped's copy)
+    ingest = None
+    if world == 1 and not args.no_q4asym:
+        import tempfile
+        from bybylang_b200.mapped_file import openReadOnlyMapping, unmapReadOnlyFile
+        path = None
+        try:
+            nbytes = 1 << 30
+            fd, path = tempfile.mkstemp(prefix="bybyb200_ingest_", suffix=".bin")
+            blk = np.random.default_rng(SEED).integers(0, 256, 64 << 20, dtype=np.uint8).tobytes()
+            with os.fdopen(fd, "wb") as f:
+                for _ in range(nbytes // len(blk)):
+                    f.write(blk)
+            dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            m = openReadOnlyMapping(path)
+            try:
+                rates = []
+                for _ in range(3):
+                    torch.cuda.synchronize()
+                    t0 = time.perf_counter()
+                    _lib.call("bybycu_upload_host_range", C.c_void_p(dst.data_ptr()), C.c_void_p(m.data), nbytes)
+                    rates.append(nbytes / (time.perf_counter() - t0) / 1e9)
+                ok = torch.equal(dst[:len(blk)], torch.from_numpy(np.frombuffer(blk, np.uint8).copy()).to(dev))
+                src = torch.from_numpy(m.view())   # pageable: the driver's own staging
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                dst.copy_(src)
+                torch.cuda.synchronize()
+                plain = nbytes / (time.perf_counter() - t0) / 1e9
+            finally:
+                unmapReadOnlyFile(m)
+            ingest = {"value": round(max(rates), 2), "unit": "GB/s", "runs": [round(r, 2) for r in rates],
+                      "workload": "1 GiB file mapping -> HBM through bybycu_upload_host_range (staged, "
+                                  f"{os.cpu_count()} host threads), page cache warm, host clock",
+                      "plain_pageable_copy_gbs": round(plain, 2), "bit_exact": bool(ok)}
+            del dst
+        except Exception as e:   # an I/O problem on the box must not cost the decode numbers
+            ingest = {"error": str(e)}
+        finally:
+            if path and os.path.exists(path):
+                os.unlink(path)
+
     if rank == 0:
         base = None
         if not args.no_cpu_baseline and world == 1:   # the host-core baseline: rank 0 at N = 1 only
@@ -584,6 +666,8 @@ def main():
             "prefill": prefill,
             "q4_asym_decode": q4asym,
             "f16_decode": f16dec,
+            "decode_x_f32": dec32,
+            "ingest": ingest,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

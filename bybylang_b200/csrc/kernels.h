@@ -91,6 +91,12 @@ bool tc_supports(const GemmArgs& a);
 int launch_tc(const GemmArgs& a);
 // The same route staging its activations in a fixed module array instead of pool memory.
 int launch_tc_static_scratch(const GemmArgs& a);
+// The asymmetric-Q4 form of the tensor-core route (matmul_q4 prefill): fp32 x [M, K],
+// interleaved nibbles [N, K/2], fp32 scales and zero points [N, K/32], fp32 out [M, N].
+bool tc_asym_supports(int M, int K, int N, int group, int n_groups, const void* x, const void* wq, const void* scales,
+                      const void* zeros, const void* out);
+int launch_tc_asym(int M, int K, int N, const float* x, const uint8_t* wq, const float* scales, const float* zeros,
+                   float* out, cudaStream_t stream);
 
 int launch_dequant(int fmt, int K, int N, const uint8_t* packed, int64_t scale_base,
                    const float* lut, float* w, cudaStream_t stream);
@@ -103,6 +109,6 @@ int upload_host_range(void* dst, const void* src, int64_t bytes);
 // prepared for the shape on this device, the plan's route and knobs replace the built-in
 // choice - if that route can run these exact arguments; otherwise nothing changes.
 void apply_tile_gemm_plan(GemmArgs* a, int* route);
-void apply_q4_plan(int M, int K, int N, int group, int groups, bool fast, int* route, int* stages);
+void apply_q4_plan(int M, int K, int N, int group, int groups, bool fast, bool tc, int* route, int* stages);
 
 }  // namespace bybycu

@@ -544,16 +544,26 @@ extern "C" int bybycu_matmul_q4(const float* a, const uint8_t* wq, const float* 
     if (n_groups_per_row < groups_needed)
         return set_error(BYBYCU_ERR_SHAPE, "matmul_q4: %d groups per row, K=%d with group %d needs %lld", n_groups_per_row,
                          K, group_size, static_cast<long long>(groups_needed));
-    if (route != BYBYCU_ROUTE_AUTO && route != BYBYCU_ROUTE_SIMT && route != BYBYCU_ROUTE_GEMV)
-        return set_error(BYBYCU_ERR_ARGS, "matmul_q4: route %d (AUTO, SIMT or GEMV)", route);
+    if (route != BYBYCU_ROUTE_AUTO && route != BYBYCU_ROUTE_SIMT && route != BYBYCU_ROUTE_GEMV &&
+        route != BYBYCU_ROUTE_TC)
+        return set_error(BYBYCU_ERR_ARGS, "matmul_q4: route %d (AUTO, SIMT, GEMV or TC)", route);
     const bool fast = q4a_fast_supports(M, K, N, group_size, n_groups_per_row, a, wq, scales, zeros);
+    const bool tc = M > 1 && tc_asym_supports(M, K, N, group_size, n_groups_per_row, a, wq, scales, zeros, c);
     int stages = 0;
-    if (route == BYBYCU_ROUTE_AUTO) apply_q4_plan(M, K, N, group_size, n_groups_per_row, fast, &route, &stages);
+    if (route == BYBYCU_ROUTE_AUTO) {
+        apply_q4_plan(M, K, N, group_size, n_groups_per_row, fast, tc, &route, &stages);
+        // no plan: the decode kernel at M = 1, the tensor-core GEMM above, else the exact kernel
+        if (route == BYBYCU_ROUTE_AUTO) route = fast ? BYBYCU_ROUTE_GEMV : tc ? BYBYCU_ROUTE_TC : BYBYCU_ROUTE_SIMT;
+    }
     if (route == BYBYCU_ROUTE_GEMV && !fast)
         return set_error(BYBYCU_ERR_SHAPE, "matmul_q4: the decode route needs M=1, group 32, K %% 128 == 0 and "
                                            "16-byte aligned slots");
+    if (route == BYBYCU_ROUTE_TC && !tc)
+        return set_error(BYBYCU_ERR_SHAPE, "matmul_q4: the tensor-core route needs M > 1, group 32, K %% 256 == 0 "
+                                           "and 16-byte aligned slots");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (route == BYBYCU_ROUTE_SIMT || !fast) {
+    if (route == BYBYCU_ROUTE_TC) return launch_tc_asym(M, K, N, a, wq, scales, zeros, c, s);
+    if (route == BYBYCU_ROUTE_SIMT) {
         dim3 grid(static_cast<unsigned>(ceil_div(N, 128)), static_cast<unsigned>(M));
         q4a_exact_kernel<<<grid, 128, 0, s>>>(M, K, N, group_size, n_groups_per_row, wq, scales, zeros, a, c);
         BYBYCU_LAUNCH_CHECK("q4a_exact_kernel");

@@ -20,6 +20,12 @@
 //     the accumulators are double-buffered, so the epilogue warps read tile t back
 //     (tcgen05.ld) and store out[token][feature] while the MMAs of tile t+1 run.
 //
+// The same kernel, instantiated with ASYM, is the prefill route of the asymmetric Q4 matmul
+// (matmul_q4, backends/cpu/cpu_kernels_impl.inc:293-319, whose Vulkan prefill runs on the
+// cooperative-matrix units): interleaved nibbles (byte j holds k = 2j low, 2j + 1 high),
+// fp32 scales and zero points per 32-block, each weight dequantised as w = RNE16(u * s - z * s)
+// with the fp32 FMA rounding once before the one rounding to fp16.
+//
 // Every wait is bounded (%globaltimer): on a timeout the kernel records an error code in
 // g_device_error, drains its copies and MMAs, frees its tensor memory and returns.
 #include "kernels.h"
@@ -59,8 +65,6 @@ static_assert(kStages % kASlots == 0 && kASlots % 2 == 0, "stage i uses A slot i
 
 constexpr uint32_t kOffX = 0;
 constexpr uint32_t kOffW = kOffX + kStages * kXStageBytes;
-constexpr uint32_t kOffS = kOffW + kWStages * kWStageBytes;
-constexpr uint32_t kOffBar = kOffS + kWStages * kSStageBytes;
 // barriers: full, x_empty [kStages]; a_empty [kASlots]; w_full, w_empty [kWStages];
 // d_full, d_empty [2]; done; then the TMEM base address and the abort flag
 constexpr uint32_t kNumBars = 2 * kStages + kASlots + 2 * kWStages + 5;
@@ -69,11 +73,21 @@ constexpr uint32_t kNumBars = 2 * kStages + kASlots + 2 * kWStages + 5;
 // every shared-memory access of that thread stalls it for ~140 cycles while the tensor core
 // streams operands, so it makes one per eight MMAs.
 constexpr uint32_t kFullArrivals = 1 + 1 + 8;
-constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
-constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
-constexpr uint32_t kSmemBytes = kOffAbort + 4 + 1024;  // + alignment slack
-// more than half an SM's shared memory: one CTA per SM, whatever the register count
-static_assert(kSmemBytes > 116 * 1024, "one CTA per SM");
+// The rest of the layout depends on the weight format: a scale stage holds fp16 scales
+// (Q4B32) or fp32 scales followed by fp32 zero points (asymmetric Q4) of 128 rows x 8 blocks.
+template <bool ASYM>
+struct Lay {
+    static constexpr uint32_t kSBytes = ASYM ? 2 * kRowsCta * (kWK / 32) * 4 : kSStageBytes;
+    static constexpr uint32_t kZOff = kSBytes / 2;    // zero points inside an asymmetric scale stage
+    static constexpr uint32_t kOffS = kOffW + kWStages * kWStageBytes;
+    static constexpr uint32_t kOffBar = kOffS + kWStages * kSBytes;
+    static constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
+    static constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
+    static constexpr uint32_t kSmemBytes = kOffAbort + 4 + 1024;  // + alignment slack
+    // more than half an SM's shared memory: one CTA per SM, whatever the register count
+    static_assert(kSmemBytes > 116 * 1024 && kSmemBytes <= 227 * 1024, "one CTA per SM");
+};
+constexpr uint32_t kSmemBytes = Lay<false>::kSmemBytes;
 
 // Instruction descriptor of kind::f16: D fp32, A and B fp16, both K-major, M=256, N=128.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(kBN >> 3) << 17) |
@@ -82,7 +96,8 @@ constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(kBN >
 struct Maps {
     CUtensorMap x;   // fp16 [M, K], box 64 (K) x 64 (tokens), 128-byte swizzle
     CUtensorMap w;   // u8 [N, K/2], box 128 x 128, 128-byte swizzle
-    CUtensorMap s;   // u16 [N, K/32], box 8 x 128
+    CUtensorMap s;   // u16 [N, K/32] (asymmetric: fp32), box 8 x 128
+    CUtensorMap z;   // asymmetric only: fp32 zero points [N, K/32], box 8 x 128
 };
 
 struct Params {
@@ -260,6 +275,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 // so MMA position kk = 2*col + half of a block reads activation k = kPerm[kk]; the pre-pass
 // writes the activations in that order.
 // ---------------------------------------------------------------------------------------
+// Asymmetric nibbles (byte j holds k = 2j low, 2j + 1 high) through the same extraction:
+//   col 4w+0: low nibbles of bytes 4w, 4w+2  -> k = 8w,   8w+4
+//   col 4w+1: high nibbles of bytes 4w, 4w+2 -> k = 8w+1, 8w+5
+//   col 4w+2: low nibbles of bytes 4w+1, 4w+3 -> k = 8w+2, 8w+6
+//   col 4w+3: high nibbles of bytes 4w+1, 4w+3 -> k = 8w+3, 8w+7
+__host__ __device__ constexpr int perm_src_asym(int kk) { return (kk & ~7) + ((kk & 7) >> 1) + 4 * (kk & 1); }
+
 __host__ __device__ constexpr int perm_src(int kk) {
     // kk = 8w + p  ->  source k inside the 32-block
     return (kk & 7) == 0 ? 4 * (kk >> 3)
@@ -287,11 +309,25 @@ __device__ __forceinline__ void dequant_word(uint32_t v, __half2 s, __half2 s16,
     col[3] = h2_bits(__hmul2(__hsub2(bits_h2((vh & 0x00F000F0u) ^ 0x64806480u), m_hi), s16));
 }
 
+// One packed word of asymmetric nibbles -> four fp16x2 columns of w = RNE16(fma(u, s, -z s)).
+// lo4 / hi4 hold the word's low / high nibbles one per byte; a byte permute puts nibble u
+// under the exponent of 2^23, and subtracting 2^23 leaves u exactly.
+__device__ __forceinline__ float asym_nib(uint32_t nibs, uint32_t sel) {
+    return __uint_as_float(__byte_perm(nibs, 0x4B000000u, sel)) - 8388608.0f;
+}
+__device__ __forceinline__ void dequant_word_asym(uint32_t v, float s, float mzs, uint32_t* col) {
+    const uint32_t lo4 = v & 0x0F0F0F0Fu, hi4 = (v >> 4) & 0x0F0F0F0Fu;
+    col[0] = h2_bits(__floats2half2_rn(fmaf(asym_nib(lo4, 0x7650), s, mzs), fmaf(asym_nib(lo4, 0x7652), s, mzs)));
+    col[1] = h2_bits(__floats2half2_rn(fmaf(asym_nib(hi4, 0x7650), s, mzs), fmaf(asym_nib(hi4, 0x7652), s, mzs)));
+    col[2] = h2_bits(__floats2half2_rn(fmaf(asym_nib(lo4, 0x7651), s, mzs), fmaf(asym_nib(lo4, 0x7653), s, mzs)));
+    col[3] = h2_bits(__floats2half2_rn(fmaf(asym_nib(hi4, 0x7651), s, mzs), fmaf(asym_nib(hi4, 0x7653), s, mzs)));
+}
+
 // ---------------------------------------------------------------------------------------
-// Pre-pass: activations (bf16 or fp32) -> fp16 in the permuted K order.  One thread per
-// 32-block.  Values outside the fp16 range are recorded as a device error.
+// Pre-pass: activations (bf16 or fp32) -> fp16 in the permuted K order of the weight format.
+// One thread per 32-block.  Values outside the fp16 range are recorded as a device error.
 // ---------------------------------------------------------------------------------------
-template <bool XF32>
+template <bool XF32, bool ASYM = false>
 __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x, uint4* __restrict__ xp,
                                                       int64_t nblocks) {
     pdl_launch_dependents();   // the GEMM may start its prologue; it waits before reading xp
@@ -322,7 +358,8 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x
     uint32_t o[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-        const float a = v[perm_src(2 * c)], b = v[perm_src(2 * c + 1)];
+        const float a = v[ASYM ? perm_src_asym(2 * c) : perm_src(2 * c)];
+        const float b = v[ASYM ? perm_src_asym(2 * c + 1) : perm_src(2 * c + 1)];
         range_ok &= fabsf(a) < 65520.0f && fabsf(b) < 65520.0f;
         o[c] = h2_bits(__floats2half2_rn(a, b));
     }
@@ -335,12 +372,14 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x
 // ---------------------------------------------------------------------------------------
 // The GEMM kernel (launched as clusters of two CTAs; rank 0 issues the MMAs)
 // ---------------------------------------------------------------------------------------
+template <bool ASYM>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
+    using L = Lay<ASYM>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* smem = smem_raw + (base - raw);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
     // full[s]: on rank 0 the whole stage is ready (both activation halves, both A slots);
     // on rank 1 its own activation half landed (its relay forwards that to rank 0)
     uint64_t* full = bars;
@@ -351,8 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     uint64_t* d_full = w_empty + kWStages;       // [2] accumulator buffer complete
     uint64_t* d_empty = d_full + 2;              // [2] (rank 0) both epilogues read it
     uint64_t* done_bar = d_full + 4;
-    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + kOffTmemSlot);
-    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kOffAbort);
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::kOffTmemSlot);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
 
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
@@ -436,6 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (lane == 0) {
             prefetch_tensormap(&maps.w);
             prefetch_tensormap(&maps.s);
+            if constexpr (ASYM) prefetch_tensormap(&maps.z);
             const uint64_t policy = l2_policy_evict_last();
             int issued = 0;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
@@ -448,9 +488,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         break;
                     }
                     if (*s_abort) break;
-                    mbar_arrive_expect_tx(&w_full[s], kWStageBytes + kSStageBytes);
+                    mbar_arrive_expect_tx(&w_full[s], kWStageBytes + L::kSBytes);
                     tma_load_2d_hint(smem + kOffW + s * kWStageBytes, &maps.w, &w_full[s], kw * (kWK / 2), row0, policy);
-                    tma_load_2d_hint(smem + kOffS + s * kSStageBytes, &maps.s, &w_full[s], kw * (kWK / 32), row0, policy);
+                    tma_load_2d_hint(smem + L::kOffS + s * L::kSBytes, &maps.s, &w_full[s], kw * (kWK / 32), row0, policy);
+                    if constexpr (ASYM)
+                        tma_load_2d_hint(smem + L::kOffS + s * L::kSBytes + L::kZOff, &maps.z, &w_full[s], kw * (kWK / 32),
+                                         row0, policy);
                     ++issued;
                 }
             }
@@ -533,7 +576,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 uint4 chunk[4];
 #pragma unroll
                 for (int h = 0; h < 4; ++h) chunk[h] = lds_u128(wrow + (((4 * grp + h) ^ (row & 7)) << 4));
-                const uint4 sc = lds_u128(base + kOffS + ws * kSStageBytes + row * 16);
+                uint4 sc;
+                float4 sa, za;   // asymmetric: fp32 scales and zero points of blocks 4 grp .. 4 grp + 3
+                if constexpr (ASYM) {
+                    const uint32_t sb = base + L::kOffS + ws * L::kSBytes + row * 32 + grp * 16;
+                    sa = lds_v4f(sb);
+                    za = lds_v4f(sb + L::kZOff);
+                } else {
+                    sc = lds_u128(base + L::kOffS + ws * L::kSBytes + row * 16);
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&w_empty[ws]);
                 ++w_used;
@@ -544,6 +595,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 ok = __all_sync(0xffffffffu, ok && !*s_abort);
                 if (!ok) break;
                 tc_fence_after();
+                if constexpr (ASYM) {
+                    const float sv[4] = {sa.x, sa.y, sa.z, sa.w};
+                    const float mz[4] = {-za.x * sa.x, -za.y * sa.y, -za.z * sa.z, -za.w * sa.w};
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        uint32_t col[32];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int blk = 2 * half + h;
+                            const uint4 u = chunk[blk];
+                            dequant_word_asym(u.x, sv[blk], mz[blk], &col[16 * h + 0]);
+                            dequant_word_asym(u.y, sv[blk], mz[blk], &col[16 * h + 4]);
+                            dequant_word_asym(u.z, sv[blk], mz[blk], &col[16 * h + 8]);
+                            dequant_word_asym(u.w, sv[blk], mz[blk], &col[16 * h + 12]);
+                        }
+                        tmem_st32(tmem + lane_addr + kAOff + slot * kACols + half * 32, col);
+                    }
+                } else {
                 // scales of blocks 4 grp .. 4 grp + 3: two 32-bit words of the row's eight
                 const uint32_t sw0 = grp ? sc.z : sc.x, sw1 = grp ? sc.w : sc.y;
 #pragma unroll
@@ -561,6 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         dequant_word(u.w, sv, s16, &col[16 * h + 12]);
                     }
                     tmem_st32(tmem + lane_addr + kAOff + slot * kACols + half * 32, col);
+                }
                 }
                 tc_wait_st();
                 tc_fence_before();
@@ -666,20 +736,18 @@ static int scratch_pool(int device, cudaMemPool_t* pool) {
 }
 
 
-// Checks, device info, the kernel attribute and the number of CTA pairs that fit at once.
-static int tc_prepare(const GemmArgs& a, DeviceInfo* info, int* max_pairs) {
-    if (!tc_supports(a))
-        return set_error(BYBYCU_ERR_SHAPE,
-                         "tensor-core route needs format 2, K %% 256 == 0, 16-byte aligned x, packed and scales "
-                         "(M=%d K=%d N=%d)", a.M, a.K, a.N);
+// Device info, the kernel attribute and the number of CTA pairs that fit at once.
+template <bool ASYM>
+static int tc_setup(DeviceInfo* info, int* max_pairs) {
     if (int rc = current_device_info(info)) return rc;
     static std::once_flag once[16];
     static cudaError_t prep_rc[16];
     static int pairs[16];
     const int dev = info->device & 15;
+    constexpr uint32_t smem = tc::Lay<ASYM>::kSmemBytes;
     std::call_once(once[dev], [&] {
-        prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(tc::kSmemBytes));
+        prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel<ASYM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem));
         if (prep_rc[dev] != cudaSuccess) return;
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
@@ -689,10 +757,10 @@ static int tc_prepare(const GemmArgs& a, DeviceInfo* info, int* max_pairs) {
         attr[0].val.clusterDim.z = 1;
         cfg.gridDim = dim3(2 * (info->sm_count / 2));
         cfg.blockDim = dim3(tc::kThreads);
-        cfg.dynamicSmemBytes = tc::kSmemBytes;
+        cfg.dynamicSmemBytes = smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        prep_rc[dev] = cudaOccupancyMaxActiveClusters(&pairs[dev], tc::gemm_kernel, &cfg);
+        prep_rc[dev] = cudaOccupancyMaxActiveClusters(&pairs[dev], tc::gemm_kernel<ASYM>, &cfg);
     });
     if (prep_rc[dev] != cudaSuccess) return cuda_fail(prep_rc[dev], "tensor-core GEMM set-up");
     if (pairs[dev] < 1) return set_error(BYBYCU_ERR_DEVICE, "no CTA pair of the tensor-core GEMM fits on the device");
@@ -700,29 +768,51 @@ static int tc_prepare(const GemmArgs& a, DeviceInfo* info, int* max_pairs) {
     return BYBYCU_OK;
 }
 
+static int tc_prepare(const GemmArgs& a, DeviceInfo* info, int* max_pairs) {
+    if (!tc_supports(a))
+        return set_error(BYBYCU_ERR_SHAPE,
+                         "tensor-core route needs format 2, K %% 256 == 0, 16-byte aligned x, packed and scales "
+                         "(M=%d K=%d N=%d)", a.M, a.K, a.N);
+    return tc_setup<false>(info, max_pairs);
+}
+
+// The weights of one tensor-core GEMM: Q4B32 (nibbles and fp16 scales in `packed`) or
+// asymmetric Q4 (nibbles, fp32 scales, fp32 zero points).
+struct TcWeights {
+    const uint8_t* nibbles = nullptr;
+    const void* scales = nullptr;
+    const float* zeros = nullptr;
+};
+
 // The staging pass and the GEMM, with `xp` (M * K fp16) as the staging buffer.  Allocates
 // nothing.
-static int tc_run(const GemmArgs& a, int max_pairs, void* xp) {
+template <bool ASYM>
+static int tc_run(const GemmArgs& a, const TcWeights& wt, int max_pairs, void* xp) {
     const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
     const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
     if (a.x_dtype == BYBYCU_DT_F32)
-        tc::stage_x_kernel<true><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+        tc::stage_x_kernel<true, ASYM><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
     else
-        tc::stage_x_kernel<false><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+        tc::stage_x_kernel<false, ASYM><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
     BYBYCU_LAUNCH_CHECK("stage_x_kernel");
 
     tc::Maps maps;
+    memset(&maps, 0, sizeof maps);
+    const uint64_t G = static_cast<uint64_t>(a.K / 32);
     int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xp, a.K, a.M,
                                   static_cast<uint64_t>(a.K) * 2, tc::kXSub, tc::kTokCta, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (!rc)
-        rc = encode_tensor_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.packed, a.K / 2, a.N, a.K / 2,
+        rc = encode_tensor_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wt.nibbles, a.K / 2, a.N, a.K / 2,
                                   tc::kWK / 2, tc::kRowsCta, CU_TENSOR_MAP_SWIZZLE_128B,
                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (!rc)
-        rc = encode_tensor_map_2d(&maps.s, CU_TENSOR_MAP_DATA_TYPE_UINT16, a.packed + a.scale_base, a.K / 32, a.N,
-                                  static_cast<uint64_t>(a.K / 32) * 2, tc::kWK / 32, tc::kRowsCta,
+        rc = encode_tensor_map_2d(&maps.s, ASYM ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                                  wt.scales, G, a.N, G * (ASYM ? 4 : 2), tc::kWK / 32, tc::kRowsCta,
                                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+    if (!rc && ASYM)
+        rc = encode_tensor_map_2d(&maps.z, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, wt.zeros, G, a.N, G * 4, tc::kWK / 32,
+                                  tc::kRowsCta, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
     if (rc) return rc;
     tc::Params p;
     p.M = a.M;
@@ -749,11 +839,26 @@ static int tc_run(const GemmArgs& a, int max_pairs, void* xp) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(tc::kThreads);
-    cfg.dynamicSmemBytes = tc::kSmemBytes;
+    cfg.dynamicSmemBytes = tc::Lay<ASYM>::kSmemBytes;
     cfg.stream = a.stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel, maps, p));
+    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel<ASYM>, maps, p));
+    return BYBYCU_OK;
+}
+
+// Stages through stream-ordered pool scratch and runs the GEMM.
+template <bool ASYM>
+static int tc_pooled(const GemmArgs& a, const TcWeights& wt, const DeviceInfo& info, int max_pairs) {
+    const size_t xp_bytes = static_cast<size_t>(a.M) * a.K * 2;
+    void* xp = nullptr;
+    cudaMemPool_t pool = nullptr;
+    if (int rc = scratch_pool(info.device, &pool)) return rc;
+    BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
+    const int rc = tc_run<ASYM>(a, wt, max_pairs, xp);
+    const cudaError_t fe = cudaFreeAsync(xp, a.stream);
+    if (rc) return rc;
+    if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc scratch)");
     return BYBYCU_OK;
 }
 
@@ -761,17 +866,42 @@ int launch_tc(const GemmArgs& a) {
     DeviceInfo info;
     int max_pairs = 0;
     if (int rc = tc_prepare(a, &info, &max_pairs)) return rc;
-    // activations -> fp16, permuted, in stream-ordered scratch
-    const size_t xp_bytes = static_cast<size_t>(a.M) * a.K * 2;
-    void* xp = nullptr;
-    cudaMemPool_t pool = nullptr;
-    if (int rc = scratch_pool(info.device, &pool)) return rc;
-    BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
-    const int rc = tc_run(a, max_pairs, xp);
-    const cudaError_t fe = cudaFreeAsync(xp, a.stream);
-    if (rc) return rc;
-    if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc scratch)");
-    return BYBYCU_OK;
+    TcWeights wt;
+    wt.nibbles = a.packed;
+    wt.scales = a.packed + a.scale_base;
+    return tc_pooled<false>(a, wt, info, max_pairs);
+}
+
+bool tc_asym_supports(int M, int K, int N, int group, int n_groups, const void* x, const void* wq, const void* scales,
+                      const void* zeros, const void* out) {
+    if (group != 32 || n_groups != K / 32 || K < tc::kWK || K % tc::kWK != 0 || M < 1 || N < 1) return false;
+    for (const void* ptr : {x, wq, scales, zeros})
+        if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return false;
+    if (reinterpret_cast<uintptr_t>(out) % 4 != 0) return false;
+    DeviceInfo info;
+    if (current_device_info(&info) != BYBYCU_OK) return false;
+    return info.cc_major == 10 && info.max_smem_optin >= static_cast<int>(tc::Lay<true>::kSmemBytes);
+}
+
+int launch_tc_asym(int M, int K, int N, const float* x, const uint8_t* wq, const float* scales, const float* zeros,
+                   float* out, cudaStream_t stream) {
+    if (!tc_asym_supports(M, K, N, 32, K / 32, x, wq, scales, zeros, out))
+        return set_error(BYBYCU_ERR_SHAPE, "matmul_q4 tensor-core route needs group 32, K %% 256 == 0 and 16-byte "
+                                           "aligned slots (M=%d K=%d N=%d)", M, K, N);
+    DeviceInfo info;
+    int max_pairs = 0;
+    if (int rc = tc_setup<true>(&info, &max_pairs)) return rc;
+    GemmArgs a;
+    a.M = M; a.K = K; a.N = N;
+    a.x = x; a.x_dtype = BYBYCU_DT_F32;
+    a.out = out; a.out_dtype = BYBYCU_DT_F32;
+    a.out_ld = N; a.out_col0 = 0;
+    a.stream = stream;
+    TcWeights wt;
+    wt.nibbles = wq;
+    wt.scales = scales;
+    wt.zeros = zeros;
+    return tc_pooled<true>(a, wt, info, max_pairs);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -808,7 +938,10 @@ int launch_tc_static_scratch(const GemmArgs& a) {
     if (int rc = tc_prepare(a, &info, &max_pairs)) return rc;
     void* xp = nullptr;
     if (int rc = static_scratch(info.device, &xp)) return rc;
-    return tc_run(a, max_pairs, xp);
+    TcWeights wt;
+    wt.nibbles = a.packed;
+    wt.scales = a.packed + a.scale_base;
+    return tc_run<false>(a, wt, max_pairs, xp);
 }
 
 }  // namespace bybycu

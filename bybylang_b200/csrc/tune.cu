@@ -504,7 +504,7 @@ void apply_tile_gemm_plan(GemmArgs* a, int* route) {
     g_dispatches.fetch_add(1, std::memory_order_relaxed);
 }
 
-void apply_q4_plan(int M, int K, int N, int group, int groups, bool fast, int* route, int* stages) {
+void apply_q4_plan(int M, int K, int N, int group, int groups, bool fast, bool tc, int* route, int* stages) {
     using namespace tune;
     if (g_count.load(std::memory_order_acquire) == 0) return;
     int dev = 0;
@@ -514,8 +514,7 @@ void apply_q4_plan(int M, int K, int N, int group, int groups, bool fast, int* r
     }
     bybycu_plan p;
     if (!find_plan(Key{dev, BYBYCU_OP_MATMUL_Q4, 0, BYBYCU_DT_F32, K, N, group, groups, mclass_of(M)}, &p)) return;
-    if (p.route == BYBYCU_ROUTE_GEMV && !fast) return;
-    if (p.route != BYBYCU_ROUTE_GEMV && p.route != BYBYCU_ROUTE_SIMT) return;
+    if ((p.route == BYBYCU_ROUTE_GEMV && !fast) || (p.route == BYBYCU_ROUTE_TC && !tc)) return;
     *route = p.route;
     *stages = p.stages;
     g_dispatches.fetch_add(1, std::memory_order_relaxed);
@@ -657,6 +656,8 @@ int bybycu_prepare_q4_tuned(const uint8_t* wq, const float* scales, const float*
     if (q4a_fast_supports(mc, K, N, group_size, n_groups_per_row, x, wq, scales, zeros))
         for (int st : {2, 3})
             cands.push_back({make_plan(BYBYCU_ROUTE_GEMV, -1, st, "q4-s8-decode-st%d", st), kTolNarrow});
+    if (mc > 1 && tc_asym_supports(mc, K, N, group_size, n_groups_per_row, x, wq, scales, zeros, out))
+        cands.push_back({make_plan(BYBYCU_ROUTE_TC, -1, 0, "q4-tc-pair256x128"), kTolNarrow});
     if (cands.size() == 1) return BYBYCU_OK;
     tune_input_kernel<<<256, 256, 0, s.st>>>(x, static_cast<int64_t>(mc) * K, 0);
     BYBYCU_LAUNCH_CHECK("tune_input_kernel");
@@ -671,6 +672,7 @@ int bybycu_prepare_q4_tuned(const uint8_t* wq, const float* scales, const float*
         const float* sc = static_cast<const float*>(wcopy[3 * copy + 1]);
         const float* z = static_cast<const float*>(wcopy[3 * copy + 2]);
         if (p.route == BYBYCU_ROUTE_GEMV) return launch_q4a(K, N, x, w, sc, z, o, st, p.stages);
+        if (p.route == BYBYCU_ROUTE_TC) return launch_tc_asym(mc, K, N, x, w, sc, z, o, st);
         return bybycu_matmul_q4(x, w, sc, z, o, mc, K, N, group_size, n_groups_per_row, BYBYCU_ROUTE_SIMT, st);
     };
     bybycu_plan best{};
@@ -698,7 +700,7 @@ int bybycu_plan_set(int op, int fmt, int x_dtype, int M, int K, int N, int group
     if (op != BYBYCU_OP_TILE_GEMM && op != BYBYCU_OP_MATMUL_Q4) return set_error(BYBYCU_ERR_ARGS, "unknown op %d", op);
     if (M <= 0 || K <= 0 || N <= 0) return set_error(BYBYCU_ERR_SHAPE, "plan_set: bad shape M=%d K=%d N=%d", M, K, N);
     if (plan && ((plan->route != BYBYCU_ROUTE_SIMT && plan->route != BYBYCU_ROUTE_GEMV && plan->route != BYBYCU_ROUTE_TC) ||
-                 (op == BYBYCU_OP_MATMUL_Q4 && plan->route == BYBYCU_ROUTE_TC) || plan->variant < -1 ||
+                 plan->variant < -1 ||
                  plan->stages < 0 || plan->stages > 8))
         return set_error(BYBYCU_ERR_ARGS, "plan_set: route %d variant %d stages %d", plan->route, plan->variant,
                          plan->stages);

@@ -134,8 +134,6 @@ def test_tuned_plan_table_host_checks(monkeypatch):
         p = _lib.Plan(route=bad.get("route", _lib.ROUTE_GEMV), variant=bad.get("variant", -1),
                       stages=bad.get("stages", 0), ms=0.0, name=b"bad")
         assert lib.bybycu_plan_set(_lib.OP_TILE_GEMM, 2, 0, 1, 64, 16, 0, 0, p) == _lib.ERR_ARGS, bad
-    tc = _lib.Plan(route=_lib.ROUTE_TC, variant=-1, stages=0, ms=0.0, name=b"tc")
-    assert lib.bybycu_plan_set(_lib.OP_MATMUL_Q4, 0, 0, 1, 64, 16, 32, 2, tc) == _lib.ERR_ARGS
     prepared = C.c_int(-1)
     vp = C.c_void_p(1 << 20)
     assert lib.bybycu_prepare_q4_tuned(vp, vp, vp, 1, 64, 16, 32, 2, None) == _lib.ERR_ARGS

@@ -121,13 +121,48 @@ def test_decode_kernel_dynamic_range():
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("M,K,N,group", [(3, 512, 300, 32), (1, 512, 100, 64), (16, 256, 40, 32), (1, 96, 7, 32)])
-def test_exact_kernel_shapes(M, K, N, group, oracle_mod):
-    """Shapes outside the decode kernel (M > 1, group 64, K % 128 != 0) take the exact kernel."""
+@pytest.mark.parametrize("M,K,N,group,route", [(3, 512, 300, 32, _lib.ROUTE_SIMT), (1, 512, 100, 64, _lib.ROUTE_AUTO),
+                                                (16, 256, 40, 32, _lib.ROUTE_SIMT), (1, 96, 7, 32, _lib.ROUTE_AUTO),
+                                                (5, 384, 50, 32, _lib.ROUTE_AUTO), (4, 512, 64, 64, _lib.ROUTE_AUTO)])
+def test_exact_kernel_shapes(M, K, N, group, route, oracle_mod):
+    """The exact kernel: route SIMT, and AUTO for the shapes neither fast route takes (group
+    64, K % 128 != 0 at M = 1, K % 256 != 0 above)."""
     O = oracle_mod
     a, wq, scales, zeros = gen_q4(M, K, N, group=group, seed=M * K + N)
-    got = run_q4(a, wq, scales, zeros, M, K, N, group)
+    got = run_q4(a, wq, scales, zeros, M, K, N, group, route=route)
     assert_close(O.ref_matmul_q4(a, wq, scales, zeros, M, K, N, group), got, PEAK_TOL, ELEM_TOL)
+
+
+TC_TOL = 1e-3   # the tensor-core route: weights and activations rounded once to fp16
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 4096, 2048), (200, 1024, 300), (2, 256, 40), (129, 2048, 513)])
+def test_tensor_core_prefill_against_reference(M, K, N, oracle_mod):
+    """M > 1, group 32, K % 256 == 0: AUTO takes the tcgen05 GEMM (the same kernel as the
+    Q4B32 prefill, dequantising w = RNE16(u s - z s)); checked with the reference test's metric
+    at the tensor-core tolerance, and explicit route TC gives the same bits."""
+    O = oracle_mod
+    a, wq, scales, zeros = gen_q4(M, K, N, seed=M + K + N)
+    want = O.ref_matmul_q4(a, wq, scales, zeros, M, K, N, 32, threads=8)
+    got = run_q4(a, wq, scales, zeros, M, K, N, 32)
+    assert_close(want, got, TC_TOL, None, f"M={M} K={K} N={N}")
+    assert np.array_equal(got, run_q4(a, wq, scales, zeros, M, K, N, 32, route=_lib.ROUTE_TC))
+    assert _lib.device_error() == 0
+
+
+def test_tensor_core_route_rules():
+    K, N = 512, 64
+    a, wq, scales, zeros = gen_q4(4, K, N, seed=3)
+    with pytest.raises(_lib.BybyCudaError):   # M = 1 is the decode kernel's
+        run_q4(a[:1], wq, scales, zeros, 1, K, N, 32, route=_lib.ROUTE_TC)
+    a2, wq2, s2, z2 = gen_q4(4, 384, N, seed=4)
+    with pytest.raises(_lib.BybyCudaError):   # K % 256 != 0
+        run_q4(a2, wq2, s2, z2, 4, 384, N, 32, route=_lib.ROUTE_TC)
+    big = a.copy()
+    big[2, 5] = 1e6                           # no fp16 image: device error 7, no fault
+    run_q4(big, wq, scales, zeros, 4, K, N, 32, route=_lib.ROUTE_TC)
+    assert _lib.device_error() == 7
+    assert _lib.device_error() == 0
 
 
 def test_exact_kernel_odd_k_and_one_group():

@@ -143,8 +143,10 @@ def test_asym_decode_plan_through_resident_api():
         gb.sessionFree(be, c)
         assert gb.q4TuningStats()[1] == d0 + 1
         assert peak_err(want.reshape(-1), got) <= 1e-4
-        # a prefill class has only the exact kernel: nothing to choose
-        assert not gb.residentPrepareQ4(w, 16)
+        # a prefill class: the tensor-core GEMM against the exact kernel
+        assert gb.residentPrepareQ4(w, 16)
+        plan16 = gb.tunedPlan(_lib.OP_MATMUL_Q4, M=9, K=K, N=N, groupSize=32, nGroupsPerRow=groups)
+        assert plan16 is not None and plan16.route == _lib.ROUTE_TC, plan16
     finally:
         gb.residentFreeQ4(be, w)
 

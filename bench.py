@@ -18,6 +18,8 @@ fp32 out - through libbybycuda's GEMV route.  Algorithmic bytes per step: 25,362
 * q4_asym_decode  the asymmetric Q4 data of the reference's matmul_q4 (interleaved nibbles, fp32
               scales and zero points per 32-block, fp32 x) at the C2 shape through
               bybycu_matmul_q4's decode kernel: GB/s of its 0.75 B/weight, rotating sets > 4x L2.
+* q4_asym_prefill  the asymmetric Q4 data at the C3 shape through bybycu_matmul_q4's
+              tensor-core route, TFLOP/s.
 * decode_x_f32  the headline step with fp32 activations (the session API's type).
 * ingest      GB/s of a 1 GiB file mapping copied into HBM by bybycu_upload_host_range (the copy
               of residentUploadQ4Mapped), host clock, beside a plain pageable copy.
@@ -427,6 +429,53 @@ def main():
         except _lib.BybyCudaError as e:
             prefill = {"error": str(e)}
 
+    # ---- asymmetric Q4 prefill at the C3 shape: bybycu_matmul_q4's tensor-core route
+    q4asym_prefill = None
+    if world == 1 and not args.no_prefill and not args.no_q4asym:
+        Mp, Kp, Np = 2048, 4096, 4096
+        try:
+            Gp = Kp // 32
+            per_set = Np * Kp // 2 + 2 * Np * Gp * 4 + Mp * Kp * 4 + Mp * Np * 4
+            n_sets = max(2, -(-4 * L2_BYTES // per_set))
+            gen = torch.Generator(device=dev).manual_seed(SEED + 51)
+            asets = []
+            for c in range(n_sets):
+                wq = torch.randint(0, 256, (Np, Kp // 2), dtype=torch.uint8, device=dev, generator=gen)
+                sc = torch.rand(Np, Gp, device=dev, generator=gen) * 0.02 + 1e-4
+                zp = torch.rand(Np, Gp, device=dev, generator=gen) * 15
+                asets.append((wq, sc, zp, torch.randn(Mp, Kp, device=dev, generator=gen),
+                              torch.empty(Mp, Np, device=dev)))
+            lib = _lib.load()
+
+            def asym_call(i):
+                wq, sc, zp, xa, oa = asets[i % n_sets]
+                _lib.check(lib.bybycu_matmul_q4(C.c_void_p(xa.data_ptr()), C.c_void_p(wq.data_ptr()),
+                                                C.c_void_p(sc.data_ptr()), C.c_void_p(zp.data_ptr()),
+                                                C.c_void_p(oa.data_ptr()), Mp, Kp, Np, 32, Gp, _lib.ROUTE_TC,
+                                                C.c_void_p(stream.cuda_stream)))
+            for i in range(2 * n_sets):
+                asym_call(i)
+            stream.synchronize()
+            reps = 10 * n_sets
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for i in range(reps):
+                asym_call(i)
+            b.record(stream)
+            stream.synchronize()
+            assert _lib.device_error() == 0
+            t = a.elapsed_time(b) / reps
+            tf = 2.0 * Mp * Np * Kp / (t / 1e3) / 1e12
+            q4asym_prefill = {"value": round(tf, 2), "unit": "TFLOP/s",
+                              "workload": "asymmetric Q4 prefill M=2048 K=N=4096 (group 32), x fp32, out fp32",
+                              "ms_per_call": round(t, 5), "calls": reps,
+                              "frac": round(tf / tc_peak, 4), "peak_kind": peak_kind,
+                              "includes": "fp16 staging pass + tcgen05 GEMM (2 launches per call)",
+                              "l2": f"inputs larger than L2: {n_sets} rotating sets, back-to-back calls"}
+            del asets
+        except _lib.BybyCudaError as e:
+            q4asym_prefill = {"error": str(e)}
+
     # ---- asymmetric Q4 decode (the matmul_q4 data: interleaved nibbles, fp32 scales and zero
     # points per 32-block, fp32 x) at the C2 shape, through bybycu_matmul_q4's decode kernel
     q4asym = None
@@ -665,6 +714,7 @@ def main():
             "cpu_baseline": base, "e2e": e2e, "gpu_launches": steps * launches_per_step, "clocks": clocks,
             "prefill": prefill,
             "q4_asym_decode": q4asym,
+            "q4_asym_prefill": q4asym_prefill,
             "f16_decode": f16dec,
             "decode_x_f32": dec32,
             "ingest": ingest,

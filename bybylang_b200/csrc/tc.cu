@@ -311,7 +311,8 @@ __device__ __forceinline__ void dequant_word(uint32_t v, __half2 s, __half2 s16,
 
 // One packed word of asymmetric nibbles -> four fp16x2 columns of w = RNE16(fma(u, s, -z s)).
 // lo4 / hi4 hold the word's low / high nibbles one per byte; a byte permute puts nibble u
-// under the exponent of 2^23, and subtracting 2^23 leaves u exactly.
+// under the exponent of 2^23, and subtracting 2^23 leaves u exactly.  (The paired fp32 forms,
+// FADD2 / FFMA2, measured no faster here: 106.7 against 104.5 us at 2048 x 4096 x 4096.)
 __device__ __forceinline__ float asym_nib(uint32_t nibs, uint32_t sel) {
     return __uint_as_float(__byte_perm(nibs, 0x4B000000u, sel)) - 8388608.0f;
 }

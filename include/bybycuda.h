@@ -169,10 +169,13 @@ BYBYCU_API int bybycu_route_for(int fmt, int M, int K, int N, int x_dtype, int* 
  * u the unsigned nibble k of wq[n, (K+1)/2] (even k in the low nibble), g = k / group_size
  * (one group when group_size <= 0).  Every slot is a DEVICE pointer: fp32 a, fp32 scales and
  * zeros [N, n_groups_per_row], fp32 c.
- *   route  AUTO: the decode kernel when it applies (M = 1, group 32, K % 128 == 0, 16-byte
+ *   route  AUTO: a tuned plan for the shape (bybycu_prepare_q4_tuned) where one is installed,
+ *          else the decode kernel when it applies (M = 1, group 32, K % 128 == 0, 16-byte
  *          aligned slots: s8 tensor-core MMAs on the raw nibbles, activations in two-digit
- *          fixed point per 32-block), SIMT otherwise; SIMT: one thread per output, fmaf in k
- *          order (the CPU VM's OP_Q4_GEMV arithmetic); GEMV: the decode kernel, or
+ *          fixed point per 32-block), else the tensor-core GEMM when it applies (M > 1,
+ *          group 32, K % 256 == 0, 16-byte aligned slots: tcgen05 MMAs on weights and
+ *          activations rounded once to fp16), else SIMT; SIMT: one thread per output, fmaf in
+ *          k order (the CPU VM's OP_Q4_GEMV arithmetic); GEMV / TC: that kernel, or
  *          BYBYCU_ERR_SHAPE when it does not apply.
  * Asynchronous on `stream`. */
 BYBYCU_API int bybycu_matmul_q4(const float* a, const uint8_t* wq, const float* scales, const float* zeros,

@@ -375,6 +375,7 @@ int take_device_error(uint32_t* code) {
 // a plan was selected; errors of candidate 0 (the reference) are returned.
 int select_plan(const char* what, const Key& key, int M, int N, const std::vector<Cand>& cands, const Runner& run,
                 int copies, Scratch& s, float* out, bybycu_plan* chosen, bool* ok) {
+    const auto t_start = std::chrono::steady_clock::now();
     *ok = false;
     const size_t n_out = static_cast<size_t>(M) * N;
     std::vector<float> ref(n_out), got(n_out);
@@ -451,9 +452,11 @@ int select_plan(const char* what, const Key& key, int M, int N, const std::vecto
     *chosen = cands[valid[best]].plan;
     chosen->ms = samples[best][1];
     *ok = true;
-    fprintf(stderr, "[q4-tune:cuda] %s %dx%d M=%d: %s %.4fms (reference %.4fms; %zu validated candidates)\n", what,
-            key.K, key.N, M, chosen->name, static_cast<double>(chosen->ms), static_cast<double>(samples[0][1]),
-            valid.size());
+    const double wall = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_start).count();
+    fprintf(stderr,
+            "[q4-tune:cuda] %s %dx%d M=%d: %s %.4fms (reference %.4fms; %zu validated candidates; tuneWall=%.3fs)\n",
+            what, key.K, key.N, M, chosen->name, static_cast<double>(chosen->ms), static_cast<double>(samples[0][1]),
+            valid.size(), wall);
     return BYBYCU_OK;
 }
 

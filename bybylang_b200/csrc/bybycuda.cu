@@ -6,6 +6,7 @@
 #include "q4asym.cu"
 #include "f16gemv.cu"
 #include "tc.cu"
+#include "tcf16.cu"
 #include "vm.cu"
 #include "session.cu"
 #include "shard.cu"

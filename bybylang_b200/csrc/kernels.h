@@ -86,9 +86,12 @@ bool gemv_supports(const GemmArgs& a);
 bool f16_gemv_supports(const GemmArgs& a);
 int launch_f16_gemv(const GemmArgs& a);
 int launch_gemv(const GemmArgs& a, const PeerGather* pg = nullptr);
-// Prefill GEMM route: tcgen05 MMAs from shared-memory fp16 tiles, fp32 accumulators in TMEM.
+// Prefill GEMM route: tcgen05 MMAs from shared-memory fp16 tiles, fp32 accumulators in TMEM
+// (format 2 dequantised into tensor memory; format 1 straight from shared memory).
 bool tc_supports(const GemmArgs& a);
 int launch_tc(const GemmArgs& a);
+bool tc_f16_supports(const GemmArgs& a);
+int launch_tc_f16(const GemmArgs& a);
 // The same route staging its activations in a fixed module array instead of pool memory.
 int launch_tc_static_scratch(const GemmArgs& a);
 // The asymmetric-Q4 form of the tensor-core route (matmul_q4 prefill): fp32 x [M, K],

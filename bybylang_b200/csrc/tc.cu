@@ -328,7 +328,12 @@ __device__ __forceinline__ void dequant_word_asym(uint32_t v, float s, float mzs
 // Pre-pass: activations (bf16 or fp32) -> fp16 in the permuted K order of the weight format.
 // One thread per 32-block.  Values outside the fp16 range are recorded as a device error.
 // ---------------------------------------------------------------------------------------
-template <bool XF32, bool ASYM = false>
+// PERM: kPermQ4B32, kPermAsym (the dequantisers' K orders) or kPermNone (fp16 weights).
+constexpr int kPermQ4B32 = 0, kPermAsym = 1, kPermNone = 2;
+__host__ __device__ constexpr int perm_of(int mode, int kk) {
+    return mode == kPermAsym ? perm_src_asym(kk) : mode == kPermNone ? kk : perm_src(kk);
+}
+template <bool XF32, int PERM = kPermQ4B32>
 __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x, uint4* __restrict__ xp,
                                                       int64_t nblocks) {
     pdl_launch_dependents();   // the GEMM may start its prologue; it waits before reading xp
@@ -359,8 +364,7 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x
     uint32_t o[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-        const float a = v[ASYM ? perm_src_asym(2 * c) : perm_src(2 * c)];
-        const float b = v[ASYM ? perm_src_asym(2 * c + 1) : perm_src(2 * c + 1)];
+        const float a = v[perm_of(PERM, 2 * c)], b = v[perm_of(PERM, 2 * c + 1)];
         range_ok &= fabsf(a) < 65520.0f && fabsf(b) < 65520.0f;
         o[c] = h2_bits(__floats2half2_rn(a, b));
     }
@@ -369,6 +373,55 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x
     for (int q = 0; q < 4; ++q) xp[i * 4 + q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
 }
 
+
+// The epilogue warps of both GEMM kernels: accumulator buffer t % 2 of each of this CTA's
+// tiles back from tensor memory (tcgen05.ld, one 32-column slice at a time) and out to
+// out[token][feature]; each warp owns the TMEM lane quarter `quarter` (32 features) and
+// frees the buffer on rank 0 when done.
+__device__ __forceinline__ void epilogue_tiles(const Params& p, uint32_t tmem, uint64_t* d_full, uint64_t* d_empty,
+                                               volatile int* s_abort, int my_tiles, int pair, int pairs,
+                                               uint32_t rank, int quarter, int lane) {
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t lead_d_empty = map_to_rank(d_empty, 0);
+    for (int t = 0; t < my_tiles; ++t) {
+        const int b = t & 1, u = t >> 1;
+        const int tile = pair + t * pairs;
+        const int feat = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta + quarter * 32 + lane;
+        const int tok0 = (tile / p.tiles_n) * kBN;
+        const bool ok = __all_sync(0xffffffffu, wait_bar(&d_full[b], u & 1, kDevErrMmaWait));
+        if (!ok) {
+            *s_abort = 1;
+            break;
+        }
+        tc_fence_after();
+        const bool feat_ok = feat < p.N;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_addr + b * kAccCols + c0, v);
+            tc_wait_ld();
+            if (feat_ok) {
+                const int nt = min(32, p.M - (tok0 + c0));
+                if (p.out_bf16) {
+                    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + p.out_col0 + feat +
+                                       static_cast<int64_t>(tok0 + c0) * p.out_ld;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < nt) o[j * p.out_ld] = __float2bfloat16_rn(__uint_as_float(v[j]));
+                } else {
+                    float* o = reinterpret_cast<float*>(p.out) + p.out_col0 + feat +
+                               static_cast<int64_t>(tok0 + c0) * p.out_ld;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < nt) o[j * p.out_ld] = __uint_as_float(v[j]);
+                }
+            }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_d_empty + 8u * b);
+    }
+}
 
 // ---------------------------------------------------------------------------------------
 // The GEMM kernel (launched as clusters of two CTAs; rank 0 issues the MMAs)
@@ -642,47 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (!ok) *s_abort = 1;
     } else {
         // ---------------------------------------------------------------------- epilogue
-        const int quarter = warp & 3;
-        const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-        const uint32_t lead_d_empty = map_to_rank(d_empty, 0);
-        for (int t = 0; t < my_tiles; ++t) {
-            const int b = t & 1, u = t >> 1;
-            const int tile = pair + t * pairs;
-            const int feat = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta + quarter * 32 + lane;
-            const int tok0 = (tile / p.tiles_n) * kBN;
-            const bool ok = __all_sync(0xffffffffu, wait_bar(&d_full[b], u & 1, kDevErrMmaWait));
-            if (!ok) {
-                *s_abort = 1;
-                break;
-            }
-            tc_fence_after();
-            const bool feat_ok = feat < p.N;
-#pragma unroll 1
-            for (int c0 = 0; c0 < kBN; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + lane_addr + b * kAccCols + c0, v);
-                tc_wait_ld();
-                if (feat_ok) {
-                    const int nt = min(32, p.M - (tok0 + c0));
-                    if (p.out_bf16) {
-                        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + p.out_col0 + feat +
-                                           static_cast<int64_t>(tok0 + c0) * p.out_ld;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (j < nt) o[j * p.out_ld] = __float2bfloat16_rn(__uint_as_float(v[j]));
-                    } else {
-                        float* o = reinterpret_cast<float*>(p.out) + p.out_col0 + feat +
-                                   static_cast<int64_t>(tok0 + c0) * p.out_ld;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (j < nt) o[j * p.out_ld] = __uint_as_float(v[j]);
-                    }
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(lead_d_empty + 8u * b);
-        }
+        epilogue_tiles(p, tmem, d_full, d_empty, s_abort, my_tiles, pair, pairs, rank, warp & 3, lane);
     }
     tc_fence_before();
     __syncthreads();
@@ -696,6 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 }  // namespace tc
 
 bool tc_supports(const GemmArgs& a) {
+    if (a.fmt == BYBYCU_FMT_F16) return tc_f16_supports(a);
     if (a.fmt != BYBYCU_FMT_Q4B32) return false;
     if (a.K < tc::kWK || a.K % tc::kWK != 0 || a.M < 1 || a.N < 1) return false;
     if (a.x_dtype != BYBYCU_DT_BF16 && a.x_dtype != BYBYCU_DT_F32) return false;
@@ -791,10 +805,11 @@ template <bool ASYM>
 static int tc_run(const GemmArgs& a, const TcWeights& wt, int max_pairs, void* xp) {
     const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
     const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
+    constexpr int perm = ASYM ? tc::kPermAsym : tc::kPermQ4B32;
     if (a.x_dtype == BYBYCU_DT_F32)
-        tc::stage_x_kernel<true, ASYM><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+        tc::stage_x_kernel<true, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
     else
-        tc::stage_x_kernel<false, ASYM><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+        tc::stage_x_kernel<false, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
     BYBYCU_LAUNCH_CHECK("stage_x_kernel");
 
     tc::Maps maps;
@@ -864,6 +879,7 @@ static int tc_pooled(const GemmArgs& a, const TcWeights& wt, const DeviceInfo& i
 }
 
 int launch_tc(const GemmArgs& a) {
+    if (a.fmt == BYBYCU_FMT_F16) return launch_tc_f16(a);
     DeviceInfo info;
     int max_pairs = 0;
     if (int rc = tc_prepare(a, &info, &max_pairs)) return rc;

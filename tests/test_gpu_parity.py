@@ -290,7 +290,8 @@ def test_f16_gemv_against_oracle(M, K, N, xbf16, oracle_mod):
 def test_auto_route_f16_decode_is_gemv():
     assert gb.route_for(1, 1, 4096, 4096) == _lib.ROUTE_GEMV
     assert gb.route_for(1, 8, 4096, 4096) == _lib.ROUTE_GEMV
-    assert gb.route_for(1, 9, 4096, 4096) == _lib.ROUTE_SIMT
+    assert gb.route_for(1, 9, 4096, 4096) == _lib.ROUTE_TC        # format 1 prefill: tcgen05
+    assert gb.route_for(1, 9, 4096 + 32, 4096) == _lib.ROUTE_SIMT  # K % 128 != 0
 
 
 # ----------------------------------------------------------------------------------------

@@ -145,3 +145,44 @@ def test_tc_activation_outside_fp16_range_is_reported(oracle_mod):
     run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_TC)
     assert _lib.device_error() == 7
     assert _lib.device_error() == 0   # read-and-clear
+
+
+# ----------------------------------------------------------------------------------------
+# Format 1 (fp16 weights) on the tensor cores: both operands straight from shared memory
+# ----------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("M,K,N,xdt", [(64, 1024, 512, "f32"), (200, 2048, 300, "bf16"), (9, 128, 40, "f32"),
+                                       (512, 1024, 1024, "bf16"), (129, 4096, 257, "f32")])
+def test_f16_tensor_core_against_oracle(M, K, N, xdt):
+    from oracle import oracle as O
+    rng = np.random.default_rng(M + K + N)
+    halves = rng.normal(0, 0.05, size=(N, K)).astype(np.float16)
+    packed = dev(halves.view(np.uint8).reshape(-1).copy())
+    if xdt == "bf16":
+        xb = O.gen_x_bf16(M, K, seed=M)
+        x, xf = dev(xb).view(torch.bfloat16), O.bf16_to_f32(xb)
+    else:
+        xf = O.gen_x_f32(M, K, seed=M)
+        x = dev(xf)
+    want = O.tile_gemm_f16(xf, halves.view(np.uint16), M, K, N)
+    out = run(1, M, K, N, x, packed, route=_lib.ROUTE_TC)
+    assert_close(want, out.cpu().numpy(), TC_TOL, what=f"M={M} K={K} N={N} {xdt}")
+    if M > 8:   # AUTO takes the same route above the decode route's 8 rows
+        assert torch.equal(out, run(1, M, K, N, x, packed))
+    assert _lib.device_error() == 0
+
+
+def test_f16_tensor_core_bf16_out_and_range():
+    from oracle import oracle as O
+    M, K, N = 32, 256, 64
+    halves = np.random.default_rng(1).normal(0, 0.05, size=(N, K)).astype(np.float16)
+    packed = dev(halves.view(np.uint8).reshape(-1).copy())
+    xf = O.gen_x_f32(M, K)
+    want = O.tile_gemm_f16(xf, halves.view(np.uint16), M, K, N)
+    out = run(1, M, K, N, dev(xf), packed, route=_lib.ROUTE_TC, out_dtype=torch.bfloat16)
+    assert_close(want, out.float().cpu().numpy(), 1e-2, what="bf16 out")
+    big = xf.copy()
+    big[3, 7] = 1e6   # no fp16 image: device error 7, no fault
+    run(1, M, K, N, dev(big), packed, route=_lib.ROUTE_TC)
+    assert _lib.device_error() == 7
+    assert _lib.device_error() == 0

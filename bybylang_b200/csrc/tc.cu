@@ -23,8 +23,8 @@
 // The same kernel, instantiated with ASYM, is the prefill route of the asymmetric Q4 matmul
 // (matmul_q4, backends/cpu/cpu_kernels_impl.inc:293-319, whose Vulkan prefill runs on the
 // cooperative-matrix units): interleaved nibbles (byte j holds k = 2j low, 2j + 1 high),
-// fp32 scales and zero points per 32-block, each weight dequantised as w = RNE16(u * s - z * s)
-// with the fp32 FMA rounding once before the one rounding to fp16.
+// fp32 scales and zero points per 32-block, each weight dequantised as
+// w = RNE16(u * RNE16(s) + RNE16(-z * s)) by one half-precision FMA.
 //
 // Every wait is bounded (%globaltimer): on a timeout the kernel records an error code in
 // g_device_error, drains its copies and MMAs, frees its tensor memory and returns.
@@ -309,19 +309,20 @@ __device__ __forceinline__ void dequant_word(uint32_t v, __half2 s, __half2 s16,
     col[3] = h2_bits(__hmul2(__hsub2(bits_h2((vh & 0x00F000F0u) ^ 0x64806480u), m_hi), s16));
 }
 
-// One packed word of asymmetric nibbles -> four fp16x2 columns of w = RNE16(fma(u, s, -z s)).
-// lo4 / hi4 hold the word's low / high nibbles one per byte; a byte permute puts nibble u
-// under the exponent of 2^23, and subtracting 2^23 leaves u exactly.  (The paired fp32 forms,
-// FADD2 / FFMA2, measured no faster here: 106.7 against 104.5 us at 2048 x 4096 x 4096.)
-__device__ __forceinline__ float asym_nib(uint32_t nibs, uint32_t sel) {
-    return __uint_as_float(__byte_perm(nibs, 0x4B000000u, sel)) - 8388608.0f;
-}
-__device__ __forceinline__ void dequant_word_asym(uint32_t v, float s, float mzs, uint32_t* col) {
-    const uint32_t lo4 = v & 0x0F0F0F0Fu, hi4 = (v >> 4) & 0x0F0F0F0Fu;
-    col[0] = h2_bits(__floats2half2_rn(fmaf(asym_nib(lo4, 0x7650), s, mzs), fmaf(asym_nib(lo4, 0x7652), s, mzs)));
-    col[1] = h2_bits(__floats2half2_rn(fmaf(asym_nib(hi4, 0x7650), s, mzs), fmaf(asym_nib(hi4, 0x7652), s, mzs)));
-    col[2] = h2_bits(__floats2half2_rn(fmaf(asym_nib(lo4, 0x7651), s, mzs), fmaf(asym_nib(lo4, 0x7653), s, mzs)));
-    col[3] = h2_bits(__floats2half2_rn(fmaf(asym_nib(hi4, 0x7651), s, mzs), fmaf(asym_nib(hi4, 0x7653), s, mzs)));
+// One packed word of asymmetric nibbles -> four fp16x2 columns of w = RNE16(u s16 + m16), with
+// s16 = RNE16(s) and m16 = RNE16(-z s) per block: the nibble placed in the mantissa of 1024
+// minus 1024 is u exactly, and the half-precision FMA rounds once.  Three operations per
+// two weights, as the Q4B32 dequantiser; the form that rounded an fp32 FMA once (byte
+// permutes, FADD, FFMA, then one conversion: seven per pair) kept the ALU pipe 51% busy
+// and the tensor pipe at 34% (644-666 TFLOP/s at 2048 x 4096 x 4096).  Rounding s and z s
+// to fp16 costs ~2^-11 of each block's contribution, inside the route's 1e-3 tolerance.
+__device__ __forceinline__ void dequant_word_asym(uint32_t v, __half2 s, __half2 mzs, uint32_t* col) {
+    const __half2 m = bits_h2(0x64006400u);   // 1024
+    const uint32_t vh = v >> 8;
+    col[0] = h2_bits(__hfma2(__hsub2(bits_h2((v & 0x000F000Fu) | 0x64006400u), m), s, mzs));
+    col[1] = h2_bits(__hfma2(__hsub2(bits_h2(((v >> 4) & 0x000F000Fu) | 0x64006400u), m), s, mzs));
+    col[2] = h2_bits(__hfma2(__hsub2(bits_h2((vh & 0x000F000Fu) | 0x64006400u), m), s, mzs));
+    col[3] = h2_bits(__hfma2(__hsub2(bits_h2(((vh >> 4) & 0x000F000Fu) | 0x64006400u), m), s, mzs));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -650,8 +651,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 if (!ok) break;
                 tc_fence_after();
                 if constexpr (ASYM) {
-                    const float sv[4] = {sa.x, sa.y, sa.z, sa.w};
-                    const float mz[4] = {-za.x * sa.x, -za.y * sa.y, -za.z * sa.z, -za.w * sa.w};
+                    const __half2 sv[4] = {__float2half2_rn(sa.x), __float2half2_rn(sa.y), __float2half2_rn(sa.z),
+                                           __float2half2_rn(sa.w)};
+                    const __half2 mz[4] = {__float2half2_rn(-za.x * sa.x), __float2half2_rn(-za.y * sa.y),
+                                           __float2half2_rn(-za.z * sa.z), __float2half2_rn(-za.w * sa.w)};
 #pragma unroll
                     for (int half = 0; half < 2; ++half) {
                         uint32_t col[32];

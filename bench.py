@@ -44,6 +44,7 @@ import subprocess
 import sys
 import threading
 import time
+import warnings
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -671,7 +672,9 @@ def main():
                     _lib.call("bybycu_upload_host_range", C.c_void_p(dst.data_ptr()), C.c_void_p(m.data), nbytes)
                     rates.append(nbytes / (time.perf_counter() - t0) / 1e9)
                 ok = torch.equal(dst[:len(blk)], torch.from_numpy(np.frombuffer(blk, np.uint8).copy()).to(dev))
-                src = torch.from_numpy(m.view())   # pageable: the driver's own staging
+                with warnings.catch_warnings():   # a read-only mapping: torch only reads it here
+                    warnings.simplefilter("ignore", UserWarning)
+                    src = torch.from_numpy(m.view())   # pageable: the driver's own staging
                 torch.cuda.synchronize()
                 t0 = time.perf_counter()
                 dst.copy_(src)

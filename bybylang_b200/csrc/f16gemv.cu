@@ -18,6 +18,7 @@ namespace {
 constexpr int kF16Rows = 4;        // rows per warp in flight
 constexpr int kF16Warps = 16;      // warps per CTA
 constexpr int kF16MaxM = 8;
+constexpr int kF16Unroll = 2;    // K steps whose loads are in flight together
 
 // MMAX activation rows at most; rows m >= M are skipped (warp-uniform).
 template <int MMAX, bool XBF16, bool OUTBF16>
@@ -47,31 +48,41 @@ __global__ void __launch_bounds__(kF16Warps * 32) f16_gemv_kernel(const __half* 
 #pragma unroll
         for (int r = 0; r < kF16Rows; ++r)
             rows[r] = reinterpret_cast<const uint4*>(w + static_cast<int64_t>(min(n0 + r, N - 1)) * K);
-        for (int k8 = lane; k8 < K / 8; k8 += 32) {
-            uint4 v[kF16Rows];
+        // two 16-byte loads per row in flight per lane (eight per lane in all): the stream is
+        // bound by DRAM latency, so every load issued before the first FMA counts
+        for (int k8 = lane; k8 < K / 8; k8 += 32 * kF16Unroll) {
+            uint4 v[kF16Unroll][kF16Rows];
 #pragma unroll
-            for (int r = 0; r < kF16Rows; ++r) v[r] = __ldcs(rows[r] + k8);   // streaming: read once
+            for (int u = 0; u < kF16Unroll; ++u)
 #pragma unroll
-            for (int m = 0; m < MMAX; ++m) {
-                if (m >= M) break;
-                const float4 xa = *reinterpret_cast<const float4*>(xs + m * K + 8 * k8);
-                const float4 xb = *reinterpret_cast<const float4*>(xs + m * K + 8 * k8 + 4);
+                for (int r = 0; r < kF16Rows; ++r)
+                    v[u][r] = k8 + 32 * u < K / 8 ? __ldcs(rows[r] + k8 + 32 * u) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-                for (int r = 0; r < kF16Rows; ++r) {
-                    const uint32_t wv[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
-                    float2 f;
-                    f = __half22float2(*reinterpret_cast<const __half2*>(&wv[0]));
-                    acc[r][m] = fmaf(f.x, xa.x, acc[r][m]);
-                    acc[r][m] = fmaf(f.y, xa.y, acc[r][m]);
-                    f = __half22float2(*reinterpret_cast<const __half2*>(&wv[1]));
-                    acc[r][m] = fmaf(f.x, xa.z, acc[r][m]);
-                    acc[r][m] = fmaf(f.y, xa.w, acc[r][m]);
-                    f = __half22float2(*reinterpret_cast<const __half2*>(&wv[2]));
-                    acc[r][m] = fmaf(f.x, xb.x, acc[r][m]);
-                    acc[r][m] = fmaf(f.y, xb.y, acc[r][m]);
-                    f = __half22float2(*reinterpret_cast<const __half2*>(&wv[3]));
-                    acc[r][m] = fmaf(f.x, xb.z, acc[r][m]);
-                    acc[r][m] = fmaf(f.y, xb.w, acc[r][m]);
+            for (int u = 0; u < kF16Unroll; ++u) {
+                const int kk = k8 + 32 * u;
+                if (kk >= K / 8) break;
+#pragma unroll
+                for (int m = 0; m < MMAX; ++m) {
+                    if (m >= M) break;
+                    const float4 xa = *reinterpret_cast<const float4*>(xs + m * K + 8 * kk);
+                    const float4 xb = *reinterpret_cast<const float4*>(xs + m * K + 8 * kk + 4);
+#pragma unroll
+                    for (int r = 0; r < kF16Rows; ++r) {
+                        const uint32_t wv[4] = {v[u][r].x, v[u][r].y, v[u][r].z, v[u][r].w};
+                        float2 f;
+                        f = __half22float2(*reinterpret_cast<const __half2*>(&wv[0]));
+                        acc[r][m] = fmaf(f.x, xa.x, acc[r][m]);
+                        acc[r][m] = fmaf(f.y, xa.y, acc[r][m]);
+                        f = __half22float2(*reinterpret_cast<const __half2*>(&wv[1]));
+                        acc[r][m] = fmaf(f.x, xa.z, acc[r][m]);
+                        acc[r][m] = fmaf(f.y, xa.w, acc[r][m]);
+                        f = __half22float2(*reinterpret_cast<const __half2*>(&wv[2]));
+                        acc[r][m] = fmaf(f.x, xb.x, acc[r][m]);
+                        acc[r][m] = fmaf(f.y, xb.y, acc[r][m]);
+                        f = __half22float2(*reinterpret_cast<const __half2*>(&wv[3]));
+                        acc[r][m] = fmaf(f.x, xb.z, acc[r][m]);
+                        acc[r][m] = fmaf(f.y, xb.w, acc[r][m]);
+                    }
                 }
             }
         }

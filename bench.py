@@ -231,7 +231,17 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # NCCL may print its version banner on stdout while the communicator comes up; send
+        # that to stderr so that stdout carries the one JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            os.dup2(saved, 1)
+            os.close(saved)
     gb.ensureGpuInit(gb.GpuBackend.gbCuda, local)
     dev = torch.device("cuda", local)
     hbm_peak, tc_peak, peak_kind = peaks()

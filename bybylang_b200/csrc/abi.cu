@@ -210,7 +210,8 @@ int bybycu_init(int device) {
     if (d.cc_major != 10)
         return set_error(BYBYCU_ERR_NODEV, "device %d is sm_%d%d; this library is built for sm_100a", device, d.cc_major,
                          d.cc_minor);
-    return BYBYCU_OK;
+    // the static-scratch route allocates nothing after this: its module memory is loaded now
+    return tc_static_scratch_load();
 }
 
 int bybycu_malloc(void** dptr, int64_t bytes) {

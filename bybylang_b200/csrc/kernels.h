@@ -94,6 +94,8 @@ bool tc_f16_supports(const GemmArgs& a);
 int launch_tc_f16(const GemmArgs& a);
 // The same route staging its activations in a fixed module array instead of pool memory.
 int launch_tc_static_scratch(const GemmArgs& a);
+// Loads that route's module array and kernels on the current device (bybycu_init).
+int tc_static_scratch_load();
 // The asymmetric-Q4 form of the tensor-core route (matmul_q4 prefill): fp32 x [M, K],
 // interleaved nibbles [N, K/2], fp32 scales and zero points [N, K/32], fp32 out [M, N].
 bool tc_asym_supports(int M, int K, int N, int group, int n_groups, const void* x, const void* wq, const void* scales,

@@ -758,10 +758,11 @@ static int scratch_pool(int device, cudaMemPool_t* pool) {
 template <bool ASYM>
 static int tc_setup(DeviceInfo* info, int* max_pairs) {
     if (int rc = current_device_info(info)) return rc;
-    static std::once_flag once[16];
-    static cudaError_t prep_rc[16];
-    static int pairs[16];
-    const int dev = info->device & 15;
+    static std::once_flag once[64];
+    static cudaError_t prep_rc[64];
+    static int pairs[64];
+    const int dev = info->device;
+    if (dev < 0 || dev >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", dev);
     constexpr uint32_t smem = tc::Lay<ASYM>::kSmemBytes;
     std::call_once(once[dev], [&] {
         prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel<ASYM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -926,23 +927,38 @@ int launch_tc_asym(int M, int K, int N, const float* x, const uint8_t* wq, const
 
 // ---------------------------------------------------------------------------------------
 // The same GEMM with staging scratch that is never allocated at call time: a fixed array in
-// the module's device memory, reserved when the library loads on a device.
+// the module's device memory.  With lazy module loading (the CUDA 12 default) a module gets
+// its device memory - code and this array - when it is first used on a device, so
+// tc_static_scratch_load() below, called by bybycu_init, uses it there: after that no call
+// of this route allocates anything.
 // ---------------------------------------------------------------------------------------
 constexpr size_t kStaticScratchBytes = size_t(32) << 20;   // M * K <= 16 Mi activations
 __device__ __align__(256) uint8_t g_tc_static_scratch[kStaticScratchBytes];
 
-// The array's address on the current device, looked up once per device.
-static int static_scratch(int device, void** ptr) {
-    static std::mutex mu;
-    static void* ptrs[64] = {};
-    if (device < 0 || device >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", device);
-    std::lock_guard<std::mutex> lock(mu);
-    if (!ptrs[device]) {
-        void* p = nullptr;
-        BYBYCU_CUDA_TRY(cudaGetSymbolAddress(&p, g_tc_static_scratch));
-        ptrs[device] = p;
-    }
-    *ptr = ptrs[device];
+// The array's address in the current device's context.  Looked up on every call (cheap once
+// the module is loaded), so a context created again after a device reset gets its own
+// address, never a stale one.
+static int static_scratch(void** ptr) {
+    void* p = nullptr;
+    BYBYCU_CUDA_TRY(cudaGetSymbolAddress(&p, g_tc_static_scratch));
+    *ptr = p;
+    return BYBYCU_OK;
+}
+
+// Loads, on the current device, the module's array and every kernel the static-scratch route
+// launches, and sets the GEMM's attributes: the allocations of lazy loading happen here.
+int tc_static_scratch_load() {
+    DeviceInfo info;
+    if (int rc = current_device_info(&info)) return rc;
+    if (info.cc_major != 10 || info.max_smem_optin < static_cast<int>(tc::kSmemBytes)) return BYBYCU_OK;
+    void* p = nullptr;
+    if (int rc = static_scratch(&p)) return rc;
+    int max_pairs = 0;
+    if (int rc = tc_setup<false>(&info, &max_pairs)) return rc;
+    cudaFuncAttributes fa;
+    BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<false, tc::kPermQ4B32>));
+    BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<true, tc::kPermQ4B32>));
+    BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::gemm_kernel<false>));
     return BYBYCU_OK;
 }
 
@@ -957,7 +973,7 @@ int launch_tc_static_scratch(const GemmArgs& a) {
     int max_pairs = 0;
     if (int rc = tc_prepare(a, &info, &max_pairs)) return rc;
     void* xp = nullptr;
-    if (int rc = static_scratch(info.device, &xp)) return rc;
+    if (int rc = static_scratch(&xp)) return rc;
     TcWeights wt;
     wt.nibbles = a.packed;
     wt.scales = a.packed + a.scale_base;

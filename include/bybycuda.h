@@ -138,8 +138,10 @@ BYBYCU_API int bybycu_tile_gemm_host(int fmt, int M, int K, int N,
  * stall on the allocator.  This entry point has no reference counterpart: the reference
  * never stages activations, so it never needs scratch.
  *   Scratch: the fp16 staging copy of x (M*K*2 bytes) lives in one fixed 32 MiB array of
- *   the library's device memory, reserved when the library loads on a device; its address
- *   is looked up once per device (cudaGetSymbolAddress).  Nothing is allocated or freed
+ *   the library's device memory.  CUDA loads a module lazily, so bybycu_init(device) loads
+ *   this array and the route's kernels on that device; call it once per device before the
+ *   first call here (and before any stream capture).  Each call then looks the array's
+ *   address up (cudaGetSymbolAddress) in the current context; nothing is allocated or freed
  *   per call.  No part of it needs to start at zero: every byte the GEMM reads is written
  *   by the same call first.
  *   Limit: M*K <= 16,777,216 (e.g. M=4096 at K=4096); larger shapes fail with

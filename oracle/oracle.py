@@ -21,7 +21,6 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "libq4_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_oracle.so")
-REFERENCE_TREE = "/root/reference"
 
 OP_TILE_GEMM = 0xB0
 OP_FP4_COOP_GEMM = 0xAC
@@ -33,9 +32,24 @@ _port = None
 _ref = None
 
 
+def reference_tree():
+    """The reference project's source tree: BYBY_REFERENCE_TREE, else the `reference_path` that
+    BASELINE.json at the repository root records; None when neither names an existing tree."""
+    tree = os.environ.get("BYBY_REFERENCE_TREE")
+    if not tree:
+        try:
+            import json
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                tree = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            tree = None
+    return tree if tree and os.path.isdir(tree) else None
+
+
 def build() -> None:
     """Compile the restatement and, when the reference tree is present, the reference C."""
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    tree = reference_tree()
+    subprocess.run(["make", "-s", "-C", HERE] + ([f"REF={tree}"] if tree else []), check=True)
 
 
 def _ptr(a: np.ndarray, ct=C.c_void_p):

@@ -69,3 +69,21 @@ def test_noalloc_rejects_shapes_beyond_the_fixed_scratch():
                                               _lib.DT_F32, M * N, None)
     assert rc == _lib.ERR_RANGE
     assert "32 MiB" in _lib.last_error()[1]
+
+
+@pytest.mark.gpu
+def test_noalloc_first_call_after_init_leaves_device_memory_unchanged():
+    """bybycu_init loads the route's module (array and kernels) on the device, so the first
+    no-alloc call after it must not change the device's free memory (cudaMemGetInfo)."""
+    gb.ensureGpuInit(gb.GpuBackend.gbCuda, 0)
+    M, K, N = 256, 1024, 512
+    w, x = _q4_case(M, K, N, seed=5)
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda:0")
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(0)
+    _noalloc(w, x, out)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(0)
+    assert _lib.device_error() == 0
+    assert free1 == free0, f"device free memory changed by {free0 - free1} bytes"
+    assert torch.isfinite(out).all()

@@ -33,7 +33,9 @@ ROUTE_AUTO = 0
 ROUTE_GEMV = 1
 ROUTE_TC = 2
 ROUTE_SIMT = 3
-ROUTE_NAMES = {ROUTE_AUTO: "auto", ROUTE_GEMV: "gemv", ROUTE_TC: "tc", ROUTE_SIMT: "simt"}
+ROUTE_TC_FP16W = 4
+ROUTE_NAMES = {ROUTE_AUTO: "auto", ROUTE_GEMV: "gemv", ROUTE_TC: "tc", ROUTE_SIMT: "simt",
+               ROUTE_TC_FP16W: "tc-fp16w"}
 
 
 OP_TILE_GEMM = 0

@@ -119,20 +119,23 @@ int choose_route(const GemmArgs& a, int requested, int* route) {
     if (requested == BYBYCU_ROUTE_SIMT) { *route = BYBYCU_ROUTE_SIMT; return BYBYCU_OK; }
     if (requested == BYBYCU_ROUTE_GEMV) {
         if (!gemv_supports(a))
-            return set_error(BYBYCU_ERR_SHAPE, "GEMV route needs format 2 (M <= 16) or format 1 (M <= 8) and "
+            return set_error(BYBYCU_ERR_SHAPE, "GEMV route needs format 2 (M <= 32) or format 1 (M <= 8) and "
                                                "16-byte aligned slots");
         *route = BYBYCU_ROUTE_GEMV;
         return BYBYCU_OK;
     }
-    if (requested == BYBYCU_ROUTE_TC) {
-        if (!tc_supports(a))
+    if (requested == BYBYCU_ROUTE_TC || requested == BYBYCU_ROUTE_TC_FP16W) {
+        if (!tc_supports(a) || (requested == BYBYCU_ROUTE_TC_FP16W && a.fmt != BYBYCU_FMT_Q4B32))
             return set_error(BYBYCU_ERR_SHAPE, "tensor-core route cannot run format %d M=%d K=%d N=%d", a.fmt, a.M,
                              a.K, a.N);
-        *route = BYBYCU_ROUTE_TC;
+        *route = requested;
         return BYBYCU_OK;
     }
     if (requested != BYBYCU_ROUTE_AUTO) return set_error(BYBYCU_ERR_ARGS, "unknown route %d", requested);
-    if (a.M <= 16 && gemv_supports(a)) *route = BYBYCU_ROUTE_GEMV;
+    // GEMV up to 16 rows, and up to 32 for fp32 rows (the tensor-core route rounds those to
+    // fp16; the GEMV keeps them exact as two bf16 terms)
+    const bool gemv_rows = a.M <= 16 || (a.M <= kGemvMaxRows && a.x_dtype == BYBYCU_DT_F32);
+    if (gemv_rows && gemv_supports(a)) *route = BYBYCU_ROUTE_GEMV;
     else if (tc_supports(a)) *route = BYBYCU_ROUTE_TC;
     else if (gemv_supports(a)) *route = BYBYCU_ROUTE_GEMV;
     else *route = BYBYCU_ROUTE_SIMT;
@@ -143,6 +146,7 @@ int run_gemm(const GemmArgs& a, int route) {
     switch (route) {
         case BYBYCU_ROUTE_GEMV: return launch_gemv(a);
         case BYBYCU_ROUTE_TC: return launch_tc(a);
+        case BYBYCU_ROUTE_TC_FP16W: return launch_tc(a, true);
         default: return launch_simt(a);
     }
 }

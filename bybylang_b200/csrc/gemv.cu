@@ -1,4 +1,5 @@
-// gemv.cu - the decode GEMV route of the tile GEMM for Q4B32 weights (format 2), M <= 16.
+// gemv.cu - the decode GEMV route of the tile GEMM for Q4B32 weights (format 2), M <= 16 per
+// launch (17..32 rows run as one launch per 16 rows).
 //
 // The arithmetic is the tile op's (backends/cpu/cpu_vm.c:605-626 with an fp16 block scale):
 //     out[m, n] = sum_g s[n, g] * sum_{k in block g} x[m, k] * q[n, k]
@@ -1095,7 +1096,7 @@ size_t round1k(size_t v) { return (v + 1023) / 1024 * 1024; }
 bool gemv_supports(const GemmArgs& a) {
     if (a.fmt == BYBYCU_FMT_F16) return f16_gemv_supports(a);   // f16gemv.cu
     if (a.fmt != BYBYCU_FMT_Q4B32) return false;
-    if (a.M < 1 || a.M > 16 || a.K % 32 != 0 || a.N < 1) return false;
+    if (a.M < 1 || a.M > kGemvMaxRows || a.K % 32 != 0 || a.N < 1) return false;
     if (a.x_dtype != BYBYCU_DT_BF16 && a.x_dtype != BYBYCU_DT_F32) return false;
     // TMA needs 16-byte aligned global bases; scales need 2-byte alignment.
     if ((reinterpret_cast<uintptr_t>(a.packed) & 15u) || (reinterpret_cast<uintptr_t>(a.x) & 15u)) return false;
@@ -1169,6 +1170,21 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     if (a.fmt == BYBYCU_FMT_F16) {
         if (pg) return set_error(BYBYCU_ERR_ARGS, "the format-1 GEMV does not store to peers");
         return launch_f16_gemv(a);
+    }
+    if (a.M > 16) {
+        // 17..32 rows: one launch per 16 rows (each streams the weights once more); this keeps
+        // fp32 activation rows exact in two bf16 terms where the tensor-core route would round
+        // them to fp16
+        if (pg) return set_error(BYBYCU_ERR_ARGS, "the GEMV stores to peers for at most 16 rows");
+        const size_t xe = a.x_dtype == BYBYCU_DT_F32 ? 4 : 2, oe = a.out_dtype == BYBYCU_DT_BF16 ? 2 : 4;
+        for (int m0 = 0; m0 < a.M; m0 += 16) {
+            GemmArgs b = a;
+            b.M = std::min(16, a.M - m0);
+            b.x = static_cast<const uint8_t*>(a.x) + static_cast<size_t>(m0) * a.K * xe;
+            b.out = static_cast<uint8_t*>(a.out) + static_cast<size_t>(m0) * a.out_ld * oe;
+            if (int rc = launch_gemv(b, nullptr)) return rc;
+        }
+        return BYBYCU_OK;
     }
     DeviceInfo dev;
     if (int rc = current_device_info(&dev)) return rc;

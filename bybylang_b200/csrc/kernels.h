@@ -79,8 +79,9 @@ __device__ __forceinline__ bool peer_gather_finish(const PeerGather& pg) {
 
 // CUDA-core FP32 route: every format, every K % 32 == 0 shape.
 int launch_simt(const GemmArgs& a);
-// Decode GEMV route (format 2, M <= 16): TMA-streamed weights, bf16 mma.sync reductions with
-// exact per-block fp32 scaling.
+// Decode GEMV route (format 2, M <= 32 - one launch per 16 rows): TMA-streamed weights, s8 or
+// bf16 mma.sync reductions with exact per-block fp32 scaling.
+constexpr int kGemvMaxRows = 32;
 bool gemv_supports(const GemmArgs& a);
 // Format 1 (fp16 weights) decode GEMV, M <= 8: 16-byte weight streams, fp32 FMAs.
 bool f16_gemv_supports(const GemmArgs& a);
@@ -89,7 +90,7 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg = nullptr);
 // Prefill GEMM route: tcgen05 MMAs from shared-memory fp16 tiles, fp32 accumulators in TMEM
 // (format 2 dequantised into tensor memory; format 1 straight from shared memory).
 bool tc_supports(const GemmArgs& a);
-int launch_tc(const GemmArgs& a);
+int launch_tc(const GemmArgs& a, bool fp16_weights = false);
 bool tc_f16_supports(const GemmArgs& a);
 int launch_tc_f16(const GemmArgs& a);
 // The same route staging its activations in a fixed module array instead of pool memory.

@@ -221,7 +221,7 @@ int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1, con
         a.stream = s;
         int route = 0;
         if (int rc = choose_route(a, BYBYCU_ROUTE_AUTO, &route)) return rc;
-        if (route == BYBYCU_ROUTE_GEMV && fmt == BYBYCU_FMT_Q4B32) {
+        if (route == BYBYCU_ROUTE_GEMV && fmt == BYBYCU_FMT_Q4B32 && M <= 16) {
             // the Q4B32 GEMV stores every value to the peers itself and ends with the signals
             if (int rc = launch_gemv(a, &pg)) return rc;
             fused = true;

@@ -229,6 +229,26 @@ __device__ __forceinline__ void mma_pair_stage(uint32_t d_tmem, uint32_t a0, con
         : "memory");
 }
 
+// The low weight term of an exact-weight stage: eight more MMAs from A slot `a0`, with the same
+// activation descriptors, accumulating into the same D (issued right after mma_pair_stage).
+__device__ __forceinline__ void mma_pair_accumulate8(uint32_t d_tmem, uint32_t a0, const uint64_t (&b)[8]) {
+    asm volatile(
+        "{\n\t.reg .pred e, q;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 q, %2, 0;\n\t"   // the instruction descriptor is never 0: accumulate
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %3, %2, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%4], %5, %2, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%6], %7, %2, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%8], %9, %2, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%10], %11, %2, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%12], %13, %2, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%14], %15, %2, q;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%16], %17, %2, q;\n\t}" ::"r"(d_tmem),
+        "r"(a0), "r"(kIdesc), "l"(b[0]), "r"(a0 + 8), "l"(b[1]), "r"(a0 + 16), "l"(b[2]), "r"(a0 + 24), "l"(b[3]),
+        "r"(a0 + 32), "l"(b[4]), "r"(a0 + 40), "l"(b[5]), "r"(a0 + 48), "l"(b[6]), "r"(a0 + 56), "l"(b[7])
+        : "memory");
+}
+
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
     return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
@@ -307,6 +327,25 @@ __device__ __forceinline__ void dequant_word(uint32_t v, __half2 s, __half2 s16,
     col[1] = h2_bits(__hmul2(__hsub2(bits_h2((v & 0x00F000F0u) ^ 0x64806480u), m_hi), s16));
     col[2] = h2_bits(__hmul2(__hsub2(bits_h2((vh & 0x000F000Fu) ^ 0x64086408u), m_lo), s));
     col[3] = h2_bits(__hmul2(__hsub2(bits_h2((vh & 0x00F000F0u) ^ 0x64806480u), m_hi), s16));
+}
+
+// The exact form: one packed word -> four fp16x2 columns of each of two weight terms,
+// w = q * s_hi + q * s_lo, where s_hi is the fp16 scale with its three lowest mantissa bits
+// cleared (at most 8 significant bits) and s_lo = s - s_hi (at most 3).  q has at most 3
+// significant bits, so both products are exact in fp16 (q * s_hi needs at most 11 bits,
+// q * s_lo at most 6) and their sum is q * s exactly: the tensor core's fp32 accumulation is
+// the only rounding left.  Every nibble goes through the low-nibble form (1032 + q, one exact
+// subtraction), the high ones after a 4-bit shift.
+__device__ __forceinline__ void dequant_word_exact(uint32_t v, __half2 s_hi, __half2 s_lo, uint32_t* hi,
+                                                   uint32_t* lo) {
+    const __half2 m_lo = bits_h2(0x64086408u);
+    const uint32_t src[4] = {v, v >> 4, v >> 8, v >> 12};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const __half2 q = __hsub2(bits_h2((src[c] & 0x000F000Fu) ^ 0x64086408u), m_lo);
+        hi[c] = h2_bits(__hmul2(q, s_hi));
+        lo[c] = h2_bits(__hmul2(q, s_lo));
+    }
 }
 
 // One packed word of asymmetric nibbles -> four fp16x2 columns of w = RNE16(u s16 + m16), with
@@ -427,9 +466,14 @@ __device__ __forceinline__ void epilogue_tiles(const Params& p, uint32_t tmem, u
 // ---------------------------------------------------------------------------------------
 // The GEMM kernel (launched as clusters of two CTAs; rank 0 issues the MMAs)
 // ---------------------------------------------------------------------------------------
-template <bool ASYM>
+// EXACT (Q4B32 only): the weights enter as the two exact fp16 terms of dequant_word_exact, in
+// a pair of A slots per stage (two stages in flight instead of four), sixteen MMAs per stage.
+template <bool ASYM, bool EXACT = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
+    static_assert(!(ASYM && EXACT), "the exact weight split is for Q4B32");
     using L = Lay<ASYM>;
+    // A slots: one per stage (kASlots stages in flight), or a pair per stage when EXACT
+    constexpr int kAStages = EXACT ? kASlots / 2 : kASlots;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -563,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             // stage i frees its activation stage and its A slot once its MMAs completed
             auto release_stage = [&](int i) {
                 tc_commit_pair(&x_empty[i % kStages]);
-                tc_commit_pair(&a_empty[i % kASlots]);
+                tc_commit_pair(&a_empty[i % kAStages]);
             };
             int consumed = 0, pending = -1;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
@@ -583,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     }
                     tc_fence_after();
                     const uint64_t bdesc = sw128_desc(base + kOffX + s * kXStageBytes);
-                    const uint32_t a0 = tmem + kAOff + (consumed % kASlots) * kACols;
+                    const uint32_t a0 = tmem + kAOff + (EXACT ? 2 : 1) * (consumed % kAStages) * kACols;
                     // 16-K steps advance 32 bytes inside a 128-byte swizzle row, then jump to
                     // the next 64-K box
                     uint64_t bk[8];
@@ -592,7 +636,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         bk[k16] = bdesc + static_cast<uint64_t>((k16 >> 2) * (kXSubBytes >> 4) + (k16 & 3) * 2);
                     const int pv = pending >= 0 ? pending : 0;
                     mma_pair_stage(d_tmem, a0, bk, ks != 0, pending >= 0, smem_u32(&x_empty[pv % kStages]),
-                                   smem_u32(&a_empty[pv % kASlots]));
+                                   smem_u32(&a_empty[pv % kAStages]));
+                    if constexpr (EXACT) mma_pair_accumulate8(d_tmem, a0 + kACols, bk);
                     pending = consumed;
                     ++consumed;
                 }
@@ -645,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 ++w_used;
                 const int i = t * n_ks + kw * kSubs + grp;          // stage index; i % 2 == grp
                 const int s = i % kStages;                          // its activation stage (full barrier)
-                const int slot = i % kASlots, r = i / kASlots;      // its A slot
+                const int slot = i % kAStages, r = i / kAStages;    // its A slot (pair, when EXACT)
                 if (r > 0) ok = wait_bar(&a_empty[slot], (r - 1) & 1, kDevErrEmptyWait);
                 ok = __all_sync(0xffffffffu, ok && !*s_abort);
                 if (!ok) break;
@@ -668,6 +713,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                             dequant_word_asym(u.w, sv[blk], mz[blk], &col[16 * h + 12]);
                         }
                         tmem_st32(tmem + lane_addr + kAOff + slot * kACols + half * 32, col);
+                    }
+                } else if constexpr (EXACT) {
+                    const uint32_t sw0 = grp ? sc.z : sc.x, sw1 = grp ? sc.w : sc.y;
+                    const uint32_t a_hi = tmem + lane_addr + kAOff + 2 * slot * kACols;
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const uint32_t pr = half ? sw1 : sw0;              // two blocks' fp16 scales
+                        const uint32_t prh = pr & 0xFFF8FFF8u;             // s_hi of both
+                        const __half2 lo2 = __hsub2(bits_h2(pr), bits_h2(prh));   // s_lo, exact
+                        uint32_t hcol[32], lcol[32];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const __half2 shi = h ? __high2half2(bits_h2(prh)) : __low2half2(bits_h2(prh));
+                            const __half2 slo = h ? __high2half2(lo2) : __low2half2(lo2);
+                            const uint4 u = chunk[2 * half + h];
+                            dequant_word_exact(u.x, shi, slo, &hcol[16 * h + 0], &lcol[16 * h + 0]);
+                            dequant_word_exact(u.y, shi, slo, &hcol[16 * h + 4], &lcol[16 * h + 4]);
+                            dequant_word_exact(u.z, shi, slo, &hcol[16 * h + 8], &lcol[16 * h + 8]);
+                            dequant_word_exact(u.w, shi, slo, &hcol[16 * h + 12], &lcol[16 * h + 12]);
+                        }
+                        tmem_st32(a_hi + half * 32, hcol);
+                        tmem_st32(a_hi + kACols + half * 32, lcol);
                     }
                 } else {
                 // scales of blocks 4 grp .. 4 grp + 3: two 32-bit words of the row's eight
@@ -755,7 +822,7 @@ static int scratch_pool(int device, cudaMemPool_t* pool) {
 
 
 // Device info, the kernel attribute and the number of CTA pairs that fit at once.
-template <bool ASYM>
+template <bool ASYM, bool EXACT = false>
 static int tc_setup(DeviceInfo* info, int* max_pairs) {
     if (int rc = current_device_info(info)) return rc;
     static std::once_flag once[64];
@@ -765,7 +832,7 @@ static int tc_setup(DeviceInfo* info, int* max_pairs) {
     if (dev < 0 || dev >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", dev);
     constexpr uint32_t smem = tc::Lay<ASYM>::kSmemBytes;
     std::call_once(once[dev], [&] {
-        prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel<ASYM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel<ASYM, EXACT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(smem));
         if (prep_rc[dev] != cudaSuccess) return;
         cudaLaunchConfig_t cfg = {};
@@ -779,7 +846,7 @@ static int tc_setup(DeviceInfo* info, int* max_pairs) {
         cfg.dynamicSmemBytes = smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        prep_rc[dev] = cudaOccupancyMaxActiveClusters(&pairs[dev], tc::gemm_kernel<ASYM>, &cfg);
+        prep_rc[dev] = cudaOccupancyMaxActiveClusters(&pairs[dev], tc::gemm_kernel<ASYM, EXACT>, &cfg);
     });
     if (prep_rc[dev] != cudaSuccess) return cuda_fail(prep_rc[dev], "tensor-core GEMM set-up");
     if (pairs[dev] < 1) return set_error(BYBYCU_ERR_DEVICE, "no CTA pair of the tensor-core GEMM fits on the device");
@@ -787,12 +854,13 @@ static int tc_setup(DeviceInfo* info, int* max_pairs) {
     return BYBYCU_OK;
 }
 
+template <bool EXACT>
 static int tc_prepare(const GemmArgs& a, DeviceInfo* info, int* max_pairs) {
     if (!tc_supports(a))
         return set_error(BYBYCU_ERR_SHAPE,
                          "tensor-core route needs format 2, K %% 256 == 0, 16-byte aligned x, packed and scales "
                          "(M=%d K=%d N=%d)", a.M, a.K, a.N);
-    return tc_setup<false>(info, max_pairs);
+    return tc_setup<false, EXACT>(info, max_pairs);
 }
 
 // The weights of one tensor-core GEMM: Q4B32 (nibbles and fp16 scales in `packed`) or
@@ -805,7 +873,7 @@ struct TcWeights {
 
 // The staging pass and the GEMM, with `xp` (M * K fp16) as the staging buffer.  Allocates
 // nothing.
-template <bool ASYM>
+template <bool ASYM, bool EXACT = false>
 static int tc_run(const GemmArgs& a, const TcWeights& wt, int max_pairs, void* xp) {
     const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
     const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
@@ -863,34 +931,40 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, int max_pairs, void* x
     cfg.stream = a.stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel<ASYM>, maps, p));
+    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel<ASYM, EXACT>, maps, p));
     return BYBYCU_OK;
 }
 
 // Stages through stream-ordered pool scratch and runs the GEMM.
-template <bool ASYM>
+template <bool ASYM, bool EXACT = false>
 static int tc_pooled(const GemmArgs& a, const TcWeights& wt, const DeviceInfo& info, int max_pairs) {
     const size_t xp_bytes = static_cast<size_t>(a.M) * a.K * 2;
     void* xp = nullptr;
     cudaMemPool_t pool = nullptr;
     if (int rc = scratch_pool(info.device, &pool)) return rc;
     BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
-    const int rc = tc_run<ASYM>(a, wt, max_pairs, xp);
+    const int rc = tc_run<ASYM, EXACT>(a, wt, max_pairs, xp);
     const cudaError_t fe = cudaFreeAsync(xp, a.stream);
     if (rc) return rc;
     if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc scratch)");
     return BYBYCU_OK;
 }
 
-int launch_tc(const GemmArgs& a) {
+// Q4B32 on the tensor cores: exact weight terms (route TC), or each weight rounded once to
+// fp16 (route TC_FP16W, the reference's cooperative-matrix lowering).
+int launch_tc(const GemmArgs& a, bool fp16_weights) {
     if (a.fmt == BYBYCU_FMT_F16) return launch_tc_f16(a);
     DeviceInfo info;
     int max_pairs = 0;
-    if (int rc = tc_prepare(a, &info, &max_pairs)) return rc;
     TcWeights wt;
     wt.nibbles = a.packed;
     wt.scales = a.packed + a.scale_base;
-    return tc_pooled<false>(a, wt, info, max_pairs);
+    if (fp16_weights) {
+        if (int rc = tc_prepare<false>(a, &info, &max_pairs)) return rc;
+        return tc_pooled<false, false>(a, wt, info, max_pairs);
+    }
+    if (int rc = tc_prepare<true>(a, &info, &max_pairs)) return rc;
+    return tc_pooled<false, true>(a, wt, info, max_pairs);
 }
 
 bool tc_asym_supports(int M, int K, int N, int group, int n_groups, const void* x, const void* wq, const void* scales,
@@ -954,11 +1028,11 @@ int tc_static_scratch_load() {
     void* p = nullptr;
     if (int rc = static_scratch(&p)) return rc;
     int max_pairs = 0;
-    if (int rc = tc_setup<false>(&info, &max_pairs)) return rc;
+    if (int rc = tc_setup<false, true>(&info, &max_pairs)) return rc;
     cudaFuncAttributes fa;
     BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<false, tc::kPermQ4B32>));
     BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<true, tc::kPermQ4B32>));
-    BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::gemm_kernel<false>));
+    BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::gemm_kernel<false, true>));
     return BYBYCU_OK;
 }
 
@@ -971,13 +1045,13 @@ int launch_tc_static_scratch(const GemmArgs& a) {
                          kStaticScratchBytes >> 20, a.M, a.K, need, kStaticScratchBytes / 2);
     DeviceInfo info;
     int max_pairs = 0;
-    if (int rc = tc_prepare(a, &info, &max_pairs)) return rc;
+    if (int rc = tc_prepare<true>(a, &info, &max_pairs)) return rc;
     void* xp = nullptr;
     if (int rc = static_scratch(&xp)) return rc;
     TcWeights wt;
     wt.nibbles = a.packed;
     wt.scales = a.packed + a.scale_base;
-    return tc_run<false>(a, wt, max_pairs, xp);
+    return tc_run<false, true>(a, wt, max_pairs, xp);
 }
 
 }  // namespace bybycu

@@ -60,10 +60,15 @@ extern "C" {
 #define BYBYCU_DT_BF16 1
 
 /* kernel routes */
-#define BYBYCU_ROUTE_AUTO 0   /* GEMV for M <= 16, tensor-core GEMM above */
+#define BYBYCU_ROUTE_AUTO 0   /* GEMV for M <= 16 (M <= 32 with fp32 x), tensor-core GEMM above */
 #define BYBYCU_ROUTE_GEMV 1   /* decode GEMV: TMA-streamed weights, register dequant */
 #define BYBYCU_ROUTE_TC 2     /* prefill GEMM: tcgen05 MMAs, fp32 accumulators in TMEM */
 #define BYBYCU_ROUTE_SIMT 3   /* CUDA-core FP32 tile loop, every format and shape */
+#define BYBYCU_ROUTE_TC_FP16W 4  /* format 2 on the tensor cores with each weight q*s rounded once
+                                    to fp16 (the reference's cooperative-matrix lowering,
+                                    micro_kernel/tile_gemm.nim:322-325): half the MMAs of route TC,
+                                    which keeps every weight exact as two fp16 terms; only when
+                                    asked for (AUTO never picks it) */
 
 /* ---- library / device -------------------------------------------------------------- */
 

@@ -29,6 +29,23 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
+PARITY_LOG = []
+
+
+@pytest.fixture(scope="session")
+def parity_log():
+    """Tests append (what, worst per-element error, bound) here; the terminal summary prints
+    every entry, so a green run still shows the measured worst cases."""
+    return PARITY_LOG
+
+
+def pytest_terminal_summary(terminalreporter):
+    if PARITY_LOG:
+        terminalreporter.write_sep("-", "measured parity (worst |got - want| / max(1, |want|) per element)")
+        for what, worst, bound in PARITY_LOG:
+            terminalreporter.write_line(f"{what}: {worst:.3e} (bound {bound:.0e})")
+
+
 @pytest.fixture(scope="session")
 def oracle_mod():
     from oracle import oracle as O

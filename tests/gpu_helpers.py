@@ -45,3 +45,11 @@ def assert_close(want, got, peak_tol, elem_tol=None, what=""):
     assert d.max() <= peak_tol * peak, f"{what}: max|diff| {d.max():.3e} peak {peak:.3f}"
     if elem_tol is not None:
         assert (d <= elem_tol * np.maximum(1.0, np.abs(want))).all(), f"{what}: per-element"
+
+
+def elem_err(want, got):
+    """The reference gate's metric (vulkan_driver.nim:2752-2754), worst element:
+    max |got - want| / max(1, |want|)."""
+    want = np.asarray(want, np.float64)
+    got = np.asarray(got, np.float64)
+    return float((np.abs(got - want) / np.maximum(1.0, np.abs(want))).max())

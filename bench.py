@@ -27,7 +27,8 @@ Algorithmic bytes per step: 295,501,824 weight + 8,192 x per rank + 513,024 logi
 * lm_head_m64  config C5 at M=64 (tensor-core route + device all-gather), TFLOP/s, checked.
 * c4_layer     config C4: the seven Llama-7B projections of one layer in sequence at
                M = 1, 16 and 128, each column-sharded and gathered over the N GPUs.
-* prefill      config C3 (M=2048, K=N=4096) TFLOP/s on the tensor-core route (N = 1).
+* prefill      config C3 (M=2048, K=N=4096) TFLOP/s on the tensor-core route with exact weights
+               (AUTO's), and prefill_fp16w on the one-rounding form (N = 1).
 * c1           config C1 (M=32, K=N=4096, x fp32) through the automatic route (N = 1).
 * q4_asym_decode / q4_asym_prefill / f16_decode / decode_x_f32 / ingest   (N = 1): the
                asymmetric Q4 data of matmul_q4, format 1 (fp16 weights), fp32 activation rows,
@@ -283,16 +284,26 @@ def call_steps(timer, fn, steps, warmup):
     longer than the host takes to queue every call (measured on one extra untimed call), so
     the device runs them back to back."""
     torch = timer.torch
+    fn(0)   # first call: one-time set-up of the route stays out of the measured host time
     timer.stream.synchronize()
     t0 = time.perf_counter()
     fn(0)
     host_s = time.perf_counter() - t0
     timer.stream.synchronize()
-    hold = int(4e6 + 2.0 * (steps + warmup) * host_s * 2.0e9)
+    if timer.world > 1:   # every rank holds its stream equally long (ranks wait for each other)
+        t = torch.tensor([host_s], dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+        timer.dist.all_reduce(t, op=timer.dist.ReduceOp.MAX)
+        host_s = float(t.item())
+    hold = int(min(4e6 + 2.0 * (steps + warmup) * host_s * 2.0e9, 4e8))
     ms = timer.run(lambda: [fn(i) for i in range(warmup)], lambda: [fn(warmup + i) for i in range(steps)],
                    hold_cycles=hold)
-    del torch
     return ms / steps
+
+
+def check_device(_lib):
+    code = _lib.device_error()
+    if code:
+        raise RuntimeError(f"device error {code} recorded by a kernel (bounded wait or range check)")
 
 
 def roofline(achieved, peak, unit, bound, peak_kind, traffic=None, source=None, **extra):
@@ -445,7 +456,7 @@ def main():
     head = ShardedProjection(ctx, N_HEAD, K_DEC, 1, SEED)
     per_ms = graph_steps(torch, timer, stream, head.launch, K, W)
     launches += K
-    assert _lib.device_error() == 0
+    check_device(_lib)
     value = head.bytes_whole_job() / (per_ms / 1e3) / 1e9
     achieved = head.bytes_per_rank() / (per_ms / 1e3) / 1e9
     check = head.check()
@@ -512,7 +523,7 @@ def main():
                 h64.bufs, h64.out = None, torch.empty(64, N_HEAD, dtype=torch.float32, device=dev)
             reps = min(K, 50)
             ms = call_steps(timer, h64.launch, reps, W)
-            assert _lib.device_error() == 0
+            check_device(_lib)
             ck = h64.check(n_cols=512)
             ck["pass"] = ck["finite"] and ck["max_abs_err_over_peak"] <= 1e-3
             fl = 2.0 * 64 * N_HEAD * K_DEC
@@ -549,7 +560,7 @@ def main():
                     ms = graph_steps(torch, timer, stream, layer, reps, W)
                 else:
                     ms = call_steps(timer, layer, reps, W)
-                assert _lib.device_error() == 0
+                check_device(_lib)
                 checks = [p.check(n_cols=256) for p in projs]
                 tol = 1e-4 if M <= 16 else 1e-3
                 ok = all(c["finite"] and c["max_abs_err_over_peak"] <= tol for c in checks)
@@ -622,7 +633,7 @@ def single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind):
     c2 = ShardedProjection(ctx, N_C2, K_DEC, 1, SEED + 11)
     c2_bytes = c2.bytes_per_rank()
     ms = graph_steps(torch, timer, stream, lambda i: c2.launch(i, route=_lib.ROUTE_GEMV), K, W)
-    assert _lib.device_error() == 0
+    check_device(_lib)
     ck = c2.check()
     ck["pass"] = ck["finite"] and ck["max_abs_err_over_peak"] <= 1e-4 and ck["max_elem_rel_err"] <= 1e-3
     gbs = c2_bytes / (ms / 1e3) / 1e9
@@ -645,7 +656,7 @@ def single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind):
     try:
         c1 = ShardedProjection(ctx, 4096, 4096, 32, SEED + 21, x_dtype=torch.float32)
         ms = graph_steps(torch, timer, stream, c1.launch, K, W)
-        assert _lib.device_error() == 0
+        check_device(_lib)
         ck = c1.check(n_cols=512)
         fl = 2.0 * 32 * 4096 * 4096
         byts = c1.bytes_per_rank()
@@ -671,21 +682,26 @@ def single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind):
                 sets.append((gb.Q4B32Weights(nib, sc, device=dev), synthetic_x(Mp, Kp, seed=SEED + 100 + c, device=dev),
                              torch.empty(Mp, Np, dtype=torch.bfloat16, device=dev)))
 
-            def pf(i):
-                wp, xp, op = sets[i % n_sets]
-                wp.matmul(xp, op, route=_lib.ROUTE_TC, stream=stream)
             reps = max(K, 20)
-            ms = call_steps(timer, pf, reps, W)
-            assert _lib.device_error() == 0
-            tf = 2.0 * Mp * Np * Kp / (ms / 1e3) / 1e12
-            extras["prefill"] = {
-                "value": round(tf, 2), "unit": "TFLOP/s", "workload": "C3 M=2048 K=N=4096 Q4B32, x bf16, bf16 out",
-                "ms_per_call": round(ms, 5), "calls": reps,
-                "roofline": roofline(tf, tc_peak, "TFLOP/s", "tensor", peak_kind,
-                                     profiled_traffic("tc_gemm_prefill_c3.md"),
-                                     "ncu --set full, one gemm_kernel launch: profiles/tc_gemm_prefill_c3.md"),
-                "includes": "every launch of the call (staging pass + tcgen05 GEMM)",
-                "l2": f"inputs larger than L2: {n_sets} rotating (W, x, out) sets ({n_sets * per_set >> 20} MiB)"}
+            for key, route, what, prof in (
+                    ("prefill", _lib.ROUTE_TC, "route TC (AUTO): every weight exact as two fp16 terms, twice the MMAs",
+                     "tc_gemm_prefill_c3.md"),
+                    ("prefill_fp16w", _lib.ROUTE_TC_FP16W,
+                     "route TC_FP16W: each weight rounded once to fp16 (the reference's cooperative lowering)",
+                     "tc_gemm_prefill_c3_fp16w.md")):
+                def pf(i, route=route):
+                    wp, xp, op = sets[i % n_sets]
+                    wp.matmul(xp, op, route=route, stream=stream)
+                ms = call_steps(timer, pf, reps, W)
+                check_device(_lib)
+                tf = 2.0 * Mp * Np * Kp / (ms / 1e3) / 1e12
+                extras[key] = {
+                    "value": round(tf, 2), "unit": "TFLOP/s", "workload": "C3 M=2048 K=N=4096 Q4B32, x bf16, bf16 out",
+                    "route": what, "ms_per_call": round(ms, 5), "calls": reps,
+                    "roofline": roofline(tf, tc_peak, "TFLOP/s", "tensor", peak_kind, profiled_traffic(prof),
+                                         f"ncu --set full, one gemm_kernel launch: profiles/{prof}"),
+                    "includes": "every launch of the call (staging pass + tcgen05 GEMM)",
+                    "l2": f"inputs larger than L2: {n_sets} rotating (W, x, out) sets ({n_sets * per_set >> 20} MiB)"}
             del sets
         except _lib.BybyCudaError as e:
             extras["prefill"] = {"error": str(e)}
@@ -729,7 +745,7 @@ def single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind):
                                "workload": "fused decode GEMV mode 1: RMSNorm(x), silu(x.Wg) * (x.Wu) + residual, "
                                            "Wg, Wu 11008 x 4096 asymmetric Q4, one launch",
                                "roofline": roofline(fb / (ms / 1e3) / 1e9, hbm_peak, "GB/s", "hbm", peak_kind)}
-        assert _lib.device_error() == 0
+        check_device(_lib)
         extras["q4_asym_decode"] = q4
         del qsets, pairs
     except _lib.BybyCudaError as e:
@@ -758,7 +774,7 @@ def single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind):
                                                 C.c_void_p(stream.cuda_stream)))
             reps = max(K, 20)
             ms = call_steps(timer, asym_call, reps, W)
-            assert _lib.device_error() == 0
+            check_device(_lib)
             tf = 2.0 * Mp * Np * Kp / (ms / 1e3) / 1e12
             extras["q4_asym_prefill"] = {
                 "value": round(tf, 2), "unit": "TFLOP/s", "ms_per_call": round(ms, 5), "calls": reps,
@@ -782,7 +798,7 @@ def single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind):
             wh, o = hsets[i % n_sets]
             gb.tile_gemm(1, xh, wh, o, M=1, K=K_DEC, N=N_C2, route=_lib.ROUTE_GEMV, stream=stream)
         ms = graph_steps(torch, timer, stream, f16, K, W)
-        assert _lib.device_error() == 0
+        check_device(_lib)
         hb = fbytes + K_DEC * 2 + N_C2 * 4
         extras["f16_decode"] = {"value": round(hb / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
                                 "us_per_launch": round(ms * 1e3, 3),

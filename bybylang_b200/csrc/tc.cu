@@ -61,33 +61,63 @@ constexpr uint32_t kAccCols = kBN;                 // one accumulator buffer: a 
 constexpr uint32_t kAOff = 2 * kAccCols;           // A slots after the two accumulator buffers
 constexpr uint32_t kACols = kXK / 2;               // A slot: two fp16 per column
 static_assert(kAOff + kASlots * kACols <= kTmemCols, "tensor memory budget");
-static_assert(kStages % kASlots == 0 && kASlots % 2 == 0, "stage i uses A slot i % kASlots; dequant groups alternate");
-
-constexpr uint32_t kOffX = 0;
-constexpr uint32_t kOffW = kOffX + kStages * kXStageBytes;
-// barriers: full, x_empty [kStages]; a_empty [kASlots]; w_full, w_empty [kWStages];
-// d_full, d_empty [2]; done; then the TMEM base address and the abort flag
-constexpr uint32_t kNumBars = 2 * kStages + kASlots + 2 * kWStages + 5;
 // Arrivals that complete a stage on rank 0: its own TMA (with the bytes), the odd CTA's relay
 // and the eight dequant warps of the pair.  The MMA thread polls this one barrier per stage:
 // every shared-memory access of that thread stalls it for ~140 cycles while the tensor core
 // streams operands, so it makes one per eight MMAs.
 constexpr uint32_t kFullArrivals = 1 + 1 + 8;
-// The rest of the layout depends on the weight format: a scale stage holds fp16 scales
-// (Q4B32) or fp32 scales followed by fp32 zero points (asymmetric Q4) of 128 rows x 8 blocks.
-template <bool ASYM>
-struct Lay {
+// A scale stage holds fp16 scales (Q4B32) or fp32 scales followed by fp32 zero points
+// (asymmetric Q4) of 128 rows x 8 blocks; the rest of the layout is in Cfg below.
+
+// Token tiles of BN tokens: the MMA's N, the token rows each CTA of the pair loads (BN / 2)
+// and the instruction descriptor.  BN = 128 for prefill; 16, 32 or 64 for a few rows, so that
+// no MMA cycle goes to token columns that do not exist.
+template <int BN>
+struct TokTile {
+    static_assert(BN == 16 || BN == 32 || BN == 64 || BN == 128, "token tile");
+    static constexpr int kTokCta = BN / 2;
+    static constexpr uint32_t kXStageBytes = kTokCta * kXK * 2;
+    static constexpr uint32_t kXSubBytes = kTokCta * kXSub * 2;
+    // kind::f16, D fp32, A and B fp16, both K-major, M = 256 (the pair), N = BN
+    static constexpr uint32_t kIdesc = (1u << 4) | (uint32_t(BN >> 3) << 17) | (uint32_t(kRowsPair >> 4) << 24);
+};
+
+// The layout of one instantiation of the Q4 GEMM kernel.
+template <bool ASYM, bool EXACT, int BN>
+struct Cfg {
+    using T = TokTile<BN>;
+    // Two accumulator buffers (the epilogue drains one while the MMAs fill the other), or one
+    // when exact weights in a 128-token tile need the tensor memory for a third A-slot pair:
+    // with two pairs the dequantiser of stage s + 2 waits for the MMAs of stage s and then
+    // has less time than one stage's MMAs to fill its slots.
+    static constexpr int kAccBufs = (EXACT && BN == 128) ? 1 : 2;
+    static constexpr uint32_t kAOff = kAccBufs * BN;
+    static constexpr uint32_t kSlotCols = EXACT ? 2 * kACols : kACols;   // tensor memory of one stage's A
+    static constexpr int kAStagesFit = static_cast<int>((kTmemCols - kAOff) / kSlotCols);
+    static constexpr int kAStages = kAStagesFit > 8 ? 8 : kAStagesFit;   // A stages in flight
+    // few tokens make a stage's MMAs short: a deeper weight ring keeps the stream in flight
+    static constexpr int kWStages = BN >= 128 ? 3 : 6;
     static constexpr uint32_t kSBytes = ASYM ? 2 * kRowsCta * (kWK / 32) * 4 : kSStageBytes;
-    static constexpr uint32_t kZOff = kSBytes / 2;    // zero points inside an asymmetric scale stage
+    static constexpr uint32_t kZOff = kSBytes / 2;
+    static constexpr uint32_t kOffX = 0;
+    static constexpr uint32_t kOffW = kOffX + kStages * T::kXStageBytes;
     static constexpr uint32_t kOffS = kOffW + kWStages * kWStageBytes;
+    // barriers: full, x_empty [kStages]; a_empty [kAStages]; w_full, w_empty [kWStages];
+    // d_full, d_empty [2]; done
+    static constexpr uint32_t kNumBars = 2 * kStages + kAStages + 2 * kWStages + 5;
     static constexpr uint32_t kOffBar = kOffS + kWStages * kSBytes;
     static constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
-    static constexpr uint32_t kSmemBytes = kOffAbort + 4 + 1024;  // + alignment slack
-    // more than half an SM's shared memory: one CTA per SM, whatever the register count
-    static_assert(kSmemBytes > 116 * 1024 && kSmemBytes <= 227 * 1024, "one CTA per SM");
+    static constexpr uint32_t kUsed = kOffAbort + 4 + 1024;   // + alignment slack
+    // more than half an SM's shared memory: one CTA per SM, so that no second CTA waits for
+    // the tensor memory this one allocates
+    static constexpr uint32_t kSmemBytes = kUsed > 117 * 1024 ? kUsed : 117 * 1024;
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+    static_assert(kAStages >= 2, "tensor memory budget");
 };
-constexpr uint32_t kSmemBytes = Lay<false>::kSmemBytes;
+// the largest shared-memory request of any instantiation (asymmetric scales, 128 tokens)
+constexpr uint32_t kSmemBytes = Cfg<true, false, 128>::kSmemBytes > Cfg<false, true, 128>::kSmemBytes
+                                    ? Cfg<true, false, 128>::kSmemBytes : Cfg<false, true, 128>::kSmemBytes;
 
 // Instruction descriptor of kind::f16: D fp32, A and B fp16, both K-major, M=256, N=128.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(kBN >> 3) << 17) |
@@ -206,7 +236,7 @@ __device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint32_t a_tmem, uint6
 // so a stage is freed as soon as possible without a commit between two queued MMAs.
 __device__ __forceinline__ void mma_pair_stage(uint32_t d_tmem, uint32_t a0, const uint64_t (&b)[8],
                                                uint32_t accumulate, uint32_t release, uint32_t x_bar,
-                                               uint32_t a_bar) {
+                                               uint32_t a_bar, uint32_t idesc = kIdesc) {
     asm volatile(
         "{\n\t.reg .pred e, p, q, r;\n\t"
         "elect.sync _|e, 0xffffffff;\n\t"
@@ -223,7 +253,7 @@ __device__ __forceinline__ void mma_pair_stage(uint32_t d_tmem, uint32_t a0, con
         "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%13], %14, %3, q;\n\t"
         "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%15], %16, %3, q;\n\t"
         "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%17], %18, %3, q;\n\t}" ::"r"(d_tmem),
-        "r"(a0), "r"(accumulate), "r"(kIdesc), "l"(b[0]), "r"(a0 + 8), "l"(b[1]), "r"(a0 + 16), "l"(b[2]),
+        "r"(a0), "r"(accumulate), "r"(idesc), "l"(b[0]), "r"(a0 + 8), "l"(b[1]), "r"(a0 + 16), "l"(b[2]),
         "r"(a0 + 24), "l"(b[3]), "r"(a0 + 32), "l"(b[4]), "r"(a0 + 40), "l"(b[5]), "r"(a0 + 48), "l"(b[6]),
         "r"(a0 + 56), "l"(b[7]), "r"(release), "r"(x_bar), "r"(a_bar), "h"(static_cast<uint16_t>(0x3))
         : "memory");
@@ -231,7 +261,8 @@ __device__ __forceinline__ void mma_pair_stage(uint32_t d_tmem, uint32_t a0, con
 
 // The low weight term of an exact-weight stage: eight more MMAs from A slot `a0`, with the same
 // activation descriptors, accumulating into the same D (issued right after mma_pair_stage).
-__device__ __forceinline__ void mma_pair_accumulate8(uint32_t d_tmem, uint32_t a0, const uint64_t (&b)[8]) {
+__device__ __forceinline__ void mma_pair_accumulate8(uint32_t d_tmem, uint32_t a0, const uint64_t (&b)[8],
+                                                     uint32_t idesc) {
     asm volatile(
         "{\n\t.reg .pred e, q;\n\t"
         "elect.sync _|e, 0xffffffff;\n\t"
@@ -244,7 +275,7 @@ __device__ __forceinline__ void mma_pair_accumulate8(uint32_t d_tmem, uint32_t a
         "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%12], %13, %2, q;\n\t"
         "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%14], %15, %2, q;\n\t"
         "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%16], %17, %2, q;\n\t}" ::"r"(d_tmem),
-        "r"(a0), "r"(kIdesc), "l"(b[0]), "r"(a0 + 8), "l"(b[1]), "r"(a0 + 16), "l"(b[2]), "r"(a0 + 24), "l"(b[3]),
+        "r"(a0), "r"(idesc), "l"(b[0]), "r"(a0 + 8), "l"(b[1]), "r"(a0 + 16), "l"(b[2]), "r"(a0 + 24), "l"(b[3]),
         "r"(a0 + 32), "l"(b[4]), "r"(a0 + 40), "l"(b[5]), "r"(a0 + 48), "l"(b[6]), "r"(a0 + 56), "l"(b[7])
         : "memory");
 }
@@ -279,6 +310,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
         : TC_OUT32(v)
+        : "r"(taddr)
+        : "memory");
+}
+
+// This warp's 32 lanes, 16 consecutive 32-bit columns from `taddr`.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr)
         : "memory");
 }
@@ -414,20 +456,22 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x
 }
 
 
-// The epilogue warps of both GEMM kernels: accumulator buffer t % 2 of each of this CTA's
-// tiles back from tensor memory (tcgen05.ld, one 32-column slice at a time) and out to
-// out[token][feature]; each warp owns the TMEM lane quarter `quarter` (32 features) and
+// The epilogue warps of the GEMM kernels: accumulator buffer t % ACCB of each of this CTA's
+// tiles of BN tokens back from tensor memory (tcgen05.ld, 32 or 16 columns at a time) and out
+// to out[token][feature]; each warp owns the TMEM lane quarter `quarter` (32 features) and
 // frees the buffer on rank 0 when done.
-__device__ __forceinline__ void epilogue_tiles(const Params& p, uint32_t tmem, uint64_t* d_full, uint64_t* d_empty,
-                                               volatile int* s_abort, int my_tiles, int pair, int pairs,
-                                               uint32_t rank, int quarter, int lane) {
+template <int BN, int ACCB>
+__device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem, uint64_t* d_full,
+                                                 uint64_t* d_empty, volatile int* s_abort, int my_tiles, int pair,
+                                                 int pairs, uint32_t rank, int quarter, int lane) {
+    constexpr int kChunk = BN < 32 ? BN : 32;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t lead_d_empty = map_to_rank(d_empty, 0);
     for (int t = 0; t < my_tiles; ++t) {
-        const int b = t & 1, u = t >> 1;
+        const int b = t % ACCB, u = t / ACCB;
         const int tile = pair + t * pairs;
         const int feat = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta + quarter * 32 + lane;
-        const int tok0 = (tile / p.tiles_n) * kBN;
+        const int tok0 = (tile / p.tiles_n) * BN;
         const bool ok = __all_sync(0xffffffffu, wait_bar(&d_full[b], u & 1, kDevErrMmaWait));
         if (!ok) {
             *s_abort = 1;
@@ -436,23 +480,24 @@ __device__ __forceinline__ void epilogue_tiles(const Params& p, uint32_t tmem, u
         tc_fence_after();
         const bool feat_ok = feat < p.N;
 #pragma unroll 1
-        for (int c0 = 0; c0 < kBN; c0 += 32) {
+        for (int c0 = 0; c0 < BN; c0 += kChunk) {
             uint32_t v[32];
-            tmem_ld32(tmem + lane_addr + b * kAccCols + c0, v);
+            if constexpr (kChunk == 32) tmem_ld32(tmem + lane_addr + b * BN + c0, v);
+            else tmem_ld16(tmem + lane_addr + b * BN + c0, v);
             tc_wait_ld();
             if (feat_ok) {
-                const int nt = min(32, p.M - (tok0 + c0));
+                const int nt = min(kChunk, p.M - (tok0 + c0));
                 if (p.out_bf16) {
                     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + p.out_col0 + feat +
                                        static_cast<int64_t>(tok0 + c0) * p.out_ld;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
+                    for (int j = 0; j < kChunk; ++j)
                         if (j < nt) o[j * p.out_ld] = __float2bfloat16_rn(__uint_as_float(v[j]));
                 } else {
                     float* o = reinterpret_cast<float*>(p.out) + p.out_col0 + feat +
                                static_cast<int64_t>(tok0 + c0) * p.out_ld;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
+                    for (int j = 0; j < kChunk; ++j)
                         if (j < nt) o[j * p.out_ld] = __uint_as_float(v[j]);
                 }
             }
@@ -463,17 +508,25 @@ __device__ __forceinline__ void epilogue_tiles(const Params& p, uint32_t tmem, u
     }
 }
 
+// The 128-token, two-buffer form (the format-1 kernel's).
+__device__ __forceinline__ void epilogue_tiles(const Params& p, uint32_t tmem, uint64_t* d_full, uint64_t* d_empty,
+                                               volatile int* s_abort, int my_tiles, int pair, int pairs,
+                                               uint32_t rank, int quarter, int lane) {
+    epilogue_tiles_t<kBN, 2>(p, tmem, d_full, d_empty, s_abort, my_tiles, pair, pairs, rank, quarter, lane);
+}
+
 // ---------------------------------------------------------------------------------------
 // The GEMM kernel (launched as clusters of two CTAs; rank 0 issues the MMAs)
 // ---------------------------------------------------------------------------------------
 // EXACT (Q4B32 only): the weights enter as the two exact fp16 terms of dequant_word_exact, in
-// a pair of A slots per stage (two stages in flight instead of four), sixteen MMAs per stage.
-template <bool ASYM, bool EXACT = false>
+// a pair of A slots per stage, sixteen MMAs per stage.  BN: tokens per pair tile (Cfg).
+template <bool ASYM, bool EXACT, int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
     static_assert(!(ASYM && EXACT), "the exact weight split is for Q4B32");
-    using L = Lay<ASYM>;
-    // A slots: one per stage (kASlots stages in flight), or a pair per stage when EXACT
-    constexpr int kAStages = EXACT ? kASlots / 2 : kASlots;
+    using L = Cfg<ASYM, EXACT, BN>;
+    using T = TokTile<BN>;
+    constexpr int kAStages = L::kAStages;   // A stages in flight (a slot, or a slot pair when EXACT)
+    constexpr int kWSt = L::kWStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -484,9 +537,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     uint64_t* full = bars;
     uint64_t* x_empty = bars + kStages;          // the pair's MMAs finished with the activation stage
     uint64_t* a_empty = bars + 2 * kStages;      // ... and with the A slot
-    uint64_t* w_full = a_empty + kASlots;
-    uint64_t* w_empty = w_full + kWStages;
-    uint64_t* d_full = w_empty + kWStages;       // [2] accumulator buffer complete
+    uint64_t* w_full = a_empty + kAStages;
+    uint64_t* w_empty = w_full + kWSt;
+    uint64_t* d_full = w_empty + kWSt;           // [2] accumulator buffer complete
     uint64_t* d_empty = d_full + 2;              // [2] (rank 0) both epilogues read it
     uint64_t* done_bar = d_full + 4;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::kOffTmemSlot);
@@ -500,8 +553,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             mbar_init(&full[i], leader ? kFullArrivals : 1);
             mbar_init(&x_empty[i], 1);
         }
-        for (int i = 0; i < kASlots; ++i) mbar_init(&a_empty[i], 1);
-        for (int i = 0; i < kWStages; ++i) {
+        for (int i = 0; i < kAStages; ++i) mbar_init(&a_empty[i], 1);
+        for (int i = 0; i < kWSt; ++i) {
             mbar_init(&w_full[i], 1);
             mbar_init(&w_empty[i], 8);       // both dequant groups
         }
@@ -532,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             int issued = 0;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
                 const int tile = pair + t * pairs;
-                const int tok = (tile / p.tiles_n) * kBN + static_cast<int>(rank) * kTokCta;
+                const int tok = (tile / p.tiles_n) * BN + static_cast<int>(rank) * T::kTokCta;
                 for (int ks = 0; ks < n_ks; ++ks) {
                     const int s = issued % kStages, r = issued / kStages;
                     if (r > 0 && !wait_bar(&x_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
@@ -540,10 +593,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         break;
                     }
                     if (*s_abort) break;
-                    mbar_arrive_expect_tx(&full[s], kXStageBytes);
-                    uint8_t* dst = smem + kOffX + s * kXStageBytes;
+                    mbar_arrive_expect_tx(&full[s], T::kXStageBytes);
+                    uint8_t* dst = smem + L::kOffX + s * T::kXStageBytes;
                     tma_load_2d(dst, &maps.x, &full[s], ks * kXK, tok);
-                    tma_load_2d(dst + kXSubBytes, &maps.x, &full[s], ks * kXK + kXSub, tok);
+                    tma_load_2d(dst + T::kXSubBytes, &maps.x, &full[s], ks * kXK + kXSub, tok);
                     ++issued;
                 }
             }
@@ -581,14 +634,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 const int tile = pair + t * pairs;
                 const int row0 = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta;
                 for (int kw = 0; kw < n_kw; ++kw) {
-                    const int s = issued % kWStages, r = issued / kWStages;
+                    const int s = issued % kWSt, r = issued / kWSt;
                     if (r > 0 && !wait_bar(&w_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
                         *s_abort = 1;
                         break;
                     }
                     if (*s_abort) break;
                     mbar_arrive_expect_tx(&w_full[s], kWStageBytes + L::kSBytes);
-                    tma_load_2d_hint(smem + kOffW + s * kWStageBytes, &maps.w, &w_full[s], kw * (kWK / 2), row0, policy);
+                    tma_load_2d_hint(smem + L::kOffW + s * kWStageBytes, &maps.w, &w_full[s], kw * (kWK / 2), row0, policy);
                     tma_load_2d_hint(smem + L::kOffS + s * L::kSBytes, &maps.s, &w_full[s], kw * (kWK / 32), row0, policy);
                     if constexpr (ASYM)
                         tma_load_2d_hint(smem + L::kOffS + s * L::kSBytes + L::kZOff, &maps.z, &w_full[s], kw * (kWK / 32),
@@ -596,8 +649,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     ++issued;
                 }
             }
-            for (int it = issued > kWStages ? issued - kWStages : 0; it < issued; ++it)
-                if (!wait_bar(&w_full[it % kWStages], (it / kWStages) & 1, kDevErrDrainWait)) break;
+            for (int it = issued > kWSt ? issued - kWSt : 0; it < issued; ++it)
+                if (!wait_bar(&w_full[it % kWSt], (it / kWSt) & 1, kDevErrDrainWait)) break;
         }
     } else if (warp == 1) {
         // ------------------------------------------------- MMA issuer (rank 0, whole warp)
@@ -611,13 +664,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             };
             int consumed = 0, pending = -1;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
-                const int b = t & 1, u = t >> 1;
+                const int b = t % L::kAccBufs, u = t / L::kAccBufs;
                 if (u > 0 && !__all_sync(0xffffffffu, wait_bar(&d_empty[b], (u - 1) & 1, kDevErrMmaWait))) {
                     *s_abort = 1;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem + b * kAccCols;
+                const uint32_t d_tmem = tmem + b * BN;
                 bool ok = true;
                 for (int ks = 0; ks < n_ks; ++ks) {
                     const int s = consumed % kStages, r = consumed / kStages;
@@ -626,18 +679,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t bdesc = sw128_desc(base + kOffX + s * kXStageBytes);
-                    const uint32_t a0 = tmem + kAOff + (EXACT ? 2 : 1) * (consumed % kAStages) * kACols;
+                    const uint64_t bdesc = sw128_desc(base + L::kOffX + s * T::kXStageBytes);
+                    const uint32_t a0 = tmem + L::kAOff + (EXACT ? 2 : 1) * (consumed % kAStages) * kACols;
                     // 16-K steps advance 32 bytes inside a 128-byte swizzle row, then jump to
                     // the next 64-K box
                     uint64_t bk[8];
 #pragma unroll
                     for (int k16 = 0; k16 < kXK / 16; ++k16)
-                        bk[k16] = bdesc + static_cast<uint64_t>((k16 >> 2) * (kXSubBytes >> 4) + (k16 & 3) * 2);
+                        bk[k16] = bdesc + static_cast<uint64_t>((k16 >> 2) * (T::kXSubBytes >> 4) + (k16 & 3) * 2);
                     const int pv = pending >= 0 ? pending : 0;
                     mma_pair_stage(d_tmem, a0, bk, ks != 0, pending >= 0, smem_u32(&x_empty[pv % kStages]),
-                                   smem_u32(&a_empty[pv % kAStages]));
-                    if constexpr (EXACT) mma_pair_accumulate8(d_tmem, a0 + kACols, bk);
+                                   smem_u32(&a_empty[pv % kAStages]), T::kIdesc);
+                    if constexpr (EXACT) mma_pair_accumulate8(d_tmem, a0 + kACols, bk, T::kIdesc);
                     pending = consumed;
                     ++consumed;
                 }
@@ -667,12 +720,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         bool ok = true;
         for (int t = 0; t < my_tiles && ok; ++t) {
             for (int kw = 0; kw < n_kw && ok; ++kw) {
-                const int ws = w_used % kWStages;
-                ok = wait_bar(&w_full[ws], (w_used / kWStages) & 1, kDevErrFullWait) && !*s_abort;
+                const int ws = w_used % kWSt;
+                ok = wait_bar(&w_full[ws], (w_used / kWSt) & 1, kDevErrFullWait) && !*s_abort;
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
                 // this group's four 32-blocks of the weight stage: c = 4 * grp + h
-                const uint32_t wrow = base + kOffW + ws * kWStageBytes + row * 128;
+                const uint32_t wrow = base + L::kOffW + ws * kWStageBytes + row * 128;
                 uint4 chunk[4];
 #pragma unroll
                 for (int h = 0; h < 4; ++h) chunk[h] = lds_u128(wrow + (((4 * grp + h) ^ (row & 7)) << 4));
@@ -712,11 +765,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                             dequant_word_asym(u.z, sv[blk], mz[blk], &col[16 * h + 8]);
                             dequant_word_asym(u.w, sv[blk], mz[blk], &col[16 * h + 12]);
                         }
-                        tmem_st32(tmem + lane_addr + kAOff + slot * kACols + half * 32, col);
+                        tmem_st32(tmem + lane_addr + L::kAOff + slot * kACols + half * 32, col);
                     }
                 } else if constexpr (EXACT) {
                     const uint32_t sw0 = grp ? sc.z : sc.x, sw1 = grp ? sc.w : sc.y;
-                    const uint32_t a_hi = tmem + lane_addr + kAOff + 2 * slot * kACols;
+                    const uint32_t a_hi = tmem + lane_addr + L::kAOff + 2 * slot * kACols;
 #pragma unroll
                     for (int half = 0; half < 2; ++half) {
                         const uint32_t pr = half ? sw1 : sw0;              // two blocks' fp16 scales
@@ -753,7 +806,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         dequant_word(u.z, sv, s16, &col[16 * h + 8]);
                         dequant_word(u.w, sv, s16, &col[16 * h + 12]);
                     }
-                    tmem_st32(tmem + lane_addr + kAOff + slot * kACols + half * 32, col);
+                    tmem_st32(tmem + lane_addr + L::kAOff + slot * kACols + half * 32, col);
                 }
                 }
                 tc_wait_st();
@@ -765,7 +818,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (!ok) *s_abort = 1;
     } else {
         // ---------------------------------------------------------------------- epilogue
-        epilogue_tiles(p, tmem, d_full, d_empty, s_abort, my_tiles, pair, pairs, rank, warp & 3, lane);
+        epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_tiles, pair, pairs, rank, warp & 3,
+                                          lane);
     }
     tc_fence_before();
     __syncthreads();
@@ -821,8 +875,13 @@ static int scratch_pool(int device, cudaMemPool_t* pool) {
 }
 
 
-// Device info, the kernel attribute and the number of CTA pairs that fit at once.
-template <bool ASYM, bool EXACT = false>
+// Token tile of an M-row call: the smallest of 16, 32 and 64 tokens that holds every row, else
+// 128 (then the rows take ceil(M / 128) tiles).
+static int tc_token_tile(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+
+// Device info, the kernel attribute and the number of CTA pairs that fit at once, per kernel
+// instantiation and device.
+template <bool ASYM, bool EXACT, int BN>
 static int tc_setup(DeviceInfo* info, int* max_pairs) {
     if (int rc = current_device_info(info)) return rc;
     static std::once_flag once[64];
@@ -830,10 +889,10 @@ static int tc_setup(DeviceInfo* info, int* max_pairs) {
     static int pairs[64];
     const int dev = info->device;
     if (dev < 0 || dev >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", dev);
-    constexpr uint32_t smem = tc::Lay<ASYM>::kSmemBytes;
+    constexpr uint32_t smem = tc::Cfg<ASYM, EXACT, BN>::kSmemBytes;
     std::call_once(once[dev], [&] {
-        prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel<ASYM, EXACT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(smem));
+        prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel<ASYM, EXACT, BN>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (prep_rc[dev] != cudaSuccess) return;
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
@@ -846,7 +905,7 @@ static int tc_setup(DeviceInfo* info, int* max_pairs) {
         cfg.dynamicSmemBytes = smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        prep_rc[dev] = cudaOccupancyMaxActiveClusters(&pairs[dev], tc::gemm_kernel<ASYM, EXACT>, &cfg);
+        prep_rc[dev] = cudaOccupancyMaxActiveClusters(&pairs[dev], tc::gemm_kernel<ASYM, EXACT, BN>, &cfg);
     });
     if (prep_rc[dev] != cudaSuccess) return cuda_fail(prep_rc[dev], "tensor-core GEMM set-up");
     if (pairs[dev] < 1) return set_error(BYBYCU_ERR_DEVICE, "no CTA pair of the tensor-core GEMM fits on the device");
@@ -854,13 +913,12 @@ static int tc_setup(DeviceInfo* info, int* max_pairs) {
     return BYBYCU_OK;
 }
 
-template <bool EXACT>
-static int tc_prepare(const GemmArgs& a, DeviceInfo* info, int* max_pairs) {
+static int tc_check(const GemmArgs& a) {
     if (!tc_supports(a))
         return set_error(BYBYCU_ERR_SHAPE,
                          "tensor-core route needs format 2, K %% 256 == 0, 16-byte aligned x, packed and scales "
                          "(M=%d K=%d N=%d)", a.M, a.K, a.N);
-    return tc_setup<false, EXACT>(info, max_pairs);
+    return BYBYCU_OK;
 }
 
 // The weights of one tensor-core GEMM: Q4B32 (nibbles and fp16 scales in `packed`) or
@@ -871,10 +929,13 @@ struct TcWeights {
     const float* zeros = nullptr;
 };
 
-// The staging pass and the GEMM, with `xp` (M * K fp16) as the staging buffer.  Allocates
-// nothing.
-template <bool ASYM, bool EXACT = false>
-static int tc_run(const GemmArgs& a, const TcWeights& wt, int max_pairs, void* xp) {
+// The staging pass and the GEMM with BN-token tiles, with `xp` (M * K fp16) as the staging
+// buffer.  Allocates nothing.
+template <bool ASYM, bool EXACT, int BN>
+static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp) {
+    DeviceInfo info;
+    int max_pairs = 0;
+    if (int rc = tc_setup<ASYM, EXACT, BN>(&info, &max_pairs)) return rc;
     const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
     const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
     constexpr int perm = ASYM ? tc::kPermAsym : tc::kPermQ4B32;
@@ -888,8 +949,8 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, int max_pairs, void* x
     memset(&maps, 0, sizeof maps);
     const uint64_t G = static_cast<uint64_t>(a.K / 32);
     int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xp, a.K, a.M,
-                                  static_cast<uint64_t>(a.K) * 2, tc::kXSub, tc::kTokCta, CU_TENSOR_MAP_SWIZZLE_128B,
-                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+                                  static_cast<uint64_t>(a.K) * 2, tc::kXSub, tc::TokTile<BN>::kTokCta,
+                                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (!rc)
         rc = encode_tensor_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wt.nibbles, a.K / 2, a.N, a.K / 2,
                                   tc::kWK / 2, tc::kRowsCta, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -907,7 +968,7 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, int max_pairs, void* x
     p.K = a.K;
     p.N = a.N;
     p.tiles_n = static_cast<int>(ceil_div(a.N, tc::kRowsPair));
-    const int64_t tiles = static_cast<int64_t>(p.tiles_n) * ceil_div(a.M, tc::kBN);
+    const int64_t tiles = static_cast<int64_t>(p.tiles_n) * ceil_div(a.M, BN);
     if (tiles > (1 << 30)) return set_error(BYBYCU_ERR_SHAPE, "tensor-core route: too many tiles (M=%d N=%d)", a.M, a.N);
     p.tiles = static_cast<int>(tiles);
     p.out = a.out;
@@ -927,23 +988,35 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, int max_pairs, void* x
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(tc::kThreads);
-    cfg.dynamicSmemBytes = tc::Lay<ASYM>::kSmemBytes;
+    cfg.dynamicSmemBytes = tc::Cfg<ASYM, EXACT, BN>::kSmemBytes;
     cfg.stream = a.stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel<ASYM, EXACT>, maps, p));
+    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel<ASYM, EXACT, BN>, maps, p));
     return BYBYCU_OK;
 }
 
+template <bool ASYM, bool EXACT>
+static int tc_run_rows(const GemmArgs& a, const TcWeights& wt, void* xp) {
+    switch (tc_token_tile(a.M)) {
+        case 16: return tc_run<ASYM, EXACT, 16>(a, wt, xp);
+        case 32: return tc_run<ASYM, EXACT, 32>(a, wt, xp);
+        case 64: return tc_run<ASYM, EXACT, 64>(a, wt, xp);
+        default: return tc_run<ASYM, EXACT, 128>(a, wt, xp);
+    }
+}
+
 // Stages through stream-ordered pool scratch and runs the GEMM.
-template <bool ASYM, bool EXACT = false>
-static int tc_pooled(const GemmArgs& a, const TcWeights& wt, const DeviceInfo& info, int max_pairs) {
+template <bool ASYM, bool EXACT>
+static int tc_pooled(const GemmArgs& a, const TcWeights& wt) {
+    DeviceInfo info;
+    if (int rc = current_device_info(&info)) return rc;
     const size_t xp_bytes = static_cast<size_t>(a.M) * a.K * 2;
     void* xp = nullptr;
     cudaMemPool_t pool = nullptr;
     if (int rc = scratch_pool(info.device, &pool)) return rc;
     BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
-    const int rc = tc_run<ASYM, EXACT>(a, wt, max_pairs, xp);
+    const int rc = tc_run_rows<ASYM, EXACT>(a, wt, xp);
     const cudaError_t fe = cudaFreeAsync(xp, a.stream);
     if (rc) return rc;
     if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc scratch)");
@@ -954,17 +1027,11 @@ static int tc_pooled(const GemmArgs& a, const TcWeights& wt, const DeviceInfo& i
 // fp16 (route TC_FP16W, the reference's cooperative-matrix lowering).
 int launch_tc(const GemmArgs& a, bool fp16_weights) {
     if (a.fmt == BYBYCU_FMT_F16) return launch_tc_f16(a);
-    DeviceInfo info;
-    int max_pairs = 0;
+    if (int rc = tc_check(a)) return rc;
     TcWeights wt;
     wt.nibbles = a.packed;
     wt.scales = a.packed + a.scale_base;
-    if (fp16_weights) {
-        if (int rc = tc_prepare<false>(a, &info, &max_pairs)) return rc;
-        return tc_pooled<false, false>(a, wt, info, max_pairs);
-    }
-    if (int rc = tc_prepare<true>(a, &info, &max_pairs)) return rc;
-    return tc_pooled<false, true>(a, wt, info, max_pairs);
+    return fp16_weights ? tc_pooled<false, false>(a, wt) : tc_pooled<false, true>(a, wt);
 }
 
 bool tc_asym_supports(int M, int K, int N, int group, int n_groups, const void* x, const void* wq, const void* scales,
@@ -975,7 +1042,7 @@ bool tc_asym_supports(int M, int K, int N, int group, int n_groups, const void* 
     if (reinterpret_cast<uintptr_t>(out) % 4 != 0) return false;
     DeviceInfo info;
     if (current_device_info(&info) != BYBYCU_OK) return false;
-    return info.cc_major == 10 && info.max_smem_optin >= static_cast<int>(tc::Lay<true>::kSmemBytes);
+    return info.cc_major == 10 && info.max_smem_optin >= static_cast<int>(tc::kSmemBytes);
 }
 
 int launch_tc_asym(int M, int K, int N, const float* x, const uint8_t* wq, const float* scales, const float* zeros,
@@ -983,9 +1050,6 @@ int launch_tc_asym(int M, int K, int N, const float* x, const uint8_t* wq, const
     if (!tc_asym_supports(M, K, N, 32, K / 32, x, wq, scales, zeros, out))
         return set_error(BYBYCU_ERR_SHAPE, "matmul_q4 tensor-core route needs group 32, K %% 256 == 0 and 16-byte "
                                            "aligned slots (M=%d K=%d N=%d)", M, K, N);
-    DeviceInfo info;
-    int max_pairs = 0;
-    if (int rc = tc_setup<true>(&info, &max_pairs)) return rc;
     GemmArgs a;
     a.M = M; a.K = K; a.N = N;
     a.x = x; a.x_dtype = BYBYCU_DT_F32;
@@ -996,7 +1060,7 @@ int launch_tc_asym(int M, int K, int N, const float* x, const uint8_t* wq, const
     wt.nibbles = wq;
     wt.scales = scales;
     wt.zeros = zeros;
-    return tc_pooled<true>(a, wt, info, max_pairs);
+    return tc_pooled<true, false>(a, wt);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1028,11 +1092,14 @@ int tc_static_scratch_load() {
     void* p = nullptr;
     if (int rc = static_scratch(&p)) return rc;
     int max_pairs = 0;
-    if (int rc = tc_setup<false, true>(&info, &max_pairs)) return rc;
+    DeviceInfo d;
+    if (int rc = tc_setup<false, true, 16>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<false, true, 32>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<false, true, 64>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<false, true, 128>(&d, &max_pairs)) return rc;
     cudaFuncAttributes fa;
     BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<false, tc::kPermQ4B32>));
     BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<true, tc::kPermQ4B32>));
-    BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::gemm_kernel<false, true>));
     return BYBYCU_OK;
 }
 
@@ -1043,15 +1110,13 @@ int launch_tc_static_scratch(const GemmArgs& a) {
                          "static-scratch tensor-core GEMM stages M*K fp16 activations in a fixed %zu MiB array: "
                          "M=%d K=%d needs %zu bytes (at most M*K = %zu)",
                          kStaticScratchBytes >> 20, a.M, a.K, need, kStaticScratchBytes / 2);
-    DeviceInfo info;
-    int max_pairs = 0;
-    if (int rc = tc_prepare<true>(a, &info, &max_pairs)) return rc;
+    if (int rc = tc_check(a)) return rc;
     void* xp = nullptr;
     if (int rc = static_scratch(&xp)) return rc;
     TcWeights wt;
     wt.nibbles = a.packed;
     wt.scales = a.packed + a.scale_base;
-    return tc_run<false, true>(a, wt, max_pairs, xp);
+    return tc_run_rows<false, true>(a, wt, xp);
 }
 
 }  // namespace bybycu

@@ -291,6 +291,35 @@ def test_fused_mode1_silu_gate_up(N, norm, res):
     assert (err <= bound).all(), f"worst excess {(err - bound).max():.3e}"
 
 
+def test_fused_gate_up_pinned_to_reference_kernel(oracle_mod):
+    """The fused decode GEMV (mode 1 with RMSNorm and the residual) against the reference's own
+    nimf_cpu_matmul_q4 (oracle/_ref) for both products, then the fused shader's order on top
+    (backends/vulkan/q4_autotune.nim:194-325): x * gamma feeds the products, the RMS of the raw
+    x gives inv = 1 / sqrt(mean(x^2) + eps), gate and up are scaled by inv, silu(gate) * up,
+    then + residual.  Bound: the decode kernel's fixed-point bound on each product."""
+    O = oracle_mod
+    if not O.ref_available():
+        pytest.skip("oracle/_ref (the reference's CPU C) is not built")
+    K, N, eps = 4096, 11008, 1e-5
+    mats, x, gamma, r, xe, _ = _fused_case((N, N), K, 61, True, True)
+    got = _run_fused(1, mats, x, gamma, r, K, eps=eps)[0]
+    xg = (x[0] * gamma).astype(np.float32)[None, :]       # the shader's x[t] = raw * gamma[k + t]
+    g_raw, u_raw = (O.ref_matmul_q4(xg, wq, sc, zp, 1, K, N, 32, threads=8)[0].astype(np.float64)
+                    for wq, sc, zp in mats)
+    inv = 1.0 / np.sqrt(np.float32(np.sum(x[0].astype(np.float32) ** 2)) / np.float32(K) + np.float32(eps))
+    g, u = g_raw * inv, u_raw * inv
+    sig = 1.0 / (1.0 + np.exp(-g))
+    want = g * sig * u + r[:N].astype(np.float64)
+    wg, wu = (dequant_np(*m, K, 32) for m in mats)
+    dg, du = inv * _bound(wg, xe), inv * _bound(wu, xe)
+    dsilu = np.abs(sig * (1.0 + g * (1.0 - sig)))
+    bound = (dsilu + 1e-3) * np.abs(u) * dg + np.abs(g * sig) * du + dg * du + 1e-5 * np.abs(want) + 1e-6
+    err = np.abs(got - want)
+    assert np.isfinite(got).all()
+    assert (err <= bound).all(), f"worst excess {(err - bound).max():.3e}"
+    assert np.abs(got - want).max() <= 1e-3 * max(1.0, np.abs(want).max())
+
+
 def test_fused_session_api_and_unsupported():
     be = gb.GpuBackend.gbCuda
     K, N = 2048, 512

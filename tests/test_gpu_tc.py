@@ -155,7 +155,9 @@ def test_tc_fp16_weight_route(oracle_mod, parity_log):
     fast = run(2, M, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_TC_FP16W).cpu().numpy()
     assert_close(want, fast, TC_TOL, what="TC_FP16W")
     parity_log.append((f"{M}x{K}x{N} route TC_FP16W", elem_err(want, fast), 0))
-    s8 = (np.asarray(s, np.uint16) & 0xFFF8).astype(np.uint16)   # q * s exact in fp16
+    # q * s exact in fp16 (8 significant bits), and s / 16 still a normal fp16 number (s >= 2^-9),
+    # which the one-rounding form's high-nibble product goes through
+    s8 = (np.maximum(np.asarray(s, np.uint16), 0x1800) & 0xFFF8).astype(np.uint16)
     slot8, sb8 = q4_slot(p, s8)
     a = run(2, M, K, N, x, slot8, scale_base=sb8, route=_lib.ROUTE_TC_FP16W)
     b = run(2, M, K, N, x, slot8, scale_base=sb8, route=_lib.ROUTE_TC)

@@ -78,8 +78,6 @@ struct GemvParams {
     uint32_t z_off;                // ... at this offset inside the stage
     const __half* scales;          // packed + scale_base
     const uint8_t* x;              // activations [M, K] (global)
-    const uint8_t* packed;         // nibbles [N, K/2] (global)
-    int l2_prefetch;               // M = 1: chunks the ring cannot hold yet are prefetched into L2
     int x_elem;                    // 2 (bf16) or 4 (fp32)
     void* out;
     int out_bf16;
@@ -838,28 +836,6 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
     for (int q = 0; q < kM1Blocks; ++q) woff[q] = g * 128 + (((blk0 + q) ^ g) << 4) + 4 * t;
     bool waited = false;
 
-    if (p.l2_prefetch && p.n_chunks > p.stages) {
-        // The chunks of the first pass that the ring cannot hold yet: pulled into L2 now, while
-        // the previous launch still runs (this CTA is resident early through programmatic
-        // dependent launch), so that their copies after the ring frees up come from L2.  The
-        // weights never depend on the previous kernel.  One 128-byte line per request.
-        const int nu = min(upass, my_tiles);
-        const int64_t row0 = p.row_split ? tile_begin : static_cast<int64_t>(tile_begin) * kTileRows;
-        const int rows = static_cast<int>(min(static_cast<int64_t>(p.row_split ? nu : nu * kTileRows), p.N - row0));
-        const int c0 = p.stages, cn = p.n_chunks - p.stages;
-        const int lines_row = cn * (p.kc / 2) / 128;                  // nibble lines per row
-        const int slines_row = (cn * (p.kc / 32) * 2 + 127) / 128;     // scale lines per row
-        const int total = rows * (lines_row + slines_row);
-        const uint8_t* scales = reinterpret_cast<const uint8_t*>(p.scales);
-        for (int i = threadIdx.x; i < total; i += kM1Warps * 32) {
-            const int r = i / (lines_row + slines_row), l = i % (lines_row + slines_row);
-            const uint8_t* a = l < lines_row
-                ? p.packed + (row0 + r) * (p.K / 2) + c0 * (p.kc / 2) + l * 128
-                : scales + ((row0 + r) * p.G + c0 * (p.kc / 32)) * 2 + (l - lines_row) * 128;
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
-        }
-    }
-
     int s = 0, round = 0, chunk = 0, t0 = tile_begin;
     for (int it = 0; it < total_it; ++it) {
         // this pass: tiles nt, rows [row0, row_end)
@@ -1031,16 +1007,6 @@ gemv_m1_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
         if (++chunk == p.n_chunks) { chunk = 0; t0 += upass; }
     }
     gemv_gather_end(p.pg, kM1Warps * 32);
-}
-
-// BYBY_CUDA_GEMV_L2PF=1: the M = 1 kernel prefetches into L2 the chunks of its first pass that
-// do not fit in its ring (measurement switch; off by default).
-bool gemv_l2_prefetch() {
-    static const int on = [] {
-        const char* e = getenv("BYBY_CUDA_GEMV_L2PF");
-        return (e && e[0] == '1') ? 1 : 0;
-    }();
-    return on != 0;
 }
 
 bool pdl_enabled() {
@@ -1312,8 +1278,6 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     p.s_pitch = s_pitch;
     p.scales = reinterpret_cast<const __half*>(scale_ptr);
     p.x = static_cast<const uint8_t*>(a.x);
-    p.packed = a.packed;
-    p.l2_prefetch = m1 && gemv_l2_prefetch() ? 1 : 0;
     p.x_elem = xe;
     p.out = a.out;
     p.out_bf16 = a.out_dtype == BYBYCU_DT_BF16;

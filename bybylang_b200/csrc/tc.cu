@@ -46,11 +46,14 @@ constexpr int kStages = 8;          // activation stages in shared memory
 constexpr int kASlots = 4;          // dequantized weight (A) slots in tensor memory
 constexpr int kWStages = 3;         // weight stages in shared memory
 constexpr int kSubs = kWK / kXK;    // activation stages per weight stage
-// 16 warps: 0 X TMA, 1 MMA (even CTA) + TMEM alloc, 2 W TMA, 3 X relay (odd CTA),
-// 4-11 dequant (two groups of four: even / odd activation stages), 12-15 epilogue
-constexpr int kThreads = 512;
+// 20 warps: 0 X TMA, 1 MMA (even CTA) + TMEM alloc, 2 W TMA, 3 X relay (odd CTA),
+// 4-15 dequant (three groups of four: activation stages i with i % 3 = group), 16-19 epilogue.
+// The dequantisers are the kernel's throughput limit: a group needs longer to fill a stage's A
+// slot than the pair's MMAs need to consume it, so three groups work on three stages at once.
+constexpr int kThreads = 640;
 constexpr int kDequantWarp0 = 4;
-constexpr int kEpilogueWarp0 = 12;
+constexpr int kDequantGroups = 3;   // activation stage i is dequantised by group i % 3
+constexpr int kEpilogueWarp0 = kDequantWarp0 + 4 * kDequantGroups;
 
 constexpr uint32_t kXStageBytes = kTokCta * kXK * 2;         // 16 KiB per CTA
 constexpr uint32_t kXSubBytes = kTokCta * kXSub * 2;         // 8 KiB
@@ -86,15 +89,15 @@ struct TokTile {
 template <bool ASYM, bool EXACT, int BN>
 struct Cfg {
     using T = TokTile<BN>;
-    // Two accumulator buffers (the epilogue drains one while the MMAs fill the other), or one
-    // when exact weights in a 128-token tile need the tensor memory for a third A-slot pair:
-    // with two pairs the dequantiser of stage s + 2 waits for the MMAs of stage s and then
-    // has less time than one stage's MMAs to fill its slots.
-    static constexpr int kAccBufs = (EXACT && BN == 128) ? 1 : 2;
+    // Two accumulator buffers: the epilogue drains one while the MMAs fill the other.
+    static constexpr int kAccBufs = 2;
     static constexpr uint32_t kAOff = kAccBufs * BN;
     static constexpr uint32_t kSlotCols = EXACT ? 2 * kACols : kACols;   // tensor memory of one stage's A
     static constexpr int kAStagesFit = static_cast<int>((kTmemCols - kAOff) / kSlotCols);
     static constexpr int kAStages = kAStagesFit > 8 ? 8 : kAStagesFit;   // A stages in flight
+    // Dequantiser groups at work: at most one per A stage in flight, so that no group waits
+    // for a slot phase two rounds ahead (a phase-parity wait cannot tell those apart).
+    static constexpr int kGroups = kDequantGroups < kAStages ? kDequantGroups : kAStages;
     // few tokens make a stage's MMAs short: a deeper weight ring keeps the stream in flight
     static constexpr int kWStages = BN >= 128 ? 3 : 6;
     static constexpr uint32_t kSBytes = ASYM ? 2 * kRowsCta * (kWK / 32) * 4 : kSStageBytes;
@@ -303,6 +306,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
         TC_REG32(v)
+        : "memory");
+}
+// This warp's 32 lanes, 16 consecutive 32-bit columns from `taddr`.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
@@ -709,89 +721,88 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
     } else if (warp < kEpilogueWarp0) {
         // ------------------------------------------------------------------ dequantizers
-        // A weight stage (K=256) holds two activation stages; group 0 fills the even ones,
-        // group 1 the odd ones.  Each warp owns the TMEM lane quarter (warp % 4) = 32 rows.
+        // A weight stage (K=256) holds two activation stages (sub = 0, 1); activation stage i
+        // of this CTA's tiles is group (i % 3)'s.  Each warp owns the TMEM lane quarter
+        // (warp % 4) = 32 rows.
         const int grp = (warp - kDequantWarp0) >> 2;
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t lead_full = map_to_rank(full, 0);
-        int w_used = 0;
         bool ok = true;
-        for (int t = 0; t < my_tiles && ok; ++t) {
-            for (int kw = 0; kw < n_kw && ok; ++kw) {
-                const int ws = w_used % kWSt;
-                ok = wait_bar(&w_full[ws], (w_used / kWSt) & 1, kDevErrFullWait) && !*s_abort;
-                ok = __all_sync(0xffffffffu, ok);
-                if (!ok) break;
-                // this group's four 32-blocks of the weight stage: c = 4 * grp + h
-                const uint32_t wrow = base + L::kOffW + ws * kWStageBytes + row * 128;
-                uint4 chunk[4];
+        const int total = my_tiles * n_ks;
+        for (int i = grp; i < total && ok && grp < L::kGroups; i += L::kGroups) {
+            const int ks = i % n_ks;
+            const int wsg = (i / n_ks) * n_kw + ks / kSubs;         // weight stage, counted over tiles
+            const int sub = ks % kSubs;                             // which half of it
+            const int ws = wsg % kWSt;
+            ok = wait_bar(&w_full[ws], (wsg / kWSt) & 1, kDevErrFullWait) && !*s_abort;
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            // this stage's four 32-blocks of the weight stage: c = 4 * sub + h
+            const uint32_t wrow = base + L::kOffW + ws * kWStageBytes + row * 128;
+            uint4 chunk[4];
 #pragma unroll
-                for (int h = 0; h < 4; ++h) chunk[h] = lds_u128(wrow + (((4 * grp + h) ^ (row & 7)) << 4));
-                uint4 sc;
-                float4 sa, za;   // asymmetric: fp32 scales and zero points of blocks 4 grp .. 4 grp + 3
-                if constexpr (ASYM) {
-                    const uint32_t sb = base + L::kOffS + ws * L::kSBytes + row * 32 + grp * 16;
-                    sa = lds_v4f(sb);
-                    za = lds_v4f(sb + L::kZOff);
-                } else {
-                    sc = lds_u128(base + L::kOffS + ws * L::kSBytes + row * 16);
+            for (int h = 0; h < 4; ++h) chunk[h] = lds_u128(wrow + (((4 * sub + h) ^ (row & 7)) << 4));
+            uint4 sc;
+            float4 sa, za;   // asymmetric: fp32 scales and zero points of blocks 4 sub .. 4 sub + 3
+            if constexpr (ASYM) {
+                const uint32_t sb = base + L::kOffS + ws * L::kSBytes + row * 32 + sub * 16;
+                sa = lds_v4f(sb);
+                za = lds_v4f(sb + L::kZOff);
+            } else {
+                sc = lds_u128(base + L::kOffS + ws * L::kSBytes + row * 16);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&w_empty[ws]);   // the two groups of its halves release it
+            const int s = i % kStages;                          // its activation stage (full barrier)
+            const int slot = i % kAStages, r = i / kAStages;    // its A slot (pair, when EXACT)
+            if (r > 0) ok = wait_bar(&a_empty[slot], (r - 1) & 1, kDevErrEmptyWait);
+            ok = __all_sync(0xffffffffu, ok && !*s_abort);
+            if (!ok) break;
+            tc_fence_after();
+            if constexpr (ASYM) {
+                const __half2 sv[4] = {__float2half2_rn(sa.x), __float2half2_rn(sa.y), __float2half2_rn(sa.z),
+                                       __float2half2_rn(sa.w)};
+                const __half2 mz[4] = {__float2half2_rn(-za.x * sa.x), __float2half2_rn(-za.y * sa.y),
+                                       __float2half2_rn(-za.z * sa.z), __float2half2_rn(-za.w * sa.w)};
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t col[32];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int blk = 2 * half + h;
+                        const uint4 u = chunk[blk];
+                        dequant_word_asym(u.x, sv[blk], mz[blk], &col[16 * h + 0]);
+                        dequant_word_asym(u.y, sv[blk], mz[blk], &col[16 * h + 4]);
+                        dequant_word_asym(u.z, sv[blk], mz[blk], &col[16 * h + 8]);
+                        dequant_word_asym(u.w, sv[blk], mz[blk], &col[16 * h + 12]);
+                    }
+                    tmem_st32(tmem + lane_addr + L::kAOff + slot * kACols + half * 32, col);
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&w_empty[ws]);
-                ++w_used;
-                const int i = t * n_ks + kw * kSubs + grp;          // stage index; i % 2 == grp
-                const int s = i % kStages;                          // its activation stage (full barrier)
-                const int slot = i % kAStages, r = i / kAStages;    // its A slot (pair, when EXACT)
-                if (r > 0) ok = wait_bar(&a_empty[slot], (r - 1) & 1, kDevErrEmptyWait);
-                ok = __all_sync(0xffffffffu, ok && !*s_abort);
-                if (!ok) break;
-                tc_fence_after();
-                if constexpr (ASYM) {
-                    const __half2 sv[4] = {__float2half2_rn(sa.x), __float2half2_rn(sa.y), __float2half2_rn(sa.z),
-                                           __float2half2_rn(sa.w)};
-                    const __half2 mz[4] = {__float2half2_rn(-za.x * sa.x), __float2half2_rn(-za.y * sa.y),
-                                           __float2half2_rn(-za.z * sa.z), __float2half2_rn(-za.w * sa.w)};
+            } else if constexpr (EXACT) {
+                const uint32_t sw0 = sub ? sc.z : sc.x, sw1 = sub ? sc.w : sc.y;
+                const uint32_t a_hi = tmem + lane_addr + L::kAOff + 2 * slot * kACols;
+                // one block (16 columns of each term) at a time: 32 live column registers
 #pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        uint32_t col[32];
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int blk = 2 * half + h;
-                            const uint4 u = chunk[blk];
-                            dequant_word_asym(u.x, sv[blk], mz[blk], &col[16 * h + 0]);
-                            dequant_word_asym(u.y, sv[blk], mz[blk], &col[16 * h + 4]);
-                            dequant_word_asym(u.z, sv[blk], mz[blk], &col[16 * h + 8]);
-                            dequant_word_asym(u.w, sv[blk], mz[blk], &col[16 * h + 12]);
-                        }
-                        tmem_st32(tmem + lane_addr + L::kAOff + slot * kACols + half * 32, col);
-                    }
-                } else if constexpr (EXACT) {
-                    const uint32_t sw0 = grp ? sc.z : sc.x, sw1 = grp ? sc.w : sc.y;
-                    const uint32_t a_hi = tmem + lane_addr + L::kAOff + 2 * slot * kACols;
-#pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const uint32_t pr = half ? sw1 : sw0;              // two blocks' fp16 scales
-                        const uint32_t prh = pr & 0xFFF8FFF8u;             // s_hi of both
-                        const __half2 lo2 = __hsub2(bits_h2(pr), bits_h2(prh));   // s_lo, exact
-                        uint32_t hcol[32], lcol[32];
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const __half2 shi = h ? __high2half2(bits_h2(prh)) : __low2half2(bits_h2(prh));
-                            const __half2 slo = h ? __high2half2(lo2) : __low2half2(lo2);
-                            const uint4 u = chunk[2 * half + h];
-                            dequant_word_exact(u.x, shi, slo, &hcol[16 * h + 0], &lcol[16 * h + 0]);
-                            dequant_word_exact(u.y, shi, slo, &hcol[16 * h + 4], &lcol[16 * h + 4]);
-                            dequant_word_exact(u.z, shi, slo, &hcol[16 * h + 8], &lcol[16 * h + 8]);
-                            dequant_word_exact(u.w, shi, slo, &hcol[16 * h + 12], &lcol[16 * h + 12]);
-                        }
-                        tmem_st32(a_hi + half * 32, hcol);
-                        tmem_st32(a_hi + kACols + half * 32, lcol);
-                    }
-                } else {
-                // scales of blocks 4 grp .. 4 grp + 3: two 32-bit words of the row's eight
-                const uint32_t sw0 = grp ? sc.z : sc.x, sw1 = grp ? sc.w : sc.y;
+                for (int blk = 0; blk < 4; ++blk) {
+                    const uint32_t pr = (blk >> 1) ? sw1 : sw0;           // two blocks' fp16 scales
+                    const uint32_t prh = pr & 0xFFF8FFF8u;                // s_hi of both
+                    const __half2 lo2 = __hsub2(bits_h2(pr), bits_h2(prh));   // s_lo, exact
+                    const __half2 shi = (blk & 1) ? __high2half2(bits_h2(prh)) : __low2half2(bits_h2(prh));
+                    const __half2 slo = (blk & 1) ? __high2half2(lo2) : __low2half2(lo2);
+                    uint32_t hcol[16], lcol[16];
+                    const uint4 u = chunk[blk];
+                    dequant_word_exact(u.x, shi, slo, &hcol[0], &lcol[0]);
+                    dequant_word_exact(u.y, shi, slo, &hcol[4], &lcol[4]);
+                    dequant_word_exact(u.z, shi, slo, &hcol[8], &lcol[8]);
+                    dequant_word_exact(u.w, shi, slo, &hcol[12], &lcol[12]);
+                    tmem_st16(a_hi + blk * 16, hcol);
+                    tmem_st16(a_hi + kACols + blk * 16, lcol);
+                }
+            } else {
+                // scales of blocks 4 sub .. 4 sub + 3: two 32-bit words of the row's eight
+                const uint32_t sw0 = sub ? sc.z : sc.x, sw1 = sub ? sc.w : sc.y;
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {
                     const __half2 pr = bits_h2(half ? sw1 : sw0);
@@ -808,12 +819,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     }
                     tmem_st32(tmem + lane_addr + L::kAOff + slot * kACols + half * 32, col);
                 }
-                }
-                tc_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(lead_full + 8u * s);
             }
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(lead_full + 8u * s);
         }
         if (!ok) *s_abort = 1;
     } else {

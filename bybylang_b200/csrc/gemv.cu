@@ -1224,8 +1224,11 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     int x_pitch = 0;
     for (int kc_try : {512, 1024, 2048}) {
         if (m1 && kc_try != kM1KC) continue;   // the M = 1 kernel: one 256-value box per warp
-        const int tp_try = std::min(tiles_max, (ntn == 2 || m1) ? 5 : 8);
-        const int tpl_try = tp_try <= 2 ? 2 : tp_try <= 5 ? 5 : 8;
+        // M = 1: a CTA's rows in one pass when they take 6 or 7 tiles (a second, short pass
+        // costs a whole sweep of K), else passes of 5 tiles
+        const int tp_m1 = tiles_max == 6 || tiles_max == 7 ? 7 : 5;
+        const int tp_try = std::min(tiles_max, m1 ? tp_m1 : ntn == 2 ? 5 : 8);
+        const int tpl_try = tp_try <= 2 ? 2 : tp_try <= 5 ? 5 : (m1 ? 7 : 8);
         const uint32_t rows = 16 * tpl_try;
         const uint32_t sp = static_cast<uint32_t>(kc_try / 32 * 2);
         const uint32_t wb = rows * 128;
@@ -1305,9 +1308,11 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     if (m1) {
         if (scale_tma)
             return tpl == 2 ? launch_m1<2, true>(mode, xf32, maps, p, grid, smem, st)
-                            : launch_m1<5, true>(mode, xf32, maps, p, grid, smem, st);
+                 : tpl == 5 ? launch_m1<5, true>(mode, xf32, maps, p, grid, smem, st)
+                            : launch_m1<7, true>(mode, xf32, maps, p, grid, smem, st);
         return tpl == 2 ? launch_m1<2, false>(mode, xf32, maps, p, grid, smem, st)
-                        : launch_m1<5, false>(mode, xf32, maps, p, grid, smem, st);
+             : tpl == 5 ? launch_m1<5, false>(mode, xf32, maps, p, grid, smem, st)
+                        : launch_m1<7, false>(mode, xf32, maps, p, grid, smem, st);
     }
     if (ntn == 2) {
         return tpl == 2 ? dispatch_x<2, 2>(xf32, maps, p, grid, smem, st) : dispatch_x<5, 2>(xf32, maps, p, grid, smem, st);

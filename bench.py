@@ -4,7 +4,9 @@ Headline workload (every N): BASELINE config C5, the LM-head vocab projection at
 x bf16 [1, 4096] ~N(0,1), Q4B32 weights [128256, 4096] (int4 uniform [-8, 7], one fp16 scale
 |N(0, 0.02)| per 32-block), fp32 logits - column-sharded over the N GPUs by the reference's
 partition rule (distributed.nim:109-135, 64-column blocks) with the fp32 logits all-gathered
-over NVLink inside the same launch (bybycu_tile_gemm_allgather).  C5 is the configuration
+over NVLink inside the same launch, in split phase (bybycu_tile_gemm_allgather_split: no launch
+waits for the other ranks at its end; the next launch, or bybycu_allgather_wait at the end of
+the timed region, does).  C5 is the configuration
 BASELINE names for 1, 2, 4 and 8 GPUs, so the same workload gives one strong-scaling curve.
 Algorithmic bytes per step: 295,501,824 weight + 8,192 x per rank + 513,024 logits per rank.
 
@@ -260,12 +262,15 @@ class Timer:
         return ms
 
 
-def capture(torch, stream, fn, n, start):
-    """A CUDA graph of fn(start), fn(start + 1), ... fn(start + n - 1) on `stream`."""
+def capture(torch, stream, fn, n, start, tail=None):
+    """A CUDA graph of fn(start), fn(start + 1), ... fn(start + n - 1) on `stream`, then tail()
+    (the completion of a split-phase gather) when given."""
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
         for i in range(n):
             fn(start + i)
+        if tail is not None:
+            tail()
     return g
 
 
@@ -283,12 +288,12 @@ def upload_graph(graph, stream):
         return False
 
 
-def graph_steps(torch, timer, stream, fn, steps, warmup):
+def graph_steps(torch, timer, stream, fn, steps, warmup, tail=None):
     """Exactly `warmup` untimed then exactly `steps` timed calls of fn(i), each set replayed
-    from its own CUDA graph (both uploaded before the hold); returns ms per step (max over
-    ranks)."""
-    gw = capture(torch, stream, fn, warmup, 0) if warmup else None
-    gt = capture(torch, stream, fn, steps, warmup)
+    from its own CUDA graph (both uploaded before the hold) and ended by tail() when given;
+    returns ms per step (max over ranks)."""
+    gw = capture(torch, stream, fn, warmup, 0, tail) if warmup else None
+    gt = capture(torch, stream, fn, steps, warmup, tail)
     for g in (gw, gt):
         if g is not None:
             upload_graph(g, stream)
@@ -298,24 +303,27 @@ def graph_steps(torch, timer, stream, fn, steps, warmup):
     return ms / steps
 
 
-def call_steps(timer, fn, steps, warmup):
+def call_steps(timer, fn, steps, warmup, tail=None):
     """The same with plain back-to-back calls (no graph).  The hold kernel in front lasts
     longer than the host takes to queue every call (measured on one extra untimed call), so
     the device runs them back to back."""
     torch = timer.torch
+    tail = tail or (lambda: None)
     fn(0)   # first call: one-time set-up of the route stays out of the measured host time
+    tail()
     timer.stream.synchronize()
     t0 = time.perf_counter()
     fn(0)
     host_s = time.perf_counter() - t0
+    tail()
     timer.stream.synchronize()
     if timer.world > 1:   # every rank holds its stream equally long (ranks wait for each other)
         t = torch.tensor([host_s], dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
         timer.dist.all_reduce(t, op=timer.dist.ReduceOp.MAX)
         host_s = float(t.item())
     hold = int(min(4e6 + 2.0 * (steps + warmup) * host_s * 2.0e9, 4e8))
-    ms = timer.run(lambda: [fn(i) for i in range(warmup)], lambda: [fn(warmup + i) for i in range(steps)],
-                   hold_cycles=hold)
+    ms = timer.run(lambda: ([fn(i) for i in range(warmup)], tail()),
+                   lambda: ([fn(warmup + i) for i in range(steps)], tail()), hold_cycles=hold)
     return ms / steps
 
 
@@ -359,13 +367,19 @@ class ShardedProjection:
             nib, sc = synthetic_q4b32(self.cols, K, seed=seed + 7919 * c + 101 * ctx.rank, device=ctx.dev)
             self.w.append(gb.Q4B32Weights(nib, sc, device=ctx.dev))
         self.x = synthetic_x(M, K, seed=seed + 2, device=ctx.dev, dtype=x_dtype)
+        self.make_outputs(M)
+
+    def make_outputs(self, M):
+        """The gathered output: at N > 1 two buffer sets that split-phase steps alternate
+        between (one signal array, the first set's), else one local buffer."""
+        torch, ctx = self.ctx.torch, self.ctx
         if ctx.world > 1:
             from bybylang_b200.distributed import PeerBuffers
-            self.bufs = PeerBuffers(M, N, ctx.world, ctx.rank)
-            self.out = self.bufs.out
+            self.bufs = [PeerBuffers(M, self.N, ctx.world, ctx.rank), PeerBuffers(M, self.N, ctx.world, ctx.rank)]
+            self.out = self.bufs[0].out
         else:
             self.bufs = None
-            self.out = torch.empty(M, N, dtype=torch.float32, device=ctx.dev)
+            self.out = torch.empty(M, self.N, dtype=torch.float32, device=ctx.dev)
 
     def bytes_per_rank(self):
         return wbytes(self.cols, self.K) + self.M * self.K * self.x.element_size() + self.M * self.cols * 4 * self.ctx.world
@@ -374,25 +388,36 @@ class ShardedProjection:
         return wbytes(self.N, self.K) + self.ctx.world * (self.M * self.K * self.x.element_size() + self.M * self.N * 4)
 
     def launch(self, i, x=None, route=None):
+        """Step i: the rank's slice, gathered in split phase into buffer set i % 2 (N > 1)."""
         _lib, gb, ctx = self.ctx._lib, self.ctx.gb, self.ctx
         w = self.w[i % self.copies]
         x = self.x if x is None else x
         if ctx.world > 1:
-            _lib.check(ctx.lib.bybycu_tile_gemm_allgather(
+            b = self.bufs[i % 2]
+            _lib.check(ctx.lib.bybycu_tile_gemm_allgather_split(
                 2, self.M, self.K, self.N, self.n0, self.n1, C.c_void_p(x.data_ptr()), gb._dtype_code(x),
                 C.c_void_p(w.packed.data_ptr()), w.packed.numel(), w.scale_base, None, 0, 0,
-                C.c_void_p(self.out.data_ptr()), self.bufs.peer_out, self.bufs.peer_sig, ctx.world, ctx.rank, 0,
+                C.c_void_p(b.out.data_ptr()), b.peer_out, self.bufs[0].peer_sig, ctx.world, ctx.rank, 0,
                 C.c_void_p(ctx.stream.cuda_stream)))
         else:
             gb.tile_gemm(2, x, w.packed, self.out, M=self.M, K=self.K, N=self.N, scale_base=w.scale_base,
                          route=_lib.ROUTE_AUTO if route is None else route, stream=ctx.stream)
 
+    def finish(self):
+        """Completes the last split-phase step (N > 1): every rank's slices have landed."""
+        ctx = self.ctx
+        if ctx.world > 1:
+            ctx._lib.check(ctx.lib.bybycu_allgather_wait(self.bufs[0].peer_sig, ctx.world, ctx.rank, 0,
+                                                         C.c_void_p(ctx.stream.cuda_stream)))
+
     def check(self, n_cols=1024):
-        """Step with copy 0, then its gathered output on `n_cols` columns spread over every
-        shard against the exact SIMT route on the same columns of the full matrix."""
+        """Step with copy 0 into buffer set 0, completed, then its gathered output on `n_cols`
+        columns spread over every shard against the exact SIMT route on the same columns of
+        the full matrix."""
         torch, gb, _lib = self.ctx.torch, self.ctx.gb, self.ctx._lib
         with torch.cuda.stream(self.ctx.stream):
             self.launch(0)
+            self.finish()
         self.ctx.stream.synchronize()
         idx = torch.linspace(0, self.N - 1, min(n_cols, self.N), device=self.ctx.dev).round().long().unique()
         nib, sc = self.full0
@@ -409,7 +434,8 @@ class ShardedProjection:
 
     def close(self):
         if self.bufs is not None:
-            self.bufs.close()
+            for b in self.bufs:
+                b.close()
 
 
 class Ctx:
@@ -473,7 +499,7 @@ def main():
 
     # ---- headline: C5 LM head at M=1, column-sharded, gathered in the GEMV's own launch
     head = ShardedProjection(ctx, N_HEAD, K_DEC, 1, SEED)
-    per_ms = graph_steps(torch, timer, stream, head.launch, K, W)
+    per_ms = graph_steps(torch, timer, stream, head.launch, K, W, tail=head.finish)
     launches += K
     check_device(_lib)
     value = head.bytes_whole_job() / (per_ms / 1e3) / 1e9
@@ -489,16 +515,17 @@ def main():
     x_bytes, o_bytes = K_DEC * 2, N_HEAD * 4
     if world > 1:
         def e2e_step(i):
-            w = head.w[i % head.copies]
+            w, b = head.w[i % head.copies], head.bufs[i % 2]
             _lib.check(lib.bybycu_upload(C.c_void_p(xd.data_ptr()), C.c_void_p(xh.data_ptr()), x_bytes, sp))
-            _lib.check(lib.bybycu_tile_gemm_allgather(
+            _lib.check(lib.bybycu_tile_gemm_allgather_split(
                 2, 1, K_DEC, N_HEAD, head.n0, head.n1, C.c_void_p(xd.data_ptr()), _lib.DT_BF16,
                 C.c_void_p(w.packed.data_ptr()), w.packed.numel(), w.scale_base, None, 0, 0,
-                C.c_void_p(head.out.data_ptr()), head.bufs.peer_out, head.bufs.peer_sig, world, rank, 0, sp))
-            _lib.check(lib.bybycu_download(C.c_void_p(oh.data_ptr()), C.c_void_p(head.out.data_ptr()), o_bytes, sp))
+                C.c_void_p(b.out.data_ptr()), b.peer_out, head.bufs[0].peer_sig, world, rank, 0, sp))
+            _lib.check(lib.bybycu_allgather_wait(head.bufs[0].peer_sig, world, rank, 0, sp))
+            _lib.check(lib.bybycu_download(C.c_void_p(oh.data_ptr()), C.c_void_p(b.out.data_ptr()), o_bytes, sp))
             _lib.check(lib.bybycu_synchronize(sp))
-        api = "bybycu_upload + bybycu_tile_gemm_allgather + bybycu_download + bybycu_synchronize (C ABI) on every " \
-              "rank, pinned host x and logits, max over ranks"
+        api = "bybycu_upload + bybycu_tile_gemm_allgather_split + bybycu_allgather_wait + bybycu_download + " \
+              "bybycu_synchronize (C ABI) on every rank, pinned host x and logits, max over ranks"
     else:
         od = torch.empty(1, N_HEAD, dtype=torch.float32, device=dev)
 
@@ -534,14 +561,9 @@ def main():
             h64 = ShardedProjection.__new__(ShardedProjection)
             h64.__dict__.update(head.__dict__)
             h64.M, h64.x = 64, x64
-            if world > 1:
-                from bybylang_b200.distributed import PeerBuffers
-                h64.bufs = PeerBuffers(64, N_HEAD, world, rank)
-                h64.out = h64.bufs.out
-            else:
-                h64.bufs, h64.out = None, torch.empty(64, N_HEAD, dtype=torch.float32, device=dev)
+            h64.make_outputs(64)
             reps = min(K, 50)
-            ms = call_steps(timer, h64.launch, reps, W)
+            ms = call_steps(timer, h64.launch, reps, W, tail=h64.finish)
             check_device(_lib)
             ck = h64.check(n_cols=512)
             ck["pass"] = ck["finite"] and ck["max_abs_err_over_peak"] <= 1e-3
@@ -556,8 +578,7 @@ def main():
                          else "tensor-core GEMM (staging pass + tcgen05)",
                 "roofline": roofline(tf / world, tc_peak, "TFLOP/s", "tensor", peak_kind, per="GPU"),
                 "check": ck}
-            if h64.bufs is not None:
-                h64.bufs.close()
+            h64.close()
             del h64
         except _lib.BybyCudaError as e:
             extras["lm_head_m64"] = {"error": str(e)}
@@ -574,11 +595,15 @@ def main():
                 def layer(i, projs=projs):
                     for p in projs:
                         p.launch(i)
+
+                def layer_done(projs=projs):
+                    for p in projs:
+                        p.finish()
                 reps = min(K, 50)
                 if M <= 16:
-                    ms = graph_steps(torch, timer, stream, layer, reps, W)
+                    ms = graph_steps(torch, timer, stream, layer, reps, W, tail=layer_done)
                 else:
-                    ms = call_steps(timer, layer, reps, W)
+                    ms = call_steps(timer, layer, reps, W, tail=layer_done)
                 check_device(_lib)
                 checks = [p.check(n_cols=256) for p in projs]
                 tol = 1e-4 if M <= 16 else 1e-3

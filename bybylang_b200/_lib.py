@@ -115,6 +115,10 @@ SIGNATURES = {
     "bybycu_tile_gemm_allgather": [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _vp, _i64, _i64,
                                    _vp, _i64, _i64, _vp, C.POINTER(_vp), C.POINTER(C.POINTER(_u32)),
                                    _i32, _i32, _u32, _vp],
+    "bybycu_tile_gemm_allgather_split": [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _vp, _i64, _i64,
+                                         _vp, _i64, _i64, _vp, C.POINTER(_vp), C.POINTER(C.POINTER(_u32)),
+                                         _i32, _i32, _u32, _vp],
+    "bybycu_allgather_wait": [C.POINTER(C.POINTER(_u32)), _i32, _i32, _u32, _vp],
     "bybycu_prepare_q4_tuned": [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, C.POINTER(_i32)],
     "bybycu_prepare_tile_gemm_tuned": [_i32, _i32, _i32, _i32, _i32, _vp, _i64, _i64, C.POINTER(_i32)],
     "bybycu_plan_get": [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, C.POINTER(Plan), C.POINTER(_i32)],

@@ -85,13 +85,6 @@ struct GemvParams {
     PeerGather pg;                 // world > 1: every output value also goes to every peer
 };
 
-// The fused all-gather: one output value to every other rank's buffer (plain NVLink stores).
-__device__ __forceinline__ void store_to_peers(const PeerGather& pg, int64_t oi, float v) {
-#pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r)
-        if (r < pg.world && r != pg.rank) pg.out[r][oi] = v;
-}
-
 // End of a GEMV launch that gathers: the barrier orders every consumer thread's stores before
 // thread 0's release (cumulative), then the last CTA signals the ranks and waits for theirs.
 // One release per CTA: a system fence per thread cost microseconds per step.
@@ -268,6 +261,10 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
                 if (++chunk == p.n_chunks) { chunk = 0; t0 += upass; }
             }
             pdl_wait();
+            // split-phase gather: every rank finished the previous launch (x may be its output,
+            // and this launch's stores overwrite what that launch's readers read); on a
+            // timeout the error is recorded and the launch goes on
+            peer_gather_wait_previous(p.pg);
             if (p.x_whole) {   // the whole row, chunk by chunk, each on its own barrier
                 uint64_t* x_bar = reinterpret_cast<uint64_t*>(smem + p.xbar_off);
                 for (int c = 0; c < p.n_chunks; ++c) {
@@ -1224,9 +1221,10 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     int x_pitch = 0;
     for (int kc_try : {512, 1024, 2048}) {
         if (m1 && kc_try != kM1KC) continue;   // the M = 1 kernel: one 256-value box per warp
-        // M = 1: a CTA's rows in one pass when they take 6 or 7 tiles (a second, short pass
-        // costs a whole sweep of K), else passes of 5 tiles
-        const int tp_m1 = tiles_max == 6 || tiles_max == 7 ? 7 : 5;
+        // M = 1: passes of 5 or 7 tiles, whichever needs fewer passes over a CTA's rows (each
+        // pass is a whole sweep of K and ends in a cross-warp reduction); 5 on a tie, whose
+        // smaller stages let two CTAs share an SM when one pass does
+        const int tp_m1 = ceil_div(tiles_max, 7) < ceil_div(tiles_max, 5) ? 7 : 5;
         const int tp_try = std::min(tiles_max, m1 ? tp_m1 : ntn == 2 ? 5 : 8);
         const int tpl_try = tp_try <= 2 ? 2 : tp_try <= 5 ? 5 : (m1 ? 7 : 8);
         const uint32_t rows = 16 * tpl_try;

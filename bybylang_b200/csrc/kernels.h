@@ -27,6 +27,9 @@ struct GemmArgs {
     // stages: the ring depth of the streamed weights (GEMV routes).
     int variant = -1;
     int stages = 0;
+    // Set by the sharded entry points: the kernel also stores its slice into every rank's
+    // output (the tensor-core route; the GEMV takes it as launch_gemv's argument).
+    const struct PeerGather* pg = nullptr;
 };
 
 // Ranks of a column-sharded GEMM whose output slices are gathered over NVLink peer
@@ -38,7 +41,52 @@ struct PeerGather {
     float* out[kMaxRanks] = {};      // every rank's output buffer as mapped here (out[rank] = local)
     uint32_t* sig[kMaxRanks] = {};   // every rank's signal array as mapped here
     uint32_t epoch = 0;              // 0: the epoch lives on the device (graph-capturable)
+    // 1 (split phase): a launch signals its epoch without waiting for the other ranks; the next
+    // split launch waits for every rank's previous epoch before it reads its input or stores
+    // to a peer, and bybycu_allgather_wait completes the last one
+    int split = 0;
 };
+
+// The fused all-gather: one output value to every other rank's buffer (plain NVLink stores).
+__device__ __forceinline__ void store_to_peers(const PeerGather& pg, int64_t oi, float v) {
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+        if (r < pg.world && r != pg.rank) pg.out[r][oi] = v;
+}
+
+// Bounded wait (one thread) until every rank's counter in this rank's signal array reached
+// `target`.  Acquire loads at system scope: what the ranks stored before their signals is
+// visible after it.  False (device error recorded) when the wait ran out.
+__device__ __forceinline__ bool peer_wait_epoch(const PeerGather& pg, uint32_t target) {
+    const uint32_t* mine = pg.sig[pg.rank];
+    for (int r = 0; r < pg.world; ++r) {
+        const uint64_t t0 = globaltimer_ns();
+        for (;;) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
+            if (static_cast<int32_t>(v - target) >= 0) break;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                record_device_error(kDevErrPeerWait);
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+// The epoch the previous launch of this rank signalled (device-side epochs), or epoch - 1.
+__device__ __forceinline__ uint32_t peer_previous_epoch(const PeerGather& pg) {
+    return pg.epoch ? pg.epoch - 1 : *reinterpret_cast<volatile const uint32_t*>(pg.sig[pg.rank] + kMaxRanks);
+}
+
+// Split phase, by one thread before anything of this launch reads its input or stores to a
+// peer: every rank has finished the previous launch (its stores into this rank's buffers
+// landed, and whatever its stream ran before that launch - the readers of the buffer this
+// launch overwrites - is done).  Called after griddepcontrol.wait.
+__device__ __forceinline__ bool peer_gather_wait_previous(const PeerGather& pg) {
+    if (pg.world <= 1 || !pg.split) return true;
+    return peer_wait_epoch(pg, peer_previous_epoch(pg));
+}
 
 // Called by one thread of every CTA after all of the CTA's output stores (local and to the
 // peers).  The last CTA of the grid raises this rank's counter in every rank's signal array
@@ -59,20 +107,11 @@ __device__ __forceinline__ bool peer_gather_finish(const PeerGather& pg) {
     for (int r = 0; r < pg.world; ++r)
         asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(pg.sig[r] + pg.rank) : "memory");
     const uint32_t target = pg.epoch ? pg.epoch : mine[kMaxRanks] + 1;
-    bool ok = true;
-    for (int r = 0; r < pg.world && ok; ++r) {
-        const uint64_t t0 = globaltimer_ns();
-        for (;;) {
-            uint32_t v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
-            if (static_cast<int32_t>(v - target) >= 0) break;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                record_device_error(kDevErrPeerWait);
-                ok = false;
-                break;
-            }
-        }
+    if (pg.split) {   // the next launch (or bybycu_allgather_wait) waits for the ranks
+        if (!pg.epoch) mine[kMaxRanks] = target;
+        return true;
     }
+    const bool ok = peer_wait_epoch(pg, target);
     if (!pg.epoch) mine[kMaxRanks] = target;
     return ok;
 }

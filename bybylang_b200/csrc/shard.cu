@@ -25,7 +25,7 @@ int run_gemm(const GemmArgs& a, int route);
 
 namespace {
 
-constexpr int kExchangeCtas = 32;
+constexpr int kExchangeCtas = 148;   // one per SM: enough stores in flight to fill NVLink
 
 // Largest-remainder partition of `length` items over `world` equal weights
 // (distributed.nim:109-135): floor of length * (1 / world), then one more to the largest
@@ -58,6 +58,10 @@ std::vector<int> partition_equal(int length, int world) {
 // store to the peers themselves.
 __global__ void __launch_bounds__(256) exchange_kernel(const float* __restrict__ out, int M, int N, int n0, int n1,
                                                        const PeerGather pg) {
+    if (pg.split) {   // every rank done with the previous launch before anything goes to a peer
+        if (threadIdx.x == 0) peer_gather_wait_previous(pg);
+        __syncthreads();
+    }
     const int cols = n1 - n0;
     const int64_t total = static_cast<int64_t>(M) * cols;
     const bool vec = ((n0 | cols | N) & 3) == 0;
@@ -87,6 +91,33 @@ __global__ void __launch_bounds__(256) exchange_kernel(const float* __restrict__
     }
     __syncthreads();   // every thread's stores before thread 0's release (peer_gather_finish)
     if (threadIdx.x == 0) peer_gather_finish(pg);
+}
+
+// One thread waits until every rank reached an epoch: the previous one (`previous`, before a
+// split launch that reads its input through another route), or the last one this rank
+// signalled (bybycu_allgather_wait).
+__global__ void allgather_wait_kernel(const PeerGather pg, int previous) {
+    if (threadIdx.x != 0) return;
+    const uint32_t last = pg.epoch ? pg.epoch
+                                   : *reinterpret_cast<volatile const uint32_t*>(pg.sig[pg.rank] + kMaxRanks);
+    peer_wait_epoch(pg, previous ? peer_previous_epoch(pg) : last);
+}
+
+int make_peer_gather(void* const* peer_out, uint32_t* const* peer_signal, int world, int rank, uint32_t epoch,
+                     int split, PeerGather* pg) {
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_signal)
+        return set_error(BYBYCU_ERR_ARGS, "all-gather: bad arguments");
+    pg->world = world;
+    pg->rank = rank;
+    pg->epoch = epoch;
+    pg->split = split;
+    for (int r = 0; r < world; ++r) {
+        if ((peer_out && !peer_out[r]) || !peer_signal[r])
+            return set_error(BYBYCU_ERR_ARGS, "all-gather: peer %d missing", r);
+        pg->out[r] = peer_out ? static_cast<float*>(peer_out[r]) : nullptr;
+        pg->sig[r] = peer_signal[r];
+    }
+    return BYBYCU_OK;
 }
 
 // Peer allocations mapped into this process, shared by every pointer inside them.
@@ -188,23 +219,15 @@ int bybycu_shard_range(int N, int world, int rank, int align, int* n0, int* n1) 
     return BYBYCU_OK;
 }
 
-int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1, const void* x, int x_dtype,
+static int tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1, const void* x, int x_dtype,
                                const void* packed, int64_t packed_len, int64_t scale_base, const float* lut,
                                int64_t lut_len, int64_t lut_base, void* out, void* const* peer_out,
-                               uint32_t* const* peer_signal, int world, int rank, uint32_t epoch, void* stream) {
-    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_out || !peer_signal || !out || !x ||
-        !packed)
-        return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: bad arguments");
+                               uint32_t* const* peer_signal, int world, int rank, uint32_t epoch, int split,
+                               void* stream) {
+    if (!peer_out || !out || !x || !packed) return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: bad arguments");
     if (n0 < 0 || n1 > N || n0 > n1) return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: bad column range");
     PeerGather pg;
-    pg.world = world;
-    pg.rank = rank;
-    pg.epoch = epoch;
-    for (int r = 0; r < world; ++r) {
-        if (!peer_out[r] || !peer_signal[r]) return set_error(BYBYCU_ERR_ARGS, "tile GEMM all-gather: peer %d missing", r);
-        pg.out[r] = static_cast<float*>(peer_out[r]);
-        pg.sig[r] = peer_signal[r];
-    }
+    if (int rc = make_peer_gather(peer_out, peer_signal, world, rank, epoch, split, &pg)) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const int cols = n1 - n0;
     bool fused = false;
@@ -223,16 +246,52 @@ int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1, con
         if (int rc = choose_route(a, BYBYCU_ROUTE_AUTO, &route)) return rc;
         if (route == BYBYCU_ROUTE_GEMV && fmt == BYBYCU_FMT_Q4B32 && M <= 16) {
             // the Q4B32 GEMV stores every value to the peers itself and ends with the signals
+            // (in split phase its producer first waits for the ranks' previous launch)
             if (int rc = launch_gemv(a, &pg)) return rc;
             fused = true;
-        } else if (int rc = run_gemm(a, route)) {
-            return rc;
+        } else if (route == BYBYCU_ROUTE_TC && fmt == BYBYCU_FMT_Q4B32) {
+            // the tensor-core GEMM's epilogue does the same, tile by tile, so the transfer
+            // overlaps the MMAs of the pair's next tiles
+            a.pg = &pg;
+            if (int rc = run_gemm(a, route)) return rc;
+            fused = true;
+        } else {
+            if (split) {   // x may be the previous launch's gathered output: wait for it first
+                allgather_wait_kernel<<<1, 32, 0, s>>>(pg, 1);
+                BYBYCU_LAUNCH_CHECK("allgather_wait_kernel");
+            }
+            if (int rc = run_gemm(a, route)) return rc;
         }
     }
     if (!fused) {
         exchange_kernel<<<kExchangeCtas, 256, 0, s>>>(static_cast<const float*>(out), M, N, n0, n1, pg);
         BYBYCU_LAUNCH_CHECK("exchange_kernel");
     }
+    return BYBYCU_OK;
+}
+
+int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1, const void* x, int x_dtype,
+                               const void* packed, int64_t packed_len, int64_t scale_base, const float* lut,
+                               int64_t lut_len, int64_t lut_base, void* out, void* const* peer_out,
+                               uint32_t* const* peer_signal, int world, int rank, uint32_t epoch, void* stream) {
+    return tile_gemm_allgather(fmt, M, K, N, n0, n1, x, x_dtype, packed, packed_len, scale_base, lut, lut_len,
+                               lut_base, out, peer_out, peer_signal, world, rank, epoch, 0, stream);
+}
+
+int bybycu_tile_gemm_allgather_split(int fmt, int M, int K, int N, int n0, int n1, const void* x, int x_dtype,
+                                     const void* packed, int64_t packed_len, int64_t scale_base, const float* lut,
+                                     int64_t lut_len, int64_t lut_base, void* out, void* const* peer_out,
+                                     uint32_t* const* peer_signal, int world, int rank, uint32_t epoch,
+                                     void* stream) {
+    return tile_gemm_allgather(fmt, M, K, N, n0, n1, x, x_dtype, packed, packed_len, scale_base, lut, lut_len,
+                               lut_base, out, peer_out, peer_signal, world, rank, epoch, 1, stream);
+}
+
+int bybycu_allgather_wait(uint32_t* const* peer_signal, int world, int rank, uint32_t epoch, void* stream) {
+    PeerGather pg;
+    if (int rc = make_peer_gather(nullptr, peer_signal, world, rank, epoch, 1, &pg)) return rc;
+    allgather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(pg, 0);
+    BYBYCU_LAUNCH_CHECK("allgather_wait_kernel");
     return BYBYCU_OK;
 }
 

@@ -140,6 +140,7 @@ struct Params {
     void* out;
     int64_t out_ld, out_col0;
     int out_bf16;
+    PeerGather pg;    // world > 1: the epilogue also stores every value to the other ranks (fp32)
 };
 
 // Bounded wait by plain try_wait polling.  With a suspend-time hint the waits of this kernel
@@ -429,8 +430,12 @@ __host__ __device__ constexpr int perm_of(int mode, int kk) {
 }
 template <bool XF32, int PERM = kPermQ4B32>
 __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x, uint4* __restrict__ xp,
-                                                      int64_t nblocks) {
+                                                      int64_t nblocks, PeerGather pg) {
     pdl_launch_dependents();   // the GEMM may start its prologue; it waits before reading xp
+    if (pg.split && pg.world > 1) {   // split phase: x may be the previous launch's gathered output
+        if (threadIdx.x == 0) peer_gather_wait_previous(pg);
+        __syncthreads();
+    }
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= nblocks) return;
     float v[32];
@@ -506,11 +511,15 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
                     for (int j = 0; j < kChunk; ++j)
                         if (j < nt) o[j * p.out_ld] = __float2bfloat16_rn(__uint_as_float(v[j]));
                 } else {
-                    float* o = reinterpret_cast<float*>(p.out) + p.out_col0 + feat +
-                               static_cast<int64_t>(tok0 + c0) * p.out_ld;
+                    const int64_t o0 = p.out_col0 + feat + static_cast<int64_t>(tok0 + c0) * p.out_ld;
+                    float* o = reinterpret_cast<float*>(p.out) + o0;
 #pragma unroll
                     for (int j = 0; j < kChunk; ++j)
                         if (j < nt) o[j * p.out_ld] = __uint_as_float(v[j]);
+                    if (p.pg.world > 1)   // the fused all-gather: the same values into every rank
+#pragma unroll
+                        for (int j = 0; j < kChunk; ++j)
+                            if (j < nt) store_to_peers(p.pg, o0 + j * p.out_ld, __uint_as_float(v[j]));
                 }
             }
         }
@@ -594,6 +603,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (lane == 0) {
             prefetch_tensormap(&maps.x);
             pdl_wait();   // the staging pass that writes xp has completed
+            // split-phase gather: every rank finished the previous launch before any value of
+            // this one reaches a peer (the staging pass waited for the same; this costs one
+            // already-satisfied load per rank)
+            peer_gather_wait_previous(p.pg);
             int issued = 0;
             for (int t = 0; t < my_tiles && !*s_abort; ++t) {
                 const int tile = pair + t * pairs;
@@ -838,6 +851,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    // the barriers above ordered every epilogue store of this CTA before thread 0's release
+    if (threadIdx.x == 0 && p.pg.world > 1) peer_gather_finish(p.pg);
 }
 
 }  // namespace tc
@@ -949,10 +964,11 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp) {
     const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
     const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
     constexpr int perm = ASYM ? tc::kPermAsym : tc::kPermQ4B32;
+    const PeerGather pg = a.pg ? *a.pg : PeerGather();
     if (a.x_dtype == BYBYCU_DT_F32)
-        tc::stage_x_kernel<true, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+        tc::stage_x_kernel<true, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg);
     else
-        tc::stage_x_kernel<false, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+        tc::stage_x_kernel<false, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg);
     BYBYCU_LAUNCH_CHECK("stage_x_kernel");
 
     tc::Maps maps;
@@ -985,6 +1001,10 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp) {
     p.out_ld = a.out_ld;
     p.out_col0 = a.out_col0;
     p.out_bf16 = a.out_dtype == BYBYCU_DT_BF16;
+    if (a.pg) {
+        if (p.out_bf16) return set_error(BYBYCU_ERR_ARGS, "tensor-core all-gather: the gathered output is fp32");
+        p.pg = *a.pg;
+    }
     const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];

@@ -263,9 +263,9 @@ int launch_tc_f16(const GemmArgs& a) {
         const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
         const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
         if (a.x_dtype == BYBYCU_DT_F32)
-            tc::stage_x_kernel<true, tc::kPermNone><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+            tc::stage_x_kernel<true, tc::kPermNone><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, PeerGather());
         else
-            tc::stage_x_kernel<false, tc::kPermNone><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks);
+            tc::stage_x_kernel<false, tc::kPermNone><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, PeerGather());
         const cudaError_t le = cudaGetLastError();
         if (le != cudaSuccess) rc = cuda_fail(le, "stage_x_kernel");
     }

@@ -137,6 +137,27 @@ class ShardedQ4B32:
             bufs.peer_sig, self.world, self.rank, bufs.epoch, _stream_ptr(stream)))
         return bufs.out
 
+    def gemm_allgather_split(self, x, bufs: PeerBuffers, signal_bufs: PeerBuffers = None, stream=None):
+        """Split phase: the slice goes into `bufs` (alternate two PeerBuffers between calls)
+        and the launch does not wait for the other ranks; the next split call, or
+        allgather_wait, completes it.  The signal array is `signal_bufs`' (default: bufs'),
+        shared by both buffer sets."""
+        sig = (signal_bufs or bufs)
+        sig.epoch += 1
+        M = x.shape[0]
+        loc = self.local
+        check(load().bybycu_tile_gemm_allgather_split(
+            TileFormatQ4B32, M, self.K, self.N, self.n0, self.n1, _ptr(x), _dtype_code(x),
+            _ptr(loc.packed) if loc else C.c_void_p(0), loc.packed.numel() if loc else 0,
+            loc.scale_base if loc else 0, None, 0, 0, C.c_void_p(bufs.out.data_ptr()), bufs.peer_out,
+            sig.peer_sig, self.world, self.rank, sig.epoch, _stream_ptr(stream)))
+        return bufs.out
+
+    def allgather_wait(self, signal_bufs: PeerBuffers, stream=None):
+        """Completes the last split-phase call (bybycu_allgather_wait)."""
+        check(load().bybycu_allgather_wait(signal_bufs.peer_sig, self.world, self.rank, signal_bufs.epoch,
+                                           _stream_ptr(stream)))
+
     def gemm_allgather_nccl(self, x, slice_buf, gathered, group=None):
         """The baseline: compute the padded slice, NCCL all-gather, reorder to [M, N]."""
         import torch

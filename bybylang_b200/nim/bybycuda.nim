@@ -106,6 +106,12 @@ proc bybycu_tile_gemm_allgather*(fmt, M, K, N, n0, n1: cint; x: pointer; xDtype:
                                 lut: ptr float32; lutLen, lutBase: int64;
                                 outp: pointer; peerOut: ptr pointer; peerSignal: ptr ptr uint32;
                                 world, rank: cint; epoch: uint32; stream: pointer): cint
+proc bybycu_tile_gemm_allgather_split*(fmt, M, K, N, n0, n1: cint; x: pointer; xDtype: cint;
+                                       packed: pointer; packedLen, scaleBase: int64;
+                                       lut: ptr float32; lutLen, lutBase: int64;
+                                       outp: pointer; peerOut: ptr pointer; peerSignal: ptr ptr uint32;
+                                       world, rank: cint; epoch: uint32; stream: pointer): cint
+proc bybycu_allgather_wait*(peerSignal: ptr ptr uint32; world, rank: cint; epoch: uint32; stream: pointer): cint
 proc bybycu_tile_gemm_noalloc*(M, K, N: cint; x: pointer; xDtype: cint; xLen: int64;
                               packed: pointer; packedLen, scaleBase: int64;
                               outp: pointer; outDtype: cint; outLen: int64; stream: pointer): cint

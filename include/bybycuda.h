@@ -407,6 +407,30 @@ BYBYCU_API int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, 
                                void* out, void* const* peer_out, uint32_t* const* peer_signal,
                                int world, int rank, uint32_t epoch, void* stream);
 
+/* The same step in split phase (the gather half of distributed.nim:304-375, overlapped with
+ * the next step): the launch stores its slices and raises its counters, and does NOT wait
+ * for the other ranks.  Instead, before it reads x or stores to a peer, it waits for every
+ * rank's previous call, which makes the previous call's output complete on this rank. So
+ * x may be the previous call's gathered output.  A step's output is complete after the next
+ * split call on this stream has started, or after bybycu_allgather_wait.
+ *   Buffers: consecutive calls alternate between two output buffers (and their peer_out
+ *   arrays), with one signal array per rank shared by both.  A call writes into the buffers
+ *   of two calls ago, whose readers were done when every rank signalled the previous call.
+ *   Mixing this and bybycu_tile_gemm_allgather on one signal array is allowed; the counts
+ *   stay in step. */
+BYBYCU_API int bybycu_tile_gemm_allgather_split(int fmt, int M, int K, int N, int n0, int n1,
+                               const void* x, int x_dtype,
+                               const void* packed, int64_t packed_len, int64_t scale_base,
+                               const float* lut, int64_t lut_len, int64_t lut_base,
+                               void* out, void* const* peer_out, uint32_t* const* peer_signal,
+                               int world, int rank, uint32_t epoch, void* stream);
+
+/* Completes the last split-phase call on this rank (one small kernel on `stream`): waits,
+ * bounded, until every rank's counter reached `epoch` (0: the epoch this rank signalled
+ * last).  After it, stream-ordered readers see the whole gathered output. */
+BYBYCU_API int bybycu_allgather_wait(uint32_t* const* peer_signal, int world, int rank, uint32_t epoch,
+                                     void* stream);
+
 #ifdef __cplusplus
 }
 #endif

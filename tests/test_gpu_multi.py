@@ -2,8 +2,9 @@
 (bybycu_tile_gemm_allgather over CUDA IPC peer pointers) every rank holds, bit for bit, the
 concatenation of the ranks' own shard GEMMs - the transport is exact - and that result matches
 the single-GPU GEMM within the route's tolerance (a shard may pick another tiling of the same
-sums than the full-width call).  The NCCL all-gather variant is checked the same way.
-Skipped with fewer than two GPUs."""
+sums than the full-width call).  The split-phase form (bybycu_tile_gemm_allgather_split over
+two alternating buffer sets, completed by bybycu_allgather_wait) and the NCCL all-gather
+variant are checked the same way.  Skipped with fewer than two GPUs."""
 import os
 import socket
 from datetime import timedelta
@@ -21,7 +22,9 @@ def _free_port():
         return s.getsockname()[1]
 
 
-CASES = [(1, 4096, 11008), (4, 4096, 1000), (16, 2048, 4160), (300, 1024, 512)]
+# GEMV (fused gather) at M = 1, 4, 16; tensor-core GEMM (gather fused into its epilogue) at
+# M = 64 over ragged 256-row tiles and at M = 300 over three token tiles
+CASES = [(1, 4096, 11008), (4, 4096, 1000), (16, 2048, 4160), (64, 4096, 4160), (300, 1024, 512)]
 
 
 def _worker(rank, world, port, q):
@@ -59,10 +62,26 @@ def _worker(rank, world, port, q):
                 exact &= bool(torch.equal(out, expect))
                 nan = max(nan, int(torch.isnan(out).sum()))
                 maxd = max(maxd, float((out - expect).abs().nan_to_num(float("inf")).max()))
+            # split phase: calls alternate between two buffer sets (one signal array), no
+            # launch waits at its end; the next call or allgather_wait completes each one
+            bufs_b = PeerBuffers(M, N, world, rank)
+            for _ in range(2):
+                for b in (bufs, bufs_b):
+                    b.out.fill_(float("nan"))
+                torch.cuda.synchronize()
+                dist.barrier()
+                sh.gemm_allgather_split(x, bufs, bufs)
+                sh.gemm_allgather_split(x, bufs_b, bufs)
+                sh.allgather_wait(bufs)
+                torch.cuda.synchronize()
+                for b in (bufs, bufs_b):
+                    exact &= bool(torch.equal(b.out, expect))
+                    nan = max(nan, int(torch.isnan(b.out).sum()))
             peak = max(1.0, float(full.abs().max()))
             rel = float((expect - full).abs().max()) / peak
             results.append((M, K, N, exact, nan, maxd, rel, _lib.device_error()))
             dist.barrier()
+            bufs_b.close()
             bufs.close()
         dist.barrier()
         dist.destroy_process_group()

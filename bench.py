@@ -442,6 +442,14 @@ class Ctx:
     pass
 
 
+LINES = ("lm_head_m64", "c4_layer", "decode_c2", "c1", "prefill", "q4_asym", "f16_decode", "ingest")
+
+
+def on(args, name):
+    """Whether the secondary line `name` runs (--lines)."""
+    return args.lines == "all" or name in args.lines.split(",")
+
+
 # --------------------------------------------------------------------------------------
 
 def main():
@@ -453,6 +461,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="only the headline, its check and e2e")
+    ap.add_argument("--lines", default="all",
+                    help="comma-separated secondary lines to run (default all): " + ", ".join(LINES))
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -556,78 +566,80 @@ def main():
     extras = {}
     if not args.no_extras:
         # ---- C5 at M=64: the tensor-core route, then the device all-gather of the logits
-        try:
-            x64 = synthetic_x(64, K_DEC, seed=SEED + 64, device=dev)
-            h64 = ShardedProjection.__new__(ShardedProjection)
-            h64.__dict__.update(head.__dict__)
-            h64.M, h64.x = 64, x64
-            h64.make_outputs(64)
-            reps = min(K, 50)
-            ms = call_steps(timer, h64.launch, reps, W, tail=h64.finish)
-            check_device(_lib)
-            ck = h64.check(n_cols=512)
-            ck["pass"] = ck["finite"] and ck["max_abs_err_over_peak"] <= 1e-3
-            fl = 2.0 * 64 * N_HEAD * K_DEC
-            tf = fl / (ms / 1e3) / 1e12
-            extras["lm_head_m64"] = {
-                "value": round(tf, 2), "unit": "TFLOP/s", "us_per_step": round(ms * 1e3, 2), "steps": reps,
-                "gbs_whole_job": round(h64.bytes_whole_job() / (ms / 1e3) / 1e9, 2),
-                "workload": "C5 at M=64: x bf16 [64, 4096], Q4B32 [128256, 4096] column-sharded, fp32 logits "
-                            "gathered on every rank",
-                "route": "tensor-core GEMM (staging pass + tcgen05) + device all-gather" if world > 1
-                         else "tensor-core GEMM (staging pass + tcgen05)",
-                "roofline": roofline(tf / world, tc_peak, "TFLOP/s", "tensor", peak_kind, per="GPU"),
-                "check": ck}
-            h64.close()
-            del h64
-        except _lib.BybyCudaError as e:
-            extras["lm_head_m64"] = {"error": str(e)}
+        if on(args, "lm_head_m64"):
+            try:
+                x64 = synthetic_x(64, K_DEC, seed=SEED + 64, device=dev)
+                h64 = ShardedProjection.__new__(ShardedProjection)
+                h64.__dict__.update(head.__dict__)
+                h64.M, h64.x = 64, x64
+                h64.make_outputs(64)
+                reps = min(K, 50)
+                ms = call_steps(timer, h64.launch, reps, W, tail=h64.finish)
+                check_device(_lib)
+                ck = h64.check(n_cols=512)
+                ck["pass"] = ck["finite"] and ck["max_abs_err_over_peak"] <= 1e-3
+                fl = 2.0 * 64 * N_HEAD * K_DEC
+                tf = fl / (ms / 1e3) / 1e12
+                extras["lm_head_m64"] = {
+                    "value": round(tf, 2), "unit": "TFLOP/s", "us_per_step": round(ms * 1e3, 2), "steps": reps,
+                    "gbs_whole_job": round(h64.bytes_whole_job() / (ms / 1e3) / 1e9, 2),
+                    "workload": "C5 at M=64: x bf16 [64, 4096], Q4B32 [128256, 4096] column-sharded, fp32 logits "
+                                "gathered on every rank",
+                    "route": "tensor-core GEMM (staging pass + tcgen05) + device all-gather" if world > 1
+                             else "tensor-core GEMM (staging pass + tcgen05)",
+                    "roofline": roofline(tf / world, tc_peak, "TFLOP/s", "tensor", peak_kind, per="GPU"),
+                    "check": ck}
+                h64.close()
+                del h64
+            except _lib.BybyCudaError as e:
+                extras["lm_head_m64"] = {"error": str(e)}
 
         # ---- C4: the seven projections of one Llama-7B layer, each sharded and gathered
-        try:
-            shapes = [("q", 4096, 4096), ("k", 4096, 4096), ("v", 4096, 4096), ("o", 4096, 4096),
-                      ("gate", 11008, 4096), ("up", 11008, 4096), ("down", 4096, 11008)]
-            c4 = {}
-            for M in (1, 16, 128):
-                projs = [ShardedProjection(ctx, n, k, M, SEED + 300 + 17 * j, min_copies=2)
-                         for j, (_, n, k) in enumerate(shapes)]
+        if on(args, "c4_layer"):
+            try:
+                shapes = [("q", 4096, 4096), ("k", 4096, 4096), ("v", 4096, 4096), ("o", 4096, 4096),
+                          ("gate", 11008, 4096), ("up", 11008, 4096), ("down", 4096, 11008)]
+                c4 = {}
+                for M in (1, 16, 128):
+                    projs = [ShardedProjection(ctx, n, k, M, SEED + 300 + 17 * j, min_copies=2)
+                             for j, (_, n, k) in enumerate(shapes)]
 
-                def layer(i, projs=projs):
-                    for p in projs:
-                        p.launch(i)
+                    def layer(i, projs=projs):
+                        for p in projs:
+                            p.launch(i)
 
-                def layer_done(projs=projs):
+                    def layer_done(projs=projs):
+                        for p in projs:
+                            p.finish()
+                    reps = min(K, 50)
+                    if M <= 16:
+                        ms = graph_steps(torch, timer, stream, layer, reps, W, tail=layer_done)
+                    else:
+                        ms = call_steps(timer, layer, reps, W, tail=layer_done)
+                    check_device(_lib)
+                    checks = [p.check(n_cols=256) for p in projs]
+                    tol = 1e-4 if M <= 16 else 1e-3
+                    ok = all(c["finite"] and c["max_abs_err_over_peak"] <= tol for c in checks)
+                    byts = sum(p.bytes_whole_job() for p in projs)
+                    fl = 2.0 * M * sum(n * k for _, n, k in shapes)
+                    gbs, tf = byts / (ms / 1e3) / 1e9, fl / (ms / 1e3) / 1e12
+                    t_roof = max(byts / world / (hbm_peak * 1e9), fl / world / (tc_peak * 1e12))
+                    c4[f"M{M}"] = {"us_per_layer": round(ms * 1e3, 2), "gbs_whole_job": round(gbs, 2),
+                                   "tflops_whole_job": round(tf, 3), "steps": reps,
+                                   "roofline_frac": round(t_roof / (ms / 1e3), 4),
+                                   "bound": "hbm" if byts / (hbm_peak * 1e9) >= fl / (tc_peak * 1e12) else "tensor",
+                                   "check_pass": ok,
+                                   "max_abs_err_over_peak": max(c["max_abs_err_over_peak"] for c in checks)}
                     for p in projs:
-                        p.finish()
-                reps = min(K, 50)
-                if M <= 16:
-                    ms = graph_steps(torch, timer, stream, layer, reps, W, tail=layer_done)
-                else:
-                    ms = call_steps(timer, layer, reps, W, tail=layer_done)
-                check_device(_lib)
-                checks = [p.check(n_cols=256) for p in projs]
-                tol = 1e-4 if M <= 16 else 1e-3
-                ok = all(c["finite"] and c["max_abs_err_over_peak"] <= tol for c in checks)
-                byts = sum(p.bytes_whole_job() for p in projs)
-                fl = 2.0 * M * sum(n * k for _, n, k in shapes)
-                gbs, tf = byts / (ms / 1e3) / 1e9, fl / (ms / 1e3) / 1e12
-                t_roof = max(byts / world / (hbm_peak * 1e9), fl / world / (tc_peak * 1e12))
-                c4[f"M{M}"] = {"us_per_layer": round(ms * 1e3, 2), "gbs_whole_job": round(gbs, 2),
-                               "tflops_whole_job": round(tf, 3), "steps": reps,
-                               "roofline_frac": round(t_roof / (ms / 1e3), 4),
-                               "bound": "hbm" if byts / (hbm_peak * 1e9) >= fl / (tc_peak * 1e12) else "tensor",
-                               "check_pass": ok,
-                               "max_abs_err_over_peak": max(c["max_abs_err_over_peak"] for c in checks)}
-                for p in projs:
-                    p.close()
-                del projs
-                torch.cuda.empty_cache()
-            extras["c4_layer"] = dict(c4, workload="C4: Llama-7B layer projections q, k, v, o [4096x4096], gate, up "
-                                                   "[11008x4096], down [4096x11008] in sequence, x bf16, each "
-                                                   "column-sharded and gathered; roofline = max(bytes/HBM, flop/peak) "
-                                                   "per GPU over the measured time")
-        except _lib.BybyCudaError as e:
-            extras["c4_layer"] = {"error": str(e)}
+                        p.close()
+                    del projs
+                    torch.cuda.empty_cache()
+                extras["c4_layer"] = dict(c4, workload="C4: Llama-7B layer projections q, k, v, o [4096x4096], gate, up "
+                                                       "[11008x4096], down [4096x11008] in sequence, x bf16, each "
+                                                       "column-sharded and gathered; roofline = max(bytes/HBM, flop/peak) "
+                                                       "per GPU over the measured time")
+            except _lib.BybyCudaError as e:
+                extras["c4_layer"] = {"error": str(e)}
 
     if world == 1 and not args.no_extras:
         single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind)
@@ -674,226 +686,232 @@ def single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind):
     K, W = args.steps, args.warmup
 
     # ---- C2: the decode GEMV, resident inputs, exactly K graph-replayed steps
-    c2 = ShardedProjection(ctx, N_C2, K_DEC, 1, SEED + 11)
-    c2_bytes = c2.bytes_per_rank()
-    ms = graph_steps(torch, timer, stream, lambda i: c2.launch(i, route=_lib.ROUTE_GEMV), K, W)
-    check_device(_lib)
-    ck = c2.check()
-    ck["pass"] = ck["finite"] and ck["max_abs_err_over_peak"] <= 1e-4 and ck["max_elem_rel_err"] <= 1e-3
-    gbs = c2_bytes / (ms / 1e3) / 1e9
-    x32 = c2.x.float().contiguous()
-    ms32 = graph_steps(torch, timer, stream, lambda i: c2.launch(i, x=x32, route=_lib.ROUTE_GEMV), K, W)
-    b32 = c2_bytes + K_DEC * 2
-    extras["decode_c2"] = {
-        "value": round(gbs, 2), "unit": "GB/s", "us_per_launch": round(ms * 1e3, 3), "steps": K, "warmup": W,
-        "workload": "C2 decode GEMV: M=1 K=4096 N=11008 Q4B32, x bf16, out fp32 (GEMV route)",
-        "algorithmic_bytes": c2_bytes,
-        "roofline": roofline(gbs, hbm_peak, "GB/s", "hbm", peak_kind, profiled_traffic("gemv_m1_decode_c2.md"),
-                             "ncu --set full, one launch: profiles/gemv_m1_decode_c2.md"),
-        "x_f32": {"value": round(b32 / (ms32 / 1e3) / 1e9, 2), "us_per_launch": round(ms32 * 1e3, 3),
-                  "frac": round(b32 / (ms32 / 1e3) / 1e9 / hbm_peak, 4)},
-        "l2": f"inputs larger than L2: {c2.copies} rotating weight copies", "check": ck}
-    c2.close()
-    del c2
+    if on(args, "decode_c2"):
+        c2 = ShardedProjection(ctx, N_C2, K_DEC, 1, SEED + 11)
+        c2_bytes = c2.bytes_per_rank()
+        ms = graph_steps(torch, timer, stream, lambda i: c2.launch(i, route=_lib.ROUTE_GEMV), K, W)
+        check_device(_lib)
+        ck = c2.check()
+        ck["pass"] = ck["finite"] and ck["max_abs_err_over_peak"] <= 1e-4 and ck["max_elem_rel_err"] <= 1e-3
+        gbs = c2_bytes / (ms / 1e3) / 1e9
+        x32 = c2.x.float().contiguous()
+        ms32 = graph_steps(torch, timer, stream, lambda i: c2.launch(i, x=x32, route=_lib.ROUTE_GEMV), K, W)
+        b32 = c2_bytes + K_DEC * 2
+        extras["decode_c2"] = {
+            "value": round(gbs, 2), "unit": "GB/s", "us_per_launch": round(ms * 1e3, 3), "steps": K, "warmup": W,
+            "workload": "C2 decode GEMV: M=1 K=4096 N=11008 Q4B32, x bf16, out fp32 (GEMV route)",
+            "algorithmic_bytes": c2_bytes,
+            "roofline": roofline(gbs, hbm_peak, "GB/s", "hbm", peak_kind, profiled_traffic("gemv_m1_decode_c2.md"),
+                                 "ncu --set full, one launch: profiles/gemv_m1_decode_c2.md"),
+            "x_f32": {"value": round(b32 / (ms32 / 1e3) / 1e9, 2), "us_per_launch": round(ms32 * 1e3, 3),
+                      "frac": round(b32 / (ms32 / 1e3) / 1e9 / hbm_peak, 4)},
+            "l2": f"inputs larger than L2: {c2.copies} rotating weight copies", "check": ck}
+        c2.close()
+        del c2
 
     # ---- C1: M=32, K=N=4096, x fp32 through the automatic route
-    try:
-        c1 = ShardedProjection(ctx, 4096, 4096, 32, SEED + 21, x_dtype=torch.float32)
-        ms = graph_steps(torch, timer, stream, c1.launch, K, W)
-        check_device(_lib)
-        ck = c1.check(n_cols=512)
-        fl = 2.0 * 32 * 4096 * 4096
-        byts = c1.bytes_per_rank()
-        extras["c1"] = {"us_per_call": round(ms * 1e3, 3), "gbs": round(byts / (ms / 1e3) / 1e9, 2),
-                        "tflops": round(fl / (ms / 1e3) / 1e12, 3),
-                        "route": _lib.ROUTE_NAMES[gb.route_for(2, 32, 4096, 4096, _lib.DT_F32)],
-                        "roofline": roofline(byts / (ms / 1e3) / 1e9, hbm_peak, "GB/s", "hbm", peak_kind),
-                        "workload": "C1: M=32 K=N=4096 Q4B32, x fp32, out fp32", "check": ck}
-        c1.close()
-        del c1
-    except _lib.BybyCudaError as e:
-        extras["c1"] = {"error": str(e)}
+    if on(args, "c1"):
+        try:
+            c1 = ShardedProjection(ctx, 4096, 4096, 32, SEED + 21, x_dtype=torch.float32)
+            ms = graph_steps(torch, timer, stream, c1.launch, K, W)
+            check_device(_lib)
+            ck = c1.check(n_cols=512)
+            fl = 2.0 * 32 * 4096 * 4096
+            byts = c1.bytes_per_rank()
+            extras["c1"] = {"us_per_call": round(ms * 1e3, 3), "gbs": round(byts / (ms / 1e3) / 1e9, 2),
+                            "tflops": round(fl / (ms / 1e3) / 1e12, 3),
+                            "route": _lib.ROUTE_NAMES[gb.route_for(2, 32, 4096, 4096, _lib.DT_F32)],
+                            "roofline": roofline(byts / (ms / 1e3) / 1e9, hbm_peak, "GB/s", "hbm", peak_kind),
+                            "workload": "C1: M=32 K=N=4096 Q4B32, x fp32, out fp32", "check": ck}
+            c1.close()
+            del c1
+        except _lib.BybyCudaError as e:
+            extras["c1"] = {"error": str(e)}
 
     # ---- C3 prefill on the tensor-core route
-    if not args.no_prefill:
-        Mp, Kp, Np = 2048, 4096, 4096
-        try:
-            per_set = wbytes(Np, Kp) + Mp * Kp * 2 + Mp * Np * 2
-            n_sets = max(2, -(-4 * L2_BYTES // per_set))
-            sets = []
-            for c in range(n_sets):
-                nib, sc = synthetic_q4b32(Np, Kp, seed=SEED + 7 + c, device=dev)
-                sets.append((gb.Q4B32Weights(nib, sc, device=dev), synthetic_x(Mp, Kp, seed=SEED + 100 + c, device=dev),
-                             torch.empty(Mp, Np, dtype=torch.bfloat16, device=dev)))
+    if on(args, "prefill"):
+        if not args.no_prefill:
+            Mp, Kp, Np = 2048, 4096, 4096
+            try:
+                per_set = wbytes(Np, Kp) + Mp * Kp * 2 + Mp * Np * 2
+                n_sets = max(2, -(-4 * L2_BYTES // per_set))
+                sets = []
+                for c in range(n_sets):
+                    nib, sc = synthetic_q4b32(Np, Kp, seed=SEED + 7 + c, device=dev)
+                    sets.append((gb.Q4B32Weights(nib, sc, device=dev), synthetic_x(Mp, Kp, seed=SEED + 100 + c, device=dev),
+                                 torch.empty(Mp, Np, dtype=torch.bfloat16, device=dev)))
 
-            reps = max(K, 20)
-            for key, route, what, prof in (
-                    ("prefill", _lib.ROUTE_TC, "route TC (AUTO): every weight exact as two fp16 terms, twice the MMAs",
-                     "tc_gemm_prefill_c3.md"),
-                    ("prefill_fp16w", _lib.ROUTE_TC_FP16W,
-                     "route TC_FP16W: each weight rounded once to fp16 (the reference's cooperative lowering)",
-                     "tc_gemm_prefill_c3_fp16w.md")):
-                def pf(i, route=route):
-                    wp, xp, op = sets[i % n_sets]
-                    wp.matmul(xp, op, route=route, stream=stream)
-                ms = call_steps(timer, pf, reps, W)
-                check_device(_lib)
-                tf = 2.0 * Mp * Np * Kp / (ms / 1e3) / 1e12
-                extras[key] = {
-                    "value": round(tf, 2), "unit": "TFLOP/s", "workload": "C3 M=2048 K=N=4096 Q4B32, x bf16, bf16 out",
-                    "route": what, "ms_per_call": round(ms, 5), "calls": reps,
-                    "roofline": roofline(tf, tc_peak, "TFLOP/s", "tensor", peak_kind, profiled_traffic(prof),
-                                         f"ncu --set full, one gemm_kernel launch: profiles/{prof}"),
-                    "includes": "every launch of the call (staging pass + tcgen05 GEMM)",
-                    "l2": f"inputs larger than L2: {n_sets} rotating (W, x, out) sets ({n_sets * per_set >> 20} MiB)"}
-            del sets
-        except _lib.BybyCudaError as e:
-            extras["prefill"] = {"error": str(e)}
+                reps = max(K, 20)
+                for key, route, what, prof in (
+                        ("prefill", _lib.ROUTE_TC, "route TC (AUTO): every weight exact as two fp16 terms, twice the MMAs",
+                         "tc_gemm_prefill_c3.md"),
+                        ("prefill_fp16w", _lib.ROUTE_TC_FP16W,
+                         "route TC_FP16W: each weight rounded once to fp16 (the reference's cooperative lowering)",
+                         "tc_gemm_prefill_c3_fp16w.md")):
+                    def pf(i, route=route):
+                        wp, xp, op = sets[i % n_sets]
+                        wp.matmul(xp, op, route=route, stream=stream)
+                    ms = call_steps(timer, pf, reps, W)
+                    check_device(_lib)
+                    tf = 2.0 * Mp * Np * Kp / (ms / 1e3) / 1e12
+                    extras[key] = {
+                        "value": round(tf, 2), "unit": "TFLOP/s", "workload": "C3 M=2048 K=N=4096 Q4B32, x bf16, bf16 out",
+                        "route": what, "ms_per_call": round(ms, 5), "calls": reps,
+                        "roofline": roofline(tf, tc_peak, "TFLOP/s", "tensor", peak_kind, profiled_traffic(prof),
+                                             f"ncu --set full, one gemm_kernel launch: profiles/{prof}"),
+                        "includes": "every launch of the call (staging pass + tcgen05 GEMM)",
+                        "l2": f"inputs larger than L2: {n_sets} rotating (W, x, out) sets ({n_sets * per_set >> 20} MiB)"}
+                del sets
+            except _lib.BybyCudaError as e:
+                extras["prefill"] = {"error": str(e)}
 
     # ---- asymmetric Q4 (matmul_q4's data): decode, the fused gate/up form, and prefill
-    try:
-        G = K_DEC // 32
-        wb = N_C2 * K_DEC // 2 + N_C2 * G * 8
-        ab = wb + K_DEC * 4 + N_C2 * 4
-        n_sets = max(2, -(-4 * L2_BYTES // wb))
-        gen = torch.Generator(device=dev).manual_seed(SEED + 31)
-        qsets = []
-        for c in range(n_sets):
-            wq = torch.randint(0, 256, (N_C2, K_DEC // 2), dtype=torch.uint8, device=dev, generator=gen)
-            sc = torch.rand(N_C2, G, device=dev, generator=gen) * 0.02 + 1e-4
-            zp = torch.rand(N_C2, G, device=dev, generator=gen) * 15
-            qsets.append((gb.Q4AsymWeights(wq, sc, zp, K_DEC), torch.empty(1, N_C2, device=dev)))
-        xa = torch.randn(1, K_DEC, device=dev, generator=gen)
-
-        def qa(i):
-            wqs, o = qsets[i % n_sets]
-            wqs.matmul(xa, o, route=_lib.ROUTE_GEMV, stream=stream)
-        ms = graph_steps(torch, timer, stream, qa, K, W)
-        gbs = ab / (ms / 1e3) / 1e9
-        q4 = {"value": round(gbs, 2), "unit": "GB/s", "us_per_launch": round(ms * 1e3, 3),
-              "workload": "asymmetric Q4 decode M=1 K=4096 N=11008 (nibbles, fp32 scales + zero points per "
-                          "32-block, x fp32, out fp32)", "algorithmic_bytes": ab,
-              "roofline": roofline(gbs, hbm_peak, "GB/s", "hbm", peak_kind)}
-        gamma = torch.rand(1, K_DEC, device=dev, generator=gen) + 0.5
-        resid = torch.randn(1, N_C2, device=dev, generator=gen)
-        pairs = [(qsets[2 * i][0], qsets[2 * i + 1][0], torch.empty(1, N_C2, device=dev),
-                  torch.empty(1, N_C2, device=dev)) for i in range(n_sets // 2)]
-
-        def fused(i):
-            wg, wu, o0, o1 = pairs[i % len(pairs)]
-            gb.matmul_q4_fused(1, xa, [wg, wu], [o0, o1], res=resid, gamma=gamma, eps=1e-5, stream=stream)
-        ms = graph_steps(torch, timer, stream, fused, K, W)
-        fb = 2 * wb + 2 * K_DEC * 4 + 2 * N_C2 * 4
-        q4["fused_gate_up"] = {"value": round(fb / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                               "us_per_launch": round(ms * 1e3, 3),
-                               "workload": "fused decode GEMV mode 1: RMSNorm(x), silu(x.Wg) * (x.Wu) + residual, "
-                                           "Wg, Wu 11008 x 4096 asymmetric Q4, one launch",
-                               "roofline": roofline(fb / (ms / 1e3) / 1e9, hbm_peak, "GB/s", "hbm", peak_kind)}
-        check_device(_lib)
-        extras["q4_asym_decode"] = q4
-        del qsets, pairs
-    except _lib.BybyCudaError as e:
-        extras["q4_asym_decode"] = {"error": str(e)}
-
-    if not args.no_prefill:
+    if on(args, "q4_asym"):
         try:
-            Mp, Kp, Np = 2048, 4096, 4096
-            Gp = Kp // 32
-            per_set = Np * Kp // 2 + 2 * Np * Gp * 4 + Mp * Kp * 4 + Mp * Np * 4
-            n_sets = max(2, -(-4 * L2_BYTES // per_set))
-            gen = torch.Generator(device=dev).manual_seed(SEED + 51)
-            asets = []
+            G = K_DEC // 32
+            wb = N_C2 * K_DEC // 2 + N_C2 * G * 8
+            ab = wb + K_DEC * 4 + N_C2 * 4
+            n_sets = max(2, -(-4 * L2_BYTES // wb))
+            gen = torch.Generator(device=dev).manual_seed(SEED + 31)
+            qsets = []
             for c in range(n_sets):
-                wq = torch.randint(0, 256, (Np, Kp // 2), dtype=torch.uint8, device=dev, generator=gen)
-                sc = torch.rand(Np, Gp, device=dev, generator=gen) * 0.02 + 1e-4
-                zp = torch.rand(Np, Gp, device=dev, generator=gen) * 15
-                asets.append((wq, sc, zp, torch.randn(Mp, Kp, device=dev, generator=gen),
-                              torch.empty(Mp, Np, device=dev)))
+                wq = torch.randint(0, 256, (N_C2, K_DEC // 2), dtype=torch.uint8, device=dev, generator=gen)
+                sc = torch.rand(N_C2, G, device=dev, generator=gen) * 0.02 + 1e-4
+                zp = torch.rand(N_C2, G, device=dev, generator=gen) * 15
+                qsets.append((gb.Q4AsymWeights(wq, sc, zp, K_DEC), torch.empty(1, N_C2, device=dev)))
+            xa = torch.randn(1, K_DEC, device=dev, generator=gen)
 
-            def asym_call(i):
-                wq, sc, zp, xa_, oa = asets[i % n_sets]
-                _lib.check(lib.bybycu_matmul_q4(C.c_void_p(xa_.data_ptr()), C.c_void_p(wq.data_ptr()),
-                                                C.c_void_p(sc.data_ptr()), C.c_void_p(zp.data_ptr()),
-                                                C.c_void_p(oa.data_ptr()), Mp, Kp, Np, 32, Gp, _lib.ROUTE_TC,
-                                                C.c_void_p(stream.cuda_stream)))
-            reps = max(K, 20)
-            ms = call_steps(timer, asym_call, reps, W)
+            def qa(i):
+                wqs, o = qsets[i % n_sets]
+                wqs.matmul(xa, o, route=_lib.ROUTE_GEMV, stream=stream)
+            ms = graph_steps(torch, timer, stream, qa, K, W)
+            gbs = ab / (ms / 1e3) / 1e9
+            q4 = {"value": round(gbs, 2), "unit": "GB/s", "us_per_launch": round(ms * 1e3, 3),
+                  "workload": "asymmetric Q4 decode M=1 K=4096 N=11008 (nibbles, fp32 scales + zero points per "
+                              "32-block, x fp32, out fp32)", "algorithmic_bytes": ab,
+                  "roofline": roofline(gbs, hbm_peak, "GB/s", "hbm", peak_kind)}
+            gamma = torch.rand(1, K_DEC, device=dev, generator=gen) + 0.5
+            resid = torch.randn(1, N_C2, device=dev, generator=gen)
+            pairs = [(qsets[2 * i][0], qsets[2 * i + 1][0], torch.empty(1, N_C2, device=dev),
+                      torch.empty(1, N_C2, device=dev)) for i in range(n_sets // 2)]
+
+            def fused(i):
+                wg, wu, o0, o1 = pairs[i % len(pairs)]
+                gb.matmul_q4_fused(1, xa, [wg, wu], [o0, o1], res=resid, gamma=gamma, eps=1e-5, stream=stream)
+            ms = graph_steps(torch, timer, stream, fused, K, W)
+            fb = 2 * wb + 2 * K_DEC * 4 + 2 * N_C2 * 4
+            q4["fused_gate_up"] = {"value": round(fb / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                                   "us_per_launch": round(ms * 1e3, 3),
+                                   "workload": "fused decode GEMV mode 1: RMSNorm(x), silu(x.Wg) * (x.Wu) + residual, "
+                                               "Wg, Wu 11008 x 4096 asymmetric Q4, one launch",
+                                   "roofline": roofline(fb / (ms / 1e3) / 1e9, hbm_peak, "GB/s", "hbm", peak_kind)}
             check_device(_lib)
-            tf = 2.0 * Mp * Np * Kp / (ms / 1e3) / 1e12
-            extras["q4_asym_prefill"] = {
-                "value": round(tf, 2), "unit": "TFLOP/s", "ms_per_call": round(ms, 5), "calls": reps,
-                "workload": "asymmetric Q4 prefill M=2048 K=N=4096 (group 32), x fp32, out fp32",
-                "roofline": roofline(tf, tc_peak, "TFLOP/s", "tensor", peak_kind),
-                "includes": "every launch of the call (staging pass + tcgen05 GEMM)"}
-            del asets
+            extras["q4_asym_decode"] = q4
+            del qsets, pairs
         except _lib.BybyCudaError as e:
-            extras["q4_asym_prefill"] = {"error": str(e)}
+            extras["q4_asym_decode"] = {"error": str(e)}
+
+        if not args.no_prefill:
+            try:
+                Mp, Kp, Np = 2048, 4096, 4096
+                Gp = Kp // 32
+                per_set = Np * Kp // 2 + 2 * Np * Gp * 4 + Mp * Kp * 4 + Mp * Np * 4
+                n_sets = max(2, -(-4 * L2_BYTES // per_set))
+                gen = torch.Generator(device=dev).manual_seed(SEED + 51)
+                asets = []
+                for c in range(n_sets):
+                    wq = torch.randint(0, 256, (Np, Kp // 2), dtype=torch.uint8, device=dev, generator=gen)
+                    sc = torch.rand(Np, Gp, device=dev, generator=gen) * 0.02 + 1e-4
+                    zp = torch.rand(Np, Gp, device=dev, generator=gen) * 15
+                    asets.append((wq, sc, zp, torch.randn(Mp, Kp, device=dev, generator=gen),
+                                  torch.empty(Mp, Np, device=dev)))
+
+                def asym_call(i):
+                    wq, sc, zp, xa_, oa = asets[i % n_sets]
+                    _lib.check(lib.bybycu_matmul_q4(C.c_void_p(xa_.data_ptr()), C.c_void_p(wq.data_ptr()),
+                                                    C.c_void_p(sc.data_ptr()), C.c_void_p(zp.data_ptr()),
+                                                    C.c_void_p(oa.data_ptr()), Mp, Kp, Np, 32, Gp, _lib.ROUTE_TC,
+                                                    C.c_void_p(stream.cuda_stream)))
+                reps = max(K, 20)
+                ms = call_steps(timer, asym_call, reps, W)
+                check_device(_lib)
+                tf = 2.0 * Mp * Np * Kp / (ms / 1e3) / 1e12
+                extras["q4_asym_prefill"] = {
+                    "value": round(tf, 2), "unit": "TFLOP/s", "ms_per_call": round(ms, 5), "calls": reps,
+                    "workload": "asymmetric Q4 prefill M=2048 K=N=4096 (group 32), x fp32, out fp32",
+                    "roofline": roofline(tf, tc_peak, "TFLOP/s", "tensor", peak_kind),
+                    "includes": "every launch of the call (staging pass + tcgen05 GEMM)"}
+                del asets
+            except _lib.BybyCudaError as e:
+                extras["q4_asym_prefill"] = {"error": str(e)}
 
     # ---- format 1 (fp16 weights, 2 B per weight) decode at the C2 shape
-    try:
-        fbytes = N_C2 * K_DEC * 2
-        n_sets = max(2, -(-4 * L2_BYTES // fbytes))
-        gen = torch.Generator(device=dev).manual_seed(SEED + 41)
-        hsets = [((torch.randn(N_C2, K_DEC, device=dev, generator=gen) * 0.05).half().view(torch.uint8),
-                  torch.empty(1, N_C2, device=dev)) for _ in range(n_sets)]
-        xh = synthetic_x(1, K_DEC, seed=SEED + 2, device=dev)
+    if on(args, "f16_decode"):
+        try:
+            fbytes = N_C2 * K_DEC * 2
+            n_sets = max(2, -(-4 * L2_BYTES // fbytes))
+            gen = torch.Generator(device=dev).manual_seed(SEED + 41)
+            hsets = [((torch.randn(N_C2, K_DEC, device=dev, generator=gen) * 0.05).half().view(torch.uint8),
+                      torch.empty(1, N_C2, device=dev)) for _ in range(n_sets)]
+            xh = synthetic_x(1, K_DEC, seed=SEED + 2, device=dev)
 
-        def f16(i):
-            wh, o = hsets[i % n_sets]
-            gb.tile_gemm(1, xh, wh, o, M=1, K=K_DEC, N=N_C2, route=_lib.ROUTE_GEMV, stream=stream)
-        ms = graph_steps(torch, timer, stream, f16, K, W)
-        check_device(_lib)
-        hb = fbytes + K_DEC * 2 + N_C2 * 4
-        extras["f16_decode"] = {"value": round(hb / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                                "us_per_launch": round(ms * 1e3, 3),
-                                "workload": "format 1 (fp16 weights) decode M=1 K=4096 N=11008, x bf16, out fp32",
-                                "roofline": roofline(hb / (ms / 1e3) / 1e9, hbm_peak, "GB/s", "hbm", peak_kind)}
-        del hsets
-    except _lib.BybyCudaError as e:
-        extras["f16_decode"] = {"error": str(e)}
+            def f16(i):
+                wh, o = hsets[i % n_sets]
+                gb.tile_gemm(1, xh, wh, o, M=1, K=K_DEC, N=N_C2, route=_lib.ROUTE_GEMV, stream=stream)
+            ms = graph_steps(torch, timer, stream, f16, K, W)
+            check_device(_lib)
+            hb = fbytes + K_DEC * 2 + N_C2 * 4
+            extras["f16_decode"] = {"value": round(hb / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                                    "us_per_launch": round(ms * 1e3, 3),
+                                    "workload": "format 1 (fp16 weights) decode M=1 K=4096 N=11008, x bf16, out fp32",
+                                    "roofline": roofline(hb / (ms / 1e3) / 1e9, hbm_peak, "GB/s", "hbm", peak_kind)}
+            del hsets
+        except _lib.BybyCudaError as e:
+            extras["f16_decode"] = {"error": str(e)}
 
     # ---- weight ingestion: a checkpoint mapping copied into HBM (residentUploadQ4Mapped's copy)
-    import tempfile
-    import numpy as np
-    from bybylang_b200.mapped_file import openReadOnlyMapping, unmapReadOnlyFile
-    path = None
-    try:
-        nbytes = 1 << 30
-        fd, path = tempfile.mkstemp(prefix="bybyb200_ingest_", suffix=".bin")
-        blk = np.random.default_rng(SEED).integers(0, 256, 64 << 20, dtype=np.uint8).tobytes()
-        with os.fdopen(fd, "wb") as f:
-            for _ in range(nbytes // len(blk)):
-                f.write(blk)
-        dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        m = openReadOnlyMapping(path)
+    if on(args, "ingest"):
+        import tempfile
+        import numpy as np
+        from bybylang_b200.mapped_file import openReadOnlyMapping, unmapReadOnlyFile
+        path = None
         try:
-            rates = []
-            for _ in range(3):
+            nbytes = 1 << 30
+            fd, path = tempfile.mkstemp(prefix="bybyb200_ingest_", suffix=".bin")
+            blk = np.random.default_rng(SEED).integers(0, 256, 64 << 20, dtype=np.uint8).tobytes()
+            with os.fdopen(fd, "wb") as f:
+                for _ in range(nbytes // len(blk)):
+                    f.write(blk)
+            dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            m = openReadOnlyMapping(path)
+            try:
+                rates = []
+                for _ in range(3):
+                    torch.cuda.synchronize()
+                    t0 = time.perf_counter()
+                    _lib.call("bybycu_upload_host_range", C.c_void_p(dst.data_ptr()), C.c_void_p(m.data), nbytes)
+                    rates.append(nbytes / (time.perf_counter() - t0) / 1e9)
+                ok = torch.equal(dst[:len(blk)], torch.from_numpy(np.frombuffer(blk, np.uint8).copy()).to(dev))
+                with warnings.catch_warnings():   # a read-only mapping: torch only reads it here
+                    warnings.simplefilter("ignore", UserWarning)
+                    src = torch.from_numpy(m.view())   # pageable: the driver's own staging
                 torch.cuda.synchronize()
                 t0 = time.perf_counter()
-                _lib.call("bybycu_upload_host_range", C.c_void_p(dst.data_ptr()), C.c_void_p(m.data), nbytes)
-                rates.append(nbytes / (time.perf_counter() - t0) / 1e9)
-            ok = torch.equal(dst[:len(blk)], torch.from_numpy(np.frombuffer(blk, np.uint8).copy()).to(dev))
-            with warnings.catch_warnings():   # a read-only mapping: torch only reads it here
-                warnings.simplefilter("ignore", UserWarning)
-                src = torch.from_numpy(m.view())   # pageable: the driver's own staging
-            torch.cuda.synchronize()
-            t0 = time.perf_counter()
-            dst.copy_(src)
-            torch.cuda.synchronize()
-            plain = nbytes / (time.perf_counter() - t0) / 1e9
+                dst.copy_(src)
+                torch.cuda.synchronize()
+                plain = nbytes / (time.perf_counter() - t0) / 1e9
+            finally:
+                unmapReadOnlyFile(m)
+            extras["ingest"] = {"value": round(max(rates), 2), "unit": "GB/s", "runs": [round(r, 2) for r in rates],
+                                "workload": "1 GiB file mapping -> HBM through bybycu_upload_host_range (staged, "
+                                            f"{os.cpu_count()} host threads), page cache warm, host clock",
+                                "plain_pageable_copy_gbs": round(plain, 2), "bit_exact": bool(ok)}
+            del dst
+        except Exception as e:   # an I/O problem on the box must not cost the decode numbers
+            extras["ingest"] = {"error": str(e)}
         finally:
-            unmapReadOnlyFile(m)
-        extras["ingest"] = {"value": round(max(rates), 2), "unit": "GB/s", "runs": [round(r, 2) for r in rates],
-                            "workload": "1 GiB file mapping -> HBM through bybycu_upload_host_range (staged, "
-                                        f"{os.cpu_count()} host threads), page cache warm, host clock",
-                            "plain_pageable_copy_gbs": round(plain, 2), "bit_exact": bool(ok)}
-        del dst
-    except Exception as e:   # an I/O problem on the box must not cost the decode numbers
-        extras["ingest"] = {"error": str(e)}
-    finally:
-        if path and os.path.exists(path):
-            os.unlink(path)
+            if path and os.path.exists(path):
+                os.unlink(path)
 
 
 if __name__ == "__main__":

@@ -48,6 +48,7 @@ enum DeviceErr : uint32_t {
     kDevErrPeerWait = 5,    // a peer rank's signal never arrived
     kDevErrTmemAlloc = 6,   // tensor memory allocation failed
     kDevErrActRange = 7,    // an activation has no image in the route's operand format (out of range, inf, NaN)
+    kDevErrSplitWait = 8,   // a split-K part's partial sums never arrived
 };
 
 __device__ uint32_t g_device_error = 0;

@@ -141,7 +141,52 @@ struct Params {
     int64_t out_ld, out_col0;
     int out_bf16;
     PeerGather pg;    // world > 1: the epilogue also stores every value to the other ranks (fp32)
+    // Work units (the Q4 kernels): tiles [0, full_tiles) whole, every later tile as `split`
+    // K-parts (one unit each, weight-stage aligned) so that the last wave fills the pairs.
+    // Parts 0 .. split-2 leave fp32 partial sums in `partial` and count them in `flags` (one
+    // counter per tail tile, CTA and epilogue warp, zeroed by the staging pass); the last
+    // part adds them, in part order, to its own and stores the tile.
+    int units = 0;    // full_tiles + (tiles - full_tiles) * split
+    int full_tiles = 0;
+    int split = 1;
+    float* partial = nullptr;
+    uint32_t* flags = nullptr;
 };
+
+// One work unit: its tile, its part and its weight stages [kw0, kw1).
+struct WorkUnit {
+    int tile, part, kw0, kw1;
+};
+__device__ __forceinline__ WorkUnit work_unit(const Params& p, int u, int n_kw) {
+    WorkUnit w;
+    if (p.split <= 1 || u < p.full_tiles) {
+        w.tile = u;
+        w.part = 0;
+        w.kw0 = 0;
+        w.kw1 = n_kw;
+    } else {
+        const int v = u - p.full_tiles;
+        w.tile = p.full_tiles + v / p.split;
+        w.part = v % p.split;
+        w.kw0 = w.part * n_kw / p.split;
+        w.kw1 = (w.part + 1) * n_kw / p.split;
+    }
+    return w;
+}
+
+// Bounded wait (a whole warp) until a split-K counter reached `target`.
+__device__ __forceinline__ bool wait_flag(const uint32_t* f, uint32_t target) {
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (v >= target) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(kDevErrSplitWait);
+            return false;
+        }
+    }
+}
 
 // Bounded wait by plain try_wait polling.  With a suspend-time hint the waits of this kernel
 // slept through tcgen05.commit arrivals (the GEMM ran 8x slower), so it polls.  The polls
@@ -430,8 +475,11 @@ __host__ __device__ constexpr int perm_of(int mode, int kk) {
 }
 template <bool XF32, int PERM = kPermQ4B32>
 __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x, uint4* __restrict__ xp,
-                                                      int64_t nblocks, PeerGather pg) {
+                                                      int64_t nblocks, PeerGather pg, uint32_t* flags = nullptr,
+                                                      int n_flags = 0) {
     pdl_launch_dependents();   // the GEMM may start its prologue; it waits before reading xp
+    if (blockIdx.x == 0)       // the GEMM's split-K counters (its griddepcontrol.wait sees these)
+        for (int f = threadIdx.x; f < n_flags; f += blockDim.x) flags[f] = 0u;
     if (pg.split && pg.world > 1) {   // split phase: x may be the previous launch's gathered output
         if (threadIdx.x == 0) peer_gather_wait_previous(pg);
         __syncthreads();
@@ -484,12 +532,25 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
     constexpr int kChunk = BN < 32 ? BN : 32;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t lead_d_empty = map_to_rank(d_empty, 0);
+    const int fl = quarter * 32 + lane;   // this thread's feature inside the CTA's 128 rows
     for (int t = 0; t < my_tiles; ++t) {
         const int b = t % ACCB, u = t / ACCB;
-        const int tile = pair + t * pairs;
-        const int feat = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta + quarter * 32 + lane;
+        const int unit = pair + t * pairs;
+        const WorkUnit w = work_unit(p, unit, 1);
+        const int tile = w.tile;
+        const int feat = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta + fl;
         const int tok0 = (tile / p.tiles_n) * BN;
-        const bool ok = __all_sync(0xffffffffu, wait_bar(&d_full[b], u & 1, kDevErrMmaWait));
+        // split-K tail tile: this CTA's 128 x BN partial sums of part q at part_at(q)
+        const bool tail = p.split > 1 && unit >= p.full_tiles;
+        const bool last = !tail || w.part == p.split - 1;
+        const int tix = tail ? (unit - p.full_tiles) / p.split : 0;
+        auto part_at = [&](int q) {
+            return p.partial + (static_cast<int64_t>(tix * (p.split - 1) + q) * 2 + rank) * (BN * kRowsCta) + fl;
+        };
+        uint32_t* flag = tail ? p.flags + (tix * 2 + rank) * 4 + quarter : nullptr;
+        bool ok = __all_sync(0xffffffffu, wait_bar(&d_full[b], u & 1, kDevErrMmaWait));
+        if (ok && tail && last)   // the other parts of this tile stored their sums
+            ok = __all_sync(0xffffffffu, wait_flag(flag, static_cast<uint32_t>(p.split - 1)));
         if (!ok) {
             *s_abort = 1;
             break;
@@ -502,6 +563,20 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
             if constexpr (kChunk == 32) tmem_ld32(tmem + lane_addr + b * BN + c0, v);
             else tmem_ld16(tmem + lane_addr + b * BN + c0, v);
             tc_wait_ld();
+            if (!last) {   // an earlier part: the partial sums, [token][feature] (coalesced)
+                float* q = part_at(w.part) + c0 * kRowsCta;
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) q[j * kRowsCta] = __uint_as_float(v[j]);
+                continue;
+            }
+            if (tail) {   // the parts' sums in part order, then this part's
+#pragma unroll
+                for (int j = 0; j < kChunk; ++j) {
+                    float sum = part_at(0)[(c0 + j) * kRowsCta];
+                    for (int q = 1; q < p.split - 1; ++q) sum += part_at(q)[(c0 + j) * kRowsCta];
+                    v[j] = __float_as_uint(sum + __uint_as_float(v[j]));
+                }
+            }
             if (feat_ok) {
                 const int nt = min(kChunk, p.M - (tok0 + c0));
                 if (p.out_bf16) {
@@ -525,7 +600,11 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(lead_d_empty + 8u * b);
+        if (lane == 0) {
+            if (!last)   // release: the warp's partial stores (ordered by the warp barrier) first
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
+            mbar_arrive_cluster(lead_d_empty + 8u * b);
+        }
     }
 }
 
@@ -594,9 +673,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const uint32_t tmem = *tmem_slot;
 
     const int pair = static_cast<int>(blockIdx.x >> 1), pairs = static_cast<int>(gridDim.x >> 1);
-    const int my_tiles = p.tiles > pair ? (p.tiles - 1 - pair) / pairs + 1 : 0;
-    const int n_ks = p.K / kXK;            // activation stages per tile
-    const int n_kw = p.K / kWK;            // weight stages per tile
+    const int my_units = p.units > pair ? (p.units - 1 - pair) / pairs + 1 : 0;
+    const int n_kw = p.K / kWK;            // weight stages of a whole tile
 
     if (warp == 0) {
         // ------------------------------------------------------------ activation producer
@@ -608,10 +686,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             // already-satisfied load per rank)
             peer_gather_wait_previous(p.pg);
             int issued = 0;
-            for (int t = 0; t < my_tiles && !*s_abort; ++t) {
-                const int tile = pair + t * pairs;
-                const int tok = (tile / p.tiles_n) * BN + static_cast<int>(rank) * T::kTokCta;
-                for (int ks = 0; ks < n_ks; ++ks) {
+            for (int t = 0; t < my_units && !*s_abort; ++t) {
+                const WorkUnit w = work_unit(p, pair + t * pairs, n_kw);
+                const int tok = (w.tile / p.tiles_n) * BN + static_cast<int>(rank) * T::kTokCta;
+                for (int ks = w.kw0 * kSubs; ks < w.kw1 * kSubs; ++ks) {
                     const int s = issued % kStages, r = issued / kStages;
                     if (r > 0 && !wait_bar(&x_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
                         *s_abort = 1;
@@ -637,7 +715,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // ------------------------------- (odd CTA) tells rank 0 that its half has landed
         if (!leader && lane == 0) {
             const uint32_t lead_full = map_to_rank(full, 0);
-            const int total = my_tiles * n_ks;
+            int total = 0;
+            for (int t = 0; t < my_units; ++t) {
+                const WorkUnit w = work_unit(p, pair + t * pairs, n_kw);
+                total += (w.kw1 - w.kw0) * kSubs;
+            }
             for (int i = 0; i < total; ++i) {
                 const int s = i % kStages;
                 if (!wait_bar(&full[s], (i / kStages) & 1, kDevErrFullWait) || *s_abort) {
@@ -655,10 +737,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             if constexpr (ASYM) prefetch_tensormap(&maps.z);
             const uint64_t policy = l2_policy_evict_last();
             int issued = 0;
-            for (int t = 0; t < my_tiles && !*s_abort; ++t) {
-                const int tile = pair + t * pairs;
-                const int row0 = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta;
-                for (int kw = 0; kw < n_kw; ++kw) {
+            for (int t = 0; t < my_units && !*s_abort; ++t) {
+                const WorkUnit w = work_unit(p, pair + t * pairs, n_kw);
+                const int row0 = (w.tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta;
+                for (int kw = w.kw0; kw < w.kw1; ++kw) {
                     const int s = issued % kWSt, r = issued / kWSt;
                     if (r > 0 && !wait_bar(&w_empty[s], (r - 1) & 1, kDevErrEmptyWait)) {
                         *s_abort = 1;
@@ -688,7 +770,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 tc_commit_pair(&a_empty[i % kAStages]);
             };
             int consumed = 0, pending = -1;
-            for (int t = 0; t < my_tiles && !*s_abort; ++t) {
+            for (int t = 0; t < my_units && !*s_abort; ++t) {
+                const WorkUnit w = work_unit(p, pair + t * pairs, n_kw);
+                const int n_ks = (w.kw1 - w.kw0) * kSubs;   // this unit's activation stages
                 const int b = t % L::kAccBufs, u = t / L::kAccBufs;
                 if (u > 0 && !__all_sync(0xffffffffu, wait_bar(&d_empty[b], (u - 1) & 1, kDevErrMmaWait))) {
                     *s_abort = 1;
@@ -742,106 +826,112 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         const int row = quarter * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
         const uint32_t lead_full = map_to_rank(full, 0);
-        bool ok = true;
-        const int total = my_tiles * n_ks;
-        for (int i = grp; i < total && ok && grp < L::kGroups; i += L::kGroups) {
-            const int ks = i % n_ks;
-            const int wsg = (i / n_ks) * n_kw + ks / kSubs;         // weight stage, counted over tiles
-            const int sub = ks % kSubs;                             // which half of it
-            const int ws = wsg % kWSt;
-            ok = wait_bar(&w_full[ws], (wsg / kWSt) & 1, kDevErrFullWait) && !*s_abort;
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            // this stage's four 32-blocks of the weight stage: c = 4 * sub + h
-            const uint32_t wrow = base + L::kOffW + ws * kWStageBytes + row * 128;
-            uint4 chunk[4];
+        bool ok = grp < L::kGroups;
+        // i counts the CTA's activation stages over its units, wbase its weight stages
+        int i = 0, wbase = 0;
+        for (int t = 0; t < my_units && ok; ++t) {
+            const WorkUnit w = work_unit(p, pair + t * pairs, n_kw);
+            const int n_ks = (w.kw1 - w.kw0) * kSubs;
+            for (int ks = 0; ks < n_ks && ok; ++ks, ++i) {
+                if (i % L::kGroups != grp) continue;
+                const int wsg = wbase + ks / kSubs;                     // weight stage, counted over units
+                const int sub = ks % kSubs;                             // which half of it
+                const int ws = wsg % kWSt;
+                ok = wait_bar(&w_full[ws], (wsg / kWSt) & 1, kDevErrFullWait) && !*s_abort;
+                ok = __all_sync(0xffffffffu, ok);
+                if (!ok) break;
+                // this stage's four 32-blocks of the weight stage: c = 4 * sub + h
+                const uint32_t wrow = base + L::kOffW + ws * kWStageBytes + row * 128;
+                uint4 chunk[4];
 #pragma unroll
-            for (int h = 0; h < 4; ++h) chunk[h] = lds_u128(wrow + (((4 * sub + h) ^ (row & 7)) << 4));
-            uint4 sc;
-            float4 sa, za;   // asymmetric: fp32 scales and zero points of blocks 4 sub .. 4 sub + 3
-            if constexpr (ASYM) {
-                const uint32_t sb = base + L::kOffS + ws * L::kSBytes + row * 32 + sub * 16;
-                sa = lds_v4f(sb);
-                za = lds_v4f(sb + L::kZOff);
-            } else {
-                sc = lds_u128(base + L::kOffS + ws * L::kSBytes + row * 16);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&w_empty[ws]);   // the two groups of its halves release it
-            const int s = i % kStages;                          // its activation stage (full barrier)
-            const int slot = i % kAStages, r = i / kAStages;    // its A slot (pair, when EXACT)
-            if (r > 0) ok = wait_bar(&a_empty[slot], (r - 1) & 1, kDevErrEmptyWait);
-            ok = __all_sync(0xffffffffu, ok && !*s_abort);
-            if (!ok) break;
-            tc_fence_after();
-            if constexpr (ASYM) {
-                const __half2 sv[4] = {__float2half2_rn(sa.x), __float2half2_rn(sa.y), __float2half2_rn(sa.z),
-                                       __float2half2_rn(sa.w)};
-                const __half2 mz[4] = {__float2half2_rn(-za.x * sa.x), __float2half2_rn(-za.y * sa.y),
-                                       __float2half2_rn(-za.z * sa.z), __float2half2_rn(-za.w * sa.w)};
+                for (int h = 0; h < 4; ++h) chunk[h] = lds_u128(wrow + (((4 * sub + h) ^ (row & 7)) << 4));
+                uint4 sc;
+                float4 sa, za;   // asymmetric: fp32 scales and zero points of blocks 4 sub .. 4 sub + 3
+                if constexpr (ASYM) {
+                    const uint32_t sb = base + L::kOffS + ws * L::kSBytes + row * 32 + sub * 16;
+                    sa = lds_v4f(sb);
+                    za = lds_v4f(sb + L::kZOff);
+                } else {
+                    sc = lds_u128(base + L::kOffS + ws * L::kSBytes + row * 16);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&w_empty[ws]);   // the two groups of its halves release it
+                const int s = i % kStages;                          // its activation stage (full barrier)
+                const int slot = i % kAStages, r = i / kAStages;    // its A slot (pair, when EXACT)
+                if (r > 0) ok = wait_bar(&a_empty[slot], (r - 1) & 1, kDevErrEmptyWait);
+                ok = __all_sync(0xffffffffu, ok && !*s_abort);
+                if (!ok) break;
+                tc_fence_after();
+                if constexpr (ASYM) {
+                    const __half2 sv[4] = {__float2half2_rn(sa.x), __float2half2_rn(sa.y), __float2half2_rn(sa.z),
+                                           __float2half2_rn(sa.w)};
+                    const __half2 mz[4] = {__float2half2_rn(-za.x * sa.x), __float2half2_rn(-za.y * sa.y),
+                                           __float2half2_rn(-za.z * sa.z), __float2half2_rn(-za.w * sa.w)};
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    uint32_t col[32];
+                    for (int half = 0; half < 2; ++half) {
+                        uint32_t col[32];
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int blk = 2 * half + h;
+                        for (int h = 0; h < 2; ++h) {
+                            const int blk = 2 * half + h;
+                            const uint4 u = chunk[blk];
+                            dequant_word_asym(u.x, sv[blk], mz[blk], &col[16 * h + 0]);
+                            dequant_word_asym(u.y, sv[blk], mz[blk], &col[16 * h + 4]);
+                            dequant_word_asym(u.z, sv[blk], mz[blk], &col[16 * h + 8]);
+                            dequant_word_asym(u.w, sv[blk], mz[blk], &col[16 * h + 12]);
+                        }
+                        tmem_st32(tmem + lane_addr + L::kAOff + slot * kACols + half * 32, col);
+                    }
+                } else if constexpr (EXACT) {
+                    const uint32_t sw0 = sub ? sc.z : sc.x, sw1 = sub ? sc.w : sc.y;
+                    const uint32_t a_hi = tmem + lane_addr + L::kAOff + 2 * slot * kACols;
+                    // one block (16 columns of each term) at a time: 32 live column registers
+#pragma unroll
+                    for (int blk = 0; blk < 4; ++blk) {
+                        const uint32_t pr = (blk >> 1) ? sw1 : sw0;           // two blocks' fp16 scales
+                        const uint32_t prh = pr & 0xFFF8FFF8u;                // s_hi of both
+                        const __half2 lo2 = __hsub2(bits_h2(pr), bits_h2(prh));   // s_lo, exact
+                        const __half2 shi = (blk & 1) ? __high2half2(bits_h2(prh)) : __low2half2(bits_h2(prh));
+                        const __half2 slo = (blk & 1) ? __high2half2(lo2) : __low2half2(lo2);
+                        uint32_t hcol[16], lcol[16];
                         const uint4 u = chunk[blk];
-                        dequant_word_asym(u.x, sv[blk], mz[blk], &col[16 * h + 0]);
-                        dequant_word_asym(u.y, sv[blk], mz[blk], &col[16 * h + 4]);
-                        dequant_word_asym(u.z, sv[blk], mz[blk], &col[16 * h + 8]);
-                        dequant_word_asym(u.w, sv[blk], mz[blk], &col[16 * h + 12]);
+                        dequant_word_exact(u.x, shi, slo, &hcol[0], &lcol[0]);
+                        dequant_word_exact(u.y, shi, slo, &hcol[4], &lcol[4]);
+                        dequant_word_exact(u.z, shi, slo, &hcol[8], &lcol[8]);
+                        dequant_word_exact(u.w, shi, slo, &hcol[12], &lcol[12]);
+                        tmem_st16(a_hi + blk * 16, hcol);
+                        tmem_st16(a_hi + kACols + blk * 16, lcol);
                     }
-                    tmem_st32(tmem + lane_addr + L::kAOff + slot * kACols + half * 32, col);
-                }
-            } else if constexpr (EXACT) {
-                const uint32_t sw0 = sub ? sc.z : sc.x, sw1 = sub ? sc.w : sc.y;
-                const uint32_t a_hi = tmem + lane_addr + L::kAOff + 2 * slot * kACols;
-                // one block (16 columns of each term) at a time: 32 live column registers
+                } else {
+                    // scales of blocks 4 sub .. 4 sub + 3: two 32-bit words of the row's eight
+                    const uint32_t sw0 = sub ? sc.z : sc.x, sw1 = sub ? sc.w : sc.y;
 #pragma unroll
-                for (int blk = 0; blk < 4; ++blk) {
-                    const uint32_t pr = (blk >> 1) ? sw1 : sw0;           // two blocks' fp16 scales
-                    const uint32_t prh = pr & 0xFFF8FFF8u;                // s_hi of both
-                    const __half2 lo2 = __hsub2(bits_h2(pr), bits_h2(prh));   // s_lo, exact
-                    const __half2 shi = (blk & 1) ? __high2half2(bits_h2(prh)) : __low2half2(bits_h2(prh));
-                    const __half2 slo = (blk & 1) ? __high2half2(lo2) : __low2half2(lo2);
-                    uint32_t hcol[16], lcol[16];
-                    const uint4 u = chunk[blk];
-                    dequant_word_exact(u.x, shi, slo, &hcol[0], &lcol[0]);
-                    dequant_word_exact(u.y, shi, slo, &hcol[4], &lcol[4]);
-                    dequant_word_exact(u.z, shi, slo, &hcol[8], &lcol[8]);
-                    dequant_word_exact(u.w, shi, slo, &hcol[12], &lcol[12]);
-                    tmem_st16(a_hi + blk * 16, hcol);
-                    tmem_st16(a_hi + kACols + blk * 16, lcol);
-                }
-            } else {
-                // scales of blocks 4 sub .. 4 sub + 3: two 32-bit words of the row's eight
-                const uint32_t sw0 = sub ? sc.z : sc.x, sw1 = sub ? sc.w : sc.y;
+                    for (int half = 0; half < 2; ++half) {
+                        const __half2 pr = bits_h2(half ? sw1 : sw0);
+                        uint32_t col[32];
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const __half2 pr = bits_h2(half ? sw1 : sw0);
-                    uint32_t col[32];
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const __half2 sv = h ? __half2half2(pr.y) : __half2half2(pr.x);
-                        const __half2 s16 = __hmul2(sv, bits_h2(0x2C002C00u));   // x 1/16
-                        const uint4 u = chunk[2 * half + h];
-                        dequant_word(u.x, sv, s16, &col[16 * h + 0]);
-                        dequant_word(u.y, sv, s16, &col[16 * h + 4]);
-                        dequant_word(u.z, sv, s16, &col[16 * h + 8]);
-                        dequant_word(u.w, sv, s16, &col[16 * h + 12]);
+                        for (int h = 0; h < 2; ++h) {
+                            const __half2 sv = h ? __half2half2(pr.y) : __half2half2(pr.x);
+                            const __half2 s16 = __hmul2(sv, bits_h2(0x2C002C00u));   // x 1/16
+                            const uint4 u = chunk[2 * half + h];
+                            dequant_word(u.x, sv, s16, &col[16 * h + 0]);
+                            dequant_word(u.y, sv, s16, &col[16 * h + 4]);
+                            dequant_word(u.z, sv, s16, &col[16 * h + 8]);
+                            dequant_word(u.w, sv, s16, &col[16 * h + 12]);
+                        }
+                        tmem_st32(tmem + lane_addr + L::kAOff + slot * kACols + half * 32, col);
                     }
-                    tmem_st32(tmem + lane_addr + L::kAOff + slot * kACols + half * 32, col);
                 }
+                tc_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(lead_full + 8u * s);
             }
-            tc_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(lead_full + 8u * s);
+            wbase += w.kw1 - w.kw0;
         }
-        if (!ok) *s_abort = 1;
+        if (!ok && grp < L::kGroups) *s_abort = 1;
     } else {
         // ---------------------------------------------------------------------- epilogue
-        epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_tiles, pair, pairs, rank, warp & 3,
+        epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_units, pair, pairs, rank, warp & 3,
                                           lane);
     }
     tc_fence_before();
@@ -954,21 +1044,43 @@ struct TcWeights {
     const float* zeros = nullptr;
 };
 
-// The staging pass and the GEMM with BN-token tiles, with `xp` (M * K fp16) as the staging
-// buffer.  Allocates nothing.
+// The split-K plan of a GEMM of `tiles` pair tiles on `max_pairs` co-resident pairs: when the
+// last wave leaves at least half of the pairs idle, its tiles are cut into `split` K-parts
+// (at most 8, weight-stage aligned) so that it fills them.
+struct SplitPlan {
+    int full_tiles, split, units;
+    int64_t partial_floats, flags;
+};
+static SplitPlan tc_split_plan(int64_t tiles, int max_pairs, int n_kw, int bn) {
+    SplitPlan sp{static_cast<int>(tiles), 1, static_cast<int>(tiles), 0, 0};
+    const int64_t full = (tiles / max_pairs) * max_pairs, tail = tiles - full;
+    if (tail == 0) return sp;
+    const int split = static_cast<int>(std::min<int64_t>(std::min<int64_t>(max_pairs / tail, 8), n_kw));
+    if (split < 2) return sp;
+    sp.full_tiles = static_cast<int>(full);
+    sp.split = split;
+    sp.units = static_cast<int>(full + tail * split);
+    sp.partial_floats = tail * (split - 1) * 2 * bn * tc::kRowsCta;
+    sp.flags = tail * 2 * 4;
+    return sp;
+}
+
+// The staging pass and the GEMM with BN-token tiles over the work units of `sp`, with `xp`
+// (M * K fp16) as the staging buffer and `partial` / `flags` as the split-K scratch.
 template <bool ASYM, bool EXACT, int BN>
-static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp) {
-    DeviceInfo info;
-    int max_pairs = 0;
-    if (int rc = tc_setup<ASYM, EXACT, BN>(&info, &max_pairs)) return rc;
+static int tc_launch(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitPlan& sp, float* partial,
+                     uint32_t* flags, int max_pairs, int tiles_n, int64_t tiles) {
     const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
     const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
     constexpr int perm = ASYM ? tc::kPermAsym : tc::kPermQ4B32;
     const PeerGather pg = a.pg ? *a.pg : PeerGather();
+    const int n_flags = static_cast<int>(sp.flags);
     if (a.x_dtype == BYBYCU_DT_F32)
-        tc::stage_x_kernel<true, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg);
+        tc::stage_x_kernel<true, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg, flags,
+                                                                     n_flags);
     else
-        tc::stage_x_kernel<false, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg);
+        tc::stage_x_kernel<false, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg,
+                                                                      flags, n_flags);
     BYBYCU_LAUNCH_CHECK("stage_x_kernel");
 
     tc::Maps maps;
@@ -993,9 +1105,7 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp) {
     p.M = a.M;
     p.K = a.K;
     p.N = a.N;
-    p.tiles_n = static_cast<int>(ceil_div(a.N, tc::kRowsPair));
-    const int64_t tiles = static_cast<int64_t>(p.tiles_n) * ceil_div(a.M, BN);
-    if (tiles > (1 << 30)) return set_error(BYBYCU_ERR_SHAPE, "tensor-core route: too many tiles (M=%d N=%d)", a.M, a.N);
+    p.tiles_n = tiles_n;
     p.tiles = static_cast<int>(tiles);
     p.out = a.out;
     p.out_ld = a.out_ld;
@@ -1005,7 +1115,12 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp) {
         if (p.out_bf16) return set_error(BYBYCU_ERR_ARGS, "tensor-core all-gather: the gathered output is fp32");
         p.pg = *a.pg;
     }
-    const int pairs = static_cast<int>(std::min<int64_t>(tiles, max_pairs));
+    p.units = sp.units;
+    p.full_tiles = sp.full_tiles;
+    p.split = sp.split;
+    p.partial = partial;
+    p.flags = flags;
+    const int pairs = std::min(sp.units, max_pairs);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1026,13 +1141,41 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp) {
     return BYBYCU_OK;
 }
 
+// tc_launch with a split-K plan: with `split_ok` a tail that leaves pairs idle is split and
+// its partial sums and counters come from the stream-ordered pool; without it the GEMM
+// allocates nothing and runs whole tiles.
+template <bool ASYM, bool EXACT, int BN>
+static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp, bool split_ok) {
+    DeviceInfo info;
+    int max_pairs = 0;
+    if (int rc = tc_setup<ASYM, EXACT, BN>(&info, &max_pairs)) return rc;
+    const int tiles_n = static_cast<int>(ceil_div(a.N, tc::kRowsPair));
+    const int64_t tiles = static_cast<int64_t>(tiles_n) * ceil_div(a.M, BN);
+    if (tiles > (1 << 30)) return set_error(BYBYCU_ERR_SHAPE, "tensor-core route: too many tiles (M=%d N=%d)", a.M, a.N);
+    SplitPlan sp{static_cast<int>(tiles), 1, static_cast<int>(tiles), 0, 0};
+    if (split_ok) sp = tc_split_plan(tiles, max_pairs, a.K / tc::kWK, BN);
+    if (sp.split == 1) return tc_launch<ASYM, EXACT, BN>(a, wt, xp, sp, nullptr, nullptr, max_pairs, tiles_n, tiles);
+    cudaMemPool_t pool = nullptr;
+    if (int rc = scratch_pool(info.device, &pool)) return rc;
+    void* part = nullptr;
+    BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&part, (sp.partial_floats + sp.flags) * 4, pool, a.stream));
+    float* partial = static_cast<float*>(part);
+    const int rc = tc_launch<ASYM, EXACT, BN>(a, wt, xp, sp, partial,
+                                              reinterpret_cast<uint32_t*>(partial + sp.partial_floats), max_pairs,
+                                              tiles_n, tiles);
+    const cudaError_t fe = cudaFreeAsync(part, a.stream);
+    if (rc) return rc;
+    if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc split-K scratch)");
+    return BYBYCU_OK;
+}
+
 template <bool ASYM, bool EXACT>
-static int tc_run_rows(const GemmArgs& a, const TcWeights& wt, void* xp) {
+static int tc_run_rows(const GemmArgs& a, const TcWeights& wt, void* xp, bool split_ok) {
     switch (tc_token_tile(a.M)) {
-        case 16: return tc_run<ASYM, EXACT, 16>(a, wt, xp);
-        case 32: return tc_run<ASYM, EXACT, 32>(a, wt, xp);
-        case 64: return tc_run<ASYM, EXACT, 64>(a, wt, xp);
-        default: return tc_run<ASYM, EXACT, 128>(a, wt, xp);
+        case 16: return tc_run<ASYM, EXACT, 16>(a, wt, xp, split_ok);
+        case 32: return tc_run<ASYM, EXACT, 32>(a, wt, xp, split_ok);
+        case 64: return tc_run<ASYM, EXACT, 64>(a, wt, xp, split_ok);
+        default: return tc_run<ASYM, EXACT, 128>(a, wt, xp, split_ok);
     }
 }
 
@@ -1046,7 +1189,7 @@ static int tc_pooled(const GemmArgs& a, const TcWeights& wt) {
     cudaMemPool_t pool = nullptr;
     if (int rc = scratch_pool(info.device, &pool)) return rc;
     BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
-    const int rc = tc_run_rows<ASYM, EXACT>(a, wt, xp);
+    const int rc = tc_run_rows<ASYM, EXACT>(a, wt, xp, true);
     const cudaError_t fe = cudaFreeAsync(xp, a.stream);
     if (rc) return rc;
     if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc scratch)");
@@ -1146,7 +1289,7 @@ int launch_tc_static_scratch(const GemmArgs& a) {
     TcWeights wt;
     wt.nibbles = a.packed;
     wt.scales = a.packed + a.scale_base;
-    return tc_run_rows<false, true>(a, wt, xp);
+    return tc_run_rows<false, true>(a, wt, xp, false);
 }
 
 }  // namespace bybycu

@@ -65,7 +65,10 @@ def test_tc_golden_cases(golden, oracle_mod):
 @pytest.mark.parametrize("M,K,N", [(1, 256, 1), (17, 256, 130), (256, 512, 128), (300, 768, 200),
                                    (513, 1024, 384), (1000, 2048, 77)])
 def test_tc_ragged_shapes_against_oracle(M, K, N, oracle_mod):
-    """Partial token tiles (M % 256) and partial weight-row tiles (N % 128)."""
+    """Partial token tiles and partial weight-row tiles.  With fewer tiles than half the CTA
+    pairs the GEMM cuts its last wave's tiles into 2 to 8 K-parts whose partial sums the last
+    part adds: every case here but the first two (one weight stage of K) takes that path, with
+    uneven parts at K = 768."""
     O = oracle_mod
     p, s, xb, slot, sb = _case(O, M, K, N, seed=M + N)
     want = O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, M, K, N, threads=8)

@@ -233,6 +233,7 @@ struct DeviceInfo {
     int device = -1;
     int sm_count = 0;
     int max_smem_optin = 0;
+    int smem_per_sm = 0;
     int cc_major = 0, cc_minor = 0;
 };
 int current_device_info(DeviceInfo* info);

@@ -1247,13 +1247,20 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
         }
     }
     if (!kc) return set_error(BYBYCU_ERR_SHAPE, "GEMV: shared memory too small for M=%d", a.M);
-    // Ring depth of the M = 1 kernel.  One pass per CTA: two stages, so that two CTAs share an
-    // SM and the next launch's CTA streams its first stages while this one computes (C2: 6.4 us
-    // against 7.1 with three stages).  Several passes: three stages and one CTA per SM, whose
-    // deeper ring keeps the long stream in flight (1 x 32000 x 4096: 16.1 us against 17.9).
+    // Ring depth of the M = 1 kernel.  One pass per CTA: as many stages as leave room for two
+    // CTAs per SM (at least two), so that the next launch's CTA streams its first stages - all
+    // of them when they fit - while this one computes (C2, 75 rows a CTA: two stages, 6.4 us
+    // against 7.1 with three and one CTA per SM; 28 rows a CTA at N = 4096: four).  Several
+    // passes: three stages and one CTA per SM, whose deeper ring keeps the long stream in
+    // flight (1 x 32000 x 4096: 16.1 us against 17.9).
     // A tuned plan's depth (a.stages), then BYBY_CUDA_GEMV_STAGES, override.
     const int fit = stages;   // the most that fit in shared memory (and are useful)
-    if (m1) stages = std::min(fit, tiles_max > tp ? 3 : 2);
+    if (m1) {
+        const size_t half_sm = static_cast<size_t>(dev.smem_per_sm) / 2 - 1024;   // per CTA, two per SM
+        const size_t fixed = 1024 + 16 + red_bytes + x_all;
+        const int two_cta = half_sm > fixed ? static_cast<int>((half_sm - fixed) / (stage_bytes + 16)) : 0;
+        stages = std::min(fit, tiles_max > tp ? 3 : std::max(2, two_cta));
+    }
     if (a.stages >= 1) stages = std::min(fit, a.stages);
     if (const char* e = getenv("BYBY_CUDA_GEMV_STAGES")) {
         const int want_stages = atoi(e);

@@ -395,10 +395,12 @@ BYBYCU_API int bybycu_shard_range(int N, int world, int rank, int align, int* n0
  * per rank, the device-side epoch and a CTA completion counter - zero before first use) and
  * waits, bounded, until every rank's counter for this epoch is present in its own.  On the
  * decode (GEMV) route the GEMV kernel itself stores to the peers and waits, so one launch
- * does the whole step.  A rank may start writing the next call's slices into a peer's out
+ * does the whole step; on the tensor-core route the GEMM's epilogue does the same tile by
+ * tile (after the staging pass); other routes add one copy kernel.  A rank may start writing the next call's slices into a peer's out
  * while that peer still reads the previous result: callers that read out while other ranks
  * may already run the next call alternate two sets of buffers.  epoch = 0 keeps the epoch on
- * the device (graph-capturable); epoch > 0 is the caller's count of calls, starting at 1.  out is [M, N] fp32 row-major on every rank.  Replaces the gather of text results
+ * the device (graph-capturable); epoch > 0 is the caller's count of calls, starting at 1.
+ * out is [M, N] fp32 row-major on every rank.  Replaces the gather of text results
  * in runShards (distributed.nim:304-375) with a device-side all-gather. */
 BYBYCU_API int bybycu_tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1,
                                const void* x, int x_dtype,

@@ -143,9 +143,10 @@ struct Params {
     PeerGather pg;    // world > 1: the epilogue also stores every value to the other ranks (fp32)
     // Work units (the Q4 kernels): tiles [0, full_tiles) whole, every later tile as `split`
     // K-parts (one unit each, weight-stage aligned) so that the last wave fills the pairs.
-    // Parts 0 .. split-2 leave fp32 partial sums in `partial` and count them in `flags` (one
-    // counter per tail tile, CTA and epilogue warp, zeroed by the staging pass); the last
-    // part adds them, in part order, to its own and stores the tile.
+    // Parts 0 .. split-2 leave fp32 partial sums in `partial` ([tail tile][part][CTA][warp]
+    // blocks of BN tokens x 32 features) and count them in `flags` (one counter per tail tile,
+    // CTA and epilogue warp, zeroed by the staging pass); the last part adds them, in part
+    // order, to its own and stores the tile.
     int units = 0;    // full_tiles + (tiles - full_tiles) * split
     int full_tiles = 0;
     int split = 1;
@@ -173,6 +174,14 @@ __device__ __forceinline__ WorkUnit work_unit(const Params& p, int u, int n_kw) 
     }
     return w;
 }
+
+// 16-byte global -> shared copies (L2 only) and their completion.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // Bounded wait (a whole warp) until a split-K counter reached `target`.
 __device__ __forceinline__ bool wait_flag(const uint32_t* f, uint32_t target) {
@@ -528,24 +537,25 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x
 template <int BN, int ACCB>
 __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem, uint64_t* d_full,
                                                  uint64_t* d_empty, volatile int* s_abort, int my_tiles, int pair,
-                                                 int pairs, uint32_t rank, int quarter, int lane) {
+                                                 int pairs, uint32_t rank, int quarter, int lane,
+                                                 uint32_t stage_smem = 0) {
     constexpr int kChunk = BN < 32 ? BN : 32;
+    constexpr int kBlock = BN * 32;   // floats of one warp's partial sums (BN tokens x 32 features)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t lead_d_empty = map_to_rank(d_empty, 0);
-    const int fl = quarter * 32 + lane;   // this thread's feature inside the CTA's 128 rows
     for (int t = 0; t < my_tiles; ++t) {
         const int b = t % ACCB, u = t / ACCB;
         const int unit = pair + t * pairs;
         const WorkUnit w = work_unit(p, unit, 1);
         const int tile = w.tile;
-        const int feat = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta + fl;
+        const int feat = (tile % p.tiles_n) * kRowsPair + static_cast<int>(rank) * kRowsCta + quarter * 32 + lane;
         const int tok0 = (tile / p.tiles_n) * BN;
-        // split-K tail tile: this CTA's 128 x BN partial sums of part q at part_at(q)
+        // split-K tail tile: this warp's partial sums of part q at part_at(q)
         const bool tail = p.split > 1 && unit >= p.full_tiles;
         const bool last = !tail || w.part == p.split - 1;
         const int tix = tail ? (unit - p.full_tiles) / p.split : 0;
         auto part_at = [&](int q) {
-            return p.partial + (static_cast<int64_t>(tix * (p.split - 1) + q) * 2 + rank) * (BN * kRowsCta) + fl;
+            return p.partial + ((static_cast<int64_t>(tix * (p.split - 1) + q) * 2 + rank) * 4 + quarter) * kBlock;
         };
         uint32_t* flag = tail ? p.flags + (tix * 2 + rank) * 4 + quarter : nullptr;
         bool ok = __all_sync(0xffffffffu, wait_bar(&d_full[b], u & 1, kDevErrMmaWait));
@@ -556,6 +566,35 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
             break;
         }
         tc_fence_after();
+        // The last part sums the others' blocks in shared memory: the activation stages, free
+        // once this unit's MMAs completed (a tail unit is its pair's last), two blocks per warp.
+        // Every copy of a part goes out at once, one round trip per part.
+        const uint32_t sum_smem = stage_smem + static_cast<uint32_t>(quarter) * (2 * kBlock * 4);
+        if (tail && last) {
+            auto fetch = [&](int q, uint32_t dst) {
+                const float* src = part_at(q);
+#pragma unroll
+                for (int k = 0; k < kBlock / 4 / 32; ++k)
+                    cp_async16(dst + (k * 32 + lane) * 16, src + (k * 32 + lane) * 4);
+                cp_async_commit();
+            };
+            fetch(0, sum_smem);
+            if (p.split > 2) fetch(1, sum_smem + kBlock * 4);
+            for (int q = 1; q < p.split - 1; ++q) {
+                cp_async_wait<0>();
+                __syncwarp();
+                // this lane's feature over all tokens: the sum so far plus part q, in part order
+#pragma unroll 8
+                for (int tk = 0; tk < BN; ++tk) {
+                    const uint32_t o = static_cast<uint32_t>(tk * 32 + lane) * 4;
+                    sts_f32(sum_smem + o, lds_f32(sum_smem + o) + lds_f32(sum_smem + kBlock * 4 + o));
+                }
+                __syncwarp();
+                if (q + 1 < p.split - 1) fetch(q + 1, sum_smem + kBlock * 4);
+            }
+            cp_async_wait<0>();
+            __syncwarp();
+        }
         const bool feat_ok = feat < p.N;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += kChunk) {
@@ -563,20 +602,17 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
             if constexpr (kChunk == 32) tmem_ld32(tmem + lane_addr + b * BN + c0, v);
             else tmem_ld16(tmem + lane_addr + b * BN + c0, v);
             tc_wait_ld();
-            if (!last) {   // an earlier part: the partial sums, [token][feature] (coalesced)
-                float* q = part_at(w.part) + c0 * kRowsCta;
+            if (!last) {   // an earlier part: its partial sums, [token][feature] (coalesced)
+                float* q = part_at(w.part) + c0 * 32 + lane;
 #pragma unroll
-                for (int j = 0; j < kChunk; ++j) q[j * kRowsCta] = __uint_as_float(v[j]);
+                for (int j = 0; j < kChunk; ++j) q[j * 32] = __uint_as_float(v[j]);
                 continue;
             }
-            if (tail) {   // the parts' sums in part order, then this part's
+            if (tail)   // the other parts' sum, then this part's
 #pragma unroll
-                for (int j = 0; j < kChunk; ++j) {
-                    float sum = part_at(0)[(c0 + j) * kRowsCta];
-                    for (int q = 1; q < p.split - 1; ++q) sum += part_at(q)[(c0 + j) * kRowsCta];
-                    v[j] = __float_as_uint(sum + __uint_as_float(v[j]));
-                }
-            }
+                for (int j = 0; j < kChunk; ++j)
+                    v[j] = __float_as_uint(lds_f32(sum_smem + static_cast<uint32_t>((c0 + j) * 32 + lane) * 4) +
+                                           __uint_as_float(v[j]));
             if (feat_ok) {
                 const int nt = min(kChunk, p.M - (tok0 + c0));
                 if (p.out_bf16) {
@@ -931,8 +967,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (!ok && grp < L::kGroups) *s_abort = 1;
     } else {
         // ---------------------------------------------------------------------- epilogue
+        static_assert(kStages * T::kXStageBytes >= 4 * 2 * BN * 32 * 4, "split-K sums: two blocks per warp");
         epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_units, pair, pairs, rank, warp & 3,
-                                          lane);
+                                          lane, base + L::kOffX);
     }
     tc_fence_before();
     __syncthreads();
@@ -1046,7 +1083,10 @@ struct TcWeights {
 
 // The split-K plan of a GEMM of `tiles` pair tiles on `max_pairs` co-resident pairs: when the
 // last wave leaves at least half of the pairs idle, its tiles are cut into `split` K-parts
-// (at most 8, weight-stage aligned) so that it fills them.
+// (at most 8, weight-stage aligned) so that it fills them.  Every tail unit then lands in
+// the last round of the round-robin over the pairs (full_tiles is a multiple of the pairs,
+// or there are no full tiles and one unit per pair), which the epilogue relies on: a tail
+// unit is its pair's last, so its activation stages are free for summing the parts.
 struct SplitPlan {
     int full_tiles, split, units;
     int64_t partial_floats, flags;
@@ -1141,24 +1181,38 @@ static int tc_launch(const GemmArgs& a, const TcWeights& wt, void* xp, const Spl
     return BYBYCU_OK;
 }
 
-// tc_launch with a split-K plan: with `split_ok` a tail that leaves pairs idle is split and
-// its partial sums and counters come from the stream-ordered pool; without it the GEMM
-// allocates nothing and runs whole tiles.
+// Where a split-K tail keeps its partial sums and counters: the stream-ordered pool, or a
+// fixed region (`bytes` at `ptr`; a plan that needs more runs whole tiles).
+struct SplitScratch {
+    bool pool = false;
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+// tc_launch with a split-K plan: a tail that leaves pairs idle is split when `ss` offers
+// room for its partial sums and counters.
 template <bool ASYM, bool EXACT, int BN>
-static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp, bool split_ok) {
+static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitScratch& ss) {
     DeviceInfo info;
     int max_pairs = 0;
     if (int rc = tc_setup<ASYM, EXACT, BN>(&info, &max_pairs)) return rc;
     const int tiles_n = static_cast<int>(ceil_div(a.N, tc::kRowsPair));
     const int64_t tiles = static_cast<int64_t>(tiles_n) * ceil_div(a.M, BN);
     if (tiles > (1 << 30)) return set_error(BYBYCU_ERR_SHAPE, "tensor-core route: too many tiles (M=%d N=%d)", a.M, a.N);
-    SplitPlan sp{static_cast<int>(tiles), 1, static_cast<int>(tiles), 0, 0};
-    if (split_ok) sp = tc_split_plan(tiles, max_pairs, a.K / tc::kWK, BN);
+    const SplitPlan whole{static_cast<int>(tiles), 1, static_cast<int>(tiles), 0, 0};
+    SplitPlan sp = tc_split_plan(tiles, max_pairs, a.K / tc::kWK, BN);
+    const size_t sp_bytes = static_cast<size_t>(sp.partial_floats + sp.flags) * 4;
+    if (sp.split > 1 && !ss.pool && sp_bytes > ss.bytes) sp = whole;
     if (sp.split == 1) return tc_launch<ASYM, EXACT, BN>(a, wt, xp, sp, nullptr, nullptr, max_pairs, tiles_n, tiles);
+    if (!ss.pool) {
+        float* partial = static_cast<float*>(ss.ptr);
+        return tc_launch<ASYM, EXACT, BN>(a, wt, xp, sp, partial, reinterpret_cast<uint32_t*>(partial + sp.partial_floats),
+                                          max_pairs, tiles_n, tiles);
+    }
     cudaMemPool_t pool = nullptr;
     if (int rc = scratch_pool(info.device, &pool)) return rc;
     void* part = nullptr;
-    BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&part, (sp.partial_floats + sp.flags) * 4, pool, a.stream));
+    BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&part, sp_bytes, pool, a.stream));
     float* partial = static_cast<float*>(part);
     const int rc = tc_launch<ASYM, EXACT, BN>(a, wt, xp, sp, partial,
                                               reinterpret_cast<uint32_t*>(partial + sp.partial_floats), max_pairs,
@@ -1170,12 +1224,12 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp, bool split_o
 }
 
 template <bool ASYM, bool EXACT>
-static int tc_run_rows(const GemmArgs& a, const TcWeights& wt, void* xp, bool split_ok) {
+static int tc_run_rows(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitScratch& ss) {
     switch (tc_token_tile(a.M)) {
-        case 16: return tc_run<ASYM, EXACT, 16>(a, wt, xp, split_ok);
-        case 32: return tc_run<ASYM, EXACT, 32>(a, wt, xp, split_ok);
-        case 64: return tc_run<ASYM, EXACT, 64>(a, wt, xp, split_ok);
-        default: return tc_run<ASYM, EXACT, 128>(a, wt, xp, split_ok);
+        case 16: return tc_run<ASYM, EXACT, 16>(a, wt, xp, ss);
+        case 32: return tc_run<ASYM, EXACT, 32>(a, wt, xp, ss);
+        case 64: return tc_run<ASYM, EXACT, 64>(a, wt, xp, ss);
+        default: return tc_run<ASYM, EXACT, 128>(a, wt, xp, ss);
     }
 }
 
@@ -1189,7 +1243,9 @@ static int tc_pooled(const GemmArgs& a, const TcWeights& wt) {
     cudaMemPool_t pool = nullptr;
     if (int rc = scratch_pool(info.device, &pool)) return rc;
     BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
-    const int rc = tc_run_rows<ASYM, EXACT>(a, wt, xp, true);
+    SplitScratch ss;
+    ss.pool = true;
+    const int rc = tc_run_rows<ASYM, EXACT>(a, wt, xp, ss);
     const cudaError_t fe = cudaFreeAsync(xp, a.stream);
     if (rc) return rc;
     if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc scratch)");
@@ -1289,7 +1345,13 @@ int launch_tc_static_scratch(const GemmArgs& a) {
     TcWeights wt;
     wt.nibbles = a.packed;
     wt.scales = a.packed + a.scale_base;
-    return tc_run_rows<false, true>(a, wt, xp, false);
+    // a split-K tail keeps its sums in the array's room past the activations when they fit
+    // (the same plan, so the same sums, as the pooled route); otherwise whole tiles
+    SplitScratch ss;
+    const size_t used = (need + 255) / 256 * 256;
+    ss.ptr = static_cast<uint8_t*>(xp) + used;
+    ss.bytes = kStaticScratchBytes - used;
+    return tc_run_rows<false, true>(a, wt, xp, ss);
 }
 
 }  // namespace bybycu

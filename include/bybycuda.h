@@ -148,7 +148,9 @@ BYBYCU_API int bybycu_tile_gemm_host(int fmt, int M, int K, int N,
  *   first call here (and before any stream capture).  Each call then looks the array's
  *   address up (cudaGetSymbolAddress) in the current context; nothing is allocated or freed
  *   per call.  No part of it needs to start at zero: every byte the GEMM reads is written
- *   by the same call first.
+ *   by the same call first.  When the route splits its last wave's tiles along K, the
+ *   partial sums use the array's room past the staged activations; without room the tiles
+ *   run whole (the same result within the route's tolerance, summed in another order).
  *   Limit: M*K <= 16,777,216 (e.g. M=4096 at K=4096); larger shapes fail with
  *   BYBYCU_ERR_RANGE before anything is launched.  Shapes the TC route cannot tile
  *   (K % 256 != 0, unaligned slots) fail with BYBYCU_ERR_SHAPE.

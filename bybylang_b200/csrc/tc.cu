@@ -98,8 +98,11 @@ struct Cfg {
     // Dequantiser groups at work: at most one per A stage in flight, so that no group waits
     // for a slot phase two rounds ahead (a phase-parity wait cannot tell those apart).
     static constexpr int kGroups = kDequantGroups < kAStages ? kDequantGroups : kAStages;
-    // few tokens make a stage's MMAs short: a deeper weight ring keeps the stream in flight
-    static constexpr int kWStages = BN >= 128 ? 3 : 6;
+    // A weight stage comes from HBM (~1-2 us) and is used up by two activation stages: with
+    // three in flight the dequantisers of 128-token tiles waited ~0.6 us per stage for their
+    // weights.  Few tokens make a stage's MMAs short and need the deepest ring.  128-token
+    // tiles take what shared memory leaves beside the eight activation stages.
+    static constexpr int kWStages = BN >= 128 ? (ASYM ? 4 : 5) : 6;
     static constexpr uint32_t kSBytes = ASYM ? 2 * kRowsCta * (kWK / 32) * 4 : kSStageBytes;
     static constexpr uint32_t kZOff = kSBytes / 2;
     static constexpr uint32_t kOffX = 0;

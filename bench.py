@@ -303,30 +303,6 @@ def graph_steps(torch, timer, stream, fn, steps, warmup, tail=None):
     return ms / steps
 
 
-def call_steps(timer, fn, steps, warmup, tail=None):
-    """The same with plain back-to-back calls (no graph).  The hold kernel in front lasts
-    longer than the host takes to queue every call (measured on one extra untimed call), so
-    the device runs them back to back."""
-    torch = timer.torch
-    tail = tail or (lambda: None)
-    fn(0)   # first call: one-time set-up of the route stays out of the measured host time
-    tail()
-    timer.stream.synchronize()
-    t0 = time.perf_counter()
-    fn(0)
-    host_s = time.perf_counter() - t0
-    tail()
-    timer.stream.synchronize()
-    if timer.world > 1:   # every rank holds its stream equally long (ranks wait for each other)
-        t = torch.tensor([host_s], dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
-        timer.dist.all_reduce(t, op=timer.dist.ReduceOp.MAX)
-        host_s = float(t.item())
-    hold = int(min(4e6 + 2.0 * (steps + warmup) * host_s * 2.0e9, 4e8))
-    ms = timer.run(lambda: ([fn(i) for i in range(warmup)], tail()),
-                   lambda: ([fn(warmup + i) for i in range(steps)], tail()), hold_cycles=hold)
-    return ms / steps
-
-
 def check_device(_lib):
     code = _lib.device_error()
     if code:
@@ -574,7 +550,7 @@ def main():
                 h64.M, h64.x = 64, x64
                 h64.make_outputs(64)
                 reps = min(K, 50)
-                ms = call_steps(timer, h64.launch, reps, W, tail=h64.finish)
+                ms = graph_steps(torch, timer, stream, h64.launch, reps, W, tail=h64.finish)
                 check_device(_lib)
                 ck = h64.check(n_cols=512)
                 ck["pass"] = ck["finite"] and ck["max_abs_err_over_peak"] <= 1e-3
@@ -612,10 +588,7 @@ def main():
                         for p in projs:
                             p.finish()
                     reps = min(K, 50)
-                    if M <= 16:
-                        ms = graph_steps(torch, timer, stream, layer, reps, W, tail=layer_done)
-                    else:
-                        ms = call_steps(timer, layer, reps, W, tail=layer_done)
+                    ms = graph_steps(torch, timer, stream, layer, reps, W, tail=layer_done)
                     check_device(_lib)
                     checks = [p.check(n_cols=256) for p in projs]
                     tol = 1e-4 if M <= 16 else 1e-3
@@ -751,7 +724,7 @@ def single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind):
                     def pf(i, route=route):
                         wp, xp, op = sets[i % n_sets]
                         wp.matmul(xp, op, route=route, stream=stream)
-                    ms = call_steps(timer, pf, reps, W)
+                    ms = graph_steps(torch, timer, stream, pf, reps, W)
                     check_device(_lib)
                     tf = 2.0 * Mp * Np * Kp / (ms / 1e3) / 1e12
                     extras[key] = {
@@ -833,7 +806,7 @@ def single_gpu_lines(args, ctx, timer, extras, hbm_peak, tc_peak, peak_kind):
                                                     C.c_void_p(oa.data_ptr()), Mp, Kp, Np, 32, Gp, _lib.ROUTE_TC,
                                                     C.c_void_p(stream.cuda_stream)))
                 reps = max(K, 20)
-                ms = call_steps(timer, asym_call, reps, W)
+                ms = graph_steps(torch, timer, stream, asym_call, reps, W)
                 check_device(_lib)
                 tf = 2.0 * Mp * Np * Kp / (ms / 1e3) / 1e12
                 extras["q4_asym_prefill"] = {

@@ -541,7 +541,7 @@ template <int BN, int ACCB>
 __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem, uint64_t* d_full,
                                                  uint64_t* d_empty, volatile int* s_abort, int my_tiles, int pair,
                                                  int pairs, uint32_t rank, int quarter, int lane,
-                                                 uint32_t stage_smem = 0) {
+                                                 uint32_t stage_smem = 0, int max_slots = 0) {
     constexpr int kChunk = BN < 32 ? BN : 32;
     constexpr int kBlock = BN * 32;   // floats of one warp's partial sums (BN tokens x 32 features)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
@@ -569,31 +569,41 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
             break;
         }
         tc_fence_after();
-        // The last part sums the others' blocks in shared memory: the activation stages, free
-        // once this unit's MMAs completed (a tail unit is its pair's last), two blocks per warp.
-        // Every copy of a part goes out at once, one round trip per part.
-        const uint32_t sum_smem = stage_smem + static_cast<uint32_t>(quarter) * (2 * kBlock * 4);
+        // The last part sums the others' blocks in shared memory: the stage buffers, free once
+        // this unit's MMAs completed (a tail unit is its pair's last), `max_slots` blocks per
+        // warp.  Every block of a batch is fetched at once (one round trip per batch; one batch
+        // when the parts fit); a later batch first folds the slots into slot 0, in part order.
+        const uint32_t slot0 = stage_smem + static_cast<uint32_t>(quarter * max_slots) * (kBlock * 4);
+        int active = 0;   // slots holding parts still to add, slot 0 first
         if (tail && last) {
-            auto fetch = [&](int q, uint32_t dst) {
+            auto fetch = [&](int q, int slot) {
                 const float* src = part_at(q);
+                const uint32_t dst = slot0 + static_cast<uint32_t>(slot) * (kBlock * 4);
 #pragma unroll
                 for (int k = 0; k < kBlock / 4 / 32; ++k)
                     cp_async16(dst + (k * 32 + lane) * 16, src + (k * 32 + lane) * 4);
-                cp_async_commit();
             };
-            fetch(0, sum_smem);
-            if (p.split > 2) fetch(1, sum_smem + kBlock * 4);
-            for (int q = 1; q < p.split - 1; ++q) {
+            const int parts = p.split - 1;
+            int done = min(parts, max_slots);
+            for (int q = 0; q < done; ++q) fetch(q, q);
+            cp_async_commit();
+            active = done;
+            while (done < parts) {
                 cp_async_wait<0>();
                 __syncwarp();
-                // this lane's feature over all tokens: the sum so far plus part q, in part order
-#pragma unroll 8
+#pragma unroll 4
                 for (int tk = 0; tk < BN; ++tk) {
                     const uint32_t o = static_cast<uint32_t>(tk * 32 + lane) * 4;
-                    sts_f32(sum_smem + o, lds_f32(sum_smem + o) + lds_f32(sum_smem + kBlock * 4 + o));
+                    float sum = lds_f32(slot0 + o);
+                    for (int k = 1; k < active; ++k) sum += lds_f32(slot0 + k * (kBlock * 4) + o);
+                    sts_f32(slot0 + o, sum);
                 }
                 __syncwarp();
-                if (q + 1 < p.split - 1) fetch(q + 1, sum_smem + kBlock * 4);
+                const int nb = min(max_slots - 1, parts - done);
+                for (int k = 0; k < nb; ++k) fetch(done + k, 1 + k);
+                cp_async_commit();
+                done += nb;
+                active = 1 + nb;
             }
             cp_async_wait<0>();
             __syncwarp();
@@ -611,11 +621,14 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
                 for (int j = 0; j < kChunk; ++j) q[j * 32] = __uint_as_float(v[j]);
                 continue;
             }
-            if (tail)   // the other parts' sum, then this part's
+            if (tail)   // the other parts in part order, then this part's
 #pragma unroll
-                for (int j = 0; j < kChunk; ++j)
-                    v[j] = __float_as_uint(lds_f32(sum_smem + static_cast<uint32_t>((c0 + j) * 32 + lane) * 4) +
-                                           __uint_as_float(v[j]));
+                for (int j = 0; j < kChunk; ++j) {
+                    const uint32_t o = static_cast<uint32_t>((c0 + j) * 32 + lane) * 4;
+                    float sum = lds_f32(slot0 + o);
+                    for (int k = 1; k < active; ++k) sum += lds_f32(slot0 + k * (kBlock * 4) + o);
+                    v[j] = __float_as_uint(sum + __uint_as_float(v[j]));
+                }
             if (feat_ok) {
                 const int nt = min(kChunk, p.M - (tok0 + c0));
                 if (p.out_bf16) {
@@ -970,9 +983,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (!ok && grp < L::kGroups) *s_abort = 1;
     } else {
         // ---------------------------------------------------------------------- epilogue
-        static_assert(kStages * T::kXStageBytes >= 4 * 2 * BN * 32 * 4, "split-K sums: two blocks per warp");
+        // split-K sums: the activation, weight and scale stages (offsets 0 .. kOffBar), a
+        // quarter per epilogue warp, in blocks of BN tokens x 32 fp32 features
+        constexpr int kSlots = static_cast<int>(L::kOffBar / 4 / (BN * 32 * 4));
+        static_assert(kSlots >= 2, "split-K sums: two blocks per warp");
         epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_units, pair, pairs, rank, warp & 3,
-                                          lane, base + L::kOffX);
+                                          lane, base, kSlots);
     }
     tc_fence_before();
     __syncthreads();
@@ -1098,7 +1114,8 @@ static SplitPlan tc_split_plan(int64_t tiles, int max_pairs, int n_kw, int bn) {
     SplitPlan sp{static_cast<int>(tiles), 1, static_cast<int>(tiles), 0, 0};
     const int64_t full = (tiles / max_pairs) * max_pairs, tail = tiles - full;
     if (tail == 0) return sp;
-    const int split = static_cast<int>(std::min<int64_t>(std::min<int64_t>(max_pairs / tail, 8), n_kw));
+    // at most 8 parts of at least two weight stages each
+    const int split = static_cast<int>(std::min<int64_t>(std::min<int64_t>(max_pairs / tail, 8), n_kw / 2));
     if (split < 2) return sp;
     sp.full_tiles = static_cast<int>(full);
     sp.split = split;

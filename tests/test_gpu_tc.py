@@ -66,9 +66,9 @@ def test_tc_golden_cases(golden, oracle_mod):
                                    (513, 1024, 384), (1000, 2048, 77)])
 def test_tc_ragged_shapes_against_oracle(M, K, N, oracle_mod):
     """Partial token tiles and partial weight-row tiles.  With fewer tiles than half the CTA
-    pairs the GEMM cuts its last wave's tiles into 2 to 8 K-parts whose partial sums the last
-    part adds: every case here but the first two (one weight stage of K) takes that path, with
-    uneven parts at K = 768."""
+    pairs the GEMM cuts its last wave's tiles into 2 to 8 K-parts of at least two weight
+    stages, whose partial sums the last part adds: the cases with K >= 1024 take that path
+    (2 and 4 parts; uneven parts at K = 11008 in test_gpu_configs.py)."""
     O = oracle_mod
     p, s, xb, slot, sb = _case(O, M, K, N, seed=M + N)
     want = O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, M, K, N, threads=8)
@@ -135,6 +135,11 @@ def test_auto_route_prefill_is_tc(oracle_mod):
     assert gb.route_for(2, 2048, 4096, 4096) == _lib.ROUTE_TC
     assert gb.route_for(2, 64, 4096, 128256) == _lib.ROUTE_TC
     assert gb.route_for(2, 16, 4096, 4096) == _lib.ROUTE_GEMV
+    assert gb.route_for(2, 3, 11008, 4096) == _lib.ROUTE_GEMV                 # few rows
+    assert gb.route_for(2, 4, 11008, 4096) == _lib.ROUTE_TC                   # long rows
+    assert gb.route_for(2, 11, 4096, 128256) == _lib.ROUTE_GEMV
+    assert gb.route_for(2, 12, 4096, 128256) == _lib.ROUTE_TC                 # very wide output
+    assert gb.route_for(2, 16, 11008, 4096, _lib.DT_F32) == _lib.ROUTE_GEMV   # fp32 rows stay exact
     assert gb.route_for(2, 32, 4096, 4096) == _lib.ROUTE_TC                  # bf16 rows
     assert gb.route_for(2, 32, 4096, 4096, _lib.DT_F32) == _lib.ROUTE_GEMV   # fp32 rows stay exact
     assert gb.route_for(2, 33, 4096, 4096, _lib.DT_F32) == _lib.ROUTE_TC

@@ -220,7 +220,9 @@ int bybycu_init(int device) {
     if (d.cc_major != 10)
         return set_error(BYBYCU_ERR_NODEV, "device %d is sm_%d%d; this library is built for sm_100a", device, d.cc_major,
                          d.cc_minor);
-    // the static-scratch route allocates nothing after this: its module memory is loaded now
+    // the static-scratch route allocates nothing after this: its module memory is loaded now;
+    // the tensor-core routes' scratch pool and launch attributes are set up too, so that a
+    // first call may be captured into a CUDA graph
     return tc_static_scratch_load();
 }
 

@@ -98,11 +98,9 @@ struct Cfg {
     // Dequantiser groups at work: at most one per A stage in flight, so that no group waits
     // for a slot phase two rounds ahead (a phase-parity wait cannot tell those apart).
     static constexpr int kGroups = kDequantGroups < kAStages ? kDequantGroups : kAStages;
-    // A weight stage comes from HBM (~1-2 us) and is used up by two activation stages: with
-    // three in flight the dequantisers of 128-token tiles waited ~0.6 us per stage for their
-    // weights.  Few tokens make a stage's MMAs short and need the deepest ring.  128-token
-    // tiles take what shared memory leaves beside the eight activation stages.
-    static constexpr int kWStages = BN >= 128 ? (ASYM ? 4 : 5) : 6;
+    // few tokens make a stage's MMAs short: a deeper weight ring keeps the stream in flight
+    // (five stages at 128 tokens measured 3-7% slower than three)
+    static constexpr int kWStages = BN >= 128 ? 3 : 6;
     static constexpr uint32_t kSBytes = ASYM ? 2 * kRowsCta * (kWK / 32) * 4 : kSStageBytes;
     static constexpr uint32_t kZOff = kSBytes / 2;
     static constexpr uint32_t kOffX = 0;
@@ -1346,6 +1344,18 @@ int tc_static_scratch_load() {
     if (int rc = tc_setup<false, true, 32>(&d, &max_pairs)) return rc;
     if (int rc = tc_setup<false, true, 64>(&d, &max_pairs)) return rc;
     if (int rc = tc_setup<false, true, 128>(&d, &max_pairs)) return rc;
+    // the pooled routes too, so that a first call may come inside a stream capture: the
+    // scratch pool and every instantiation's attributes exist before it
+    cudaMemPool_t pool = nullptr;
+    if (int rc = scratch_pool(info.device, &pool)) return rc;
+    if (int rc = tc_setup<false, false, 16>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<false, false, 32>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<false, false, 64>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<false, false, 128>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<true, false, 16>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<true, false, 32>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<true, false, 64>(&d, &max_pairs)) return rc;
+    if (int rc = tc_setup<true, false, 128>(&d, &max_pairs)) return rc;
     cudaFuncAttributes fa;
     BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<false, tc::kPermQ4B32>));
     BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<true, tc::kPermQ4B32>));

@@ -981,10 +981,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (!ok && grp < L::kGroups) *s_abort = 1;
     } else {
         // ---------------------------------------------------------------------- epilogue
-        // split-K sums: the activation, weight and scale stages (offsets 0 .. kOffBar), a
-        // quarter per epilogue warp, in blocks of BN tokens x 32 fp32 features
-        constexpr int kSlots = static_cast<int>(L::kOffBar / 4 / (BN * 32 * 4));
-        static_assert(kSlots >= 2, "split-K sums: two blocks per warp");
+        // split-K sums: two blocks of BN tokens x 32 fp32 features per epilogue warp in the
+        // stage buffers (offsets 0 .. kOffBar).  Fetching every part at once into more slots
+        // measured slower (16 and 64 tokens: 16.5 against 14.9 us, 22.5 against 18.8 us at
+        // 4096 x 4096) than two slots and a fold between batches.
+        constexpr int kSlots = 2;
+        static_assert(4 * kSlots * BN * 32 * 4 <= L::kOffBar, "split-K sums: two blocks per warp");
         epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_units, pair, pairs, rank, warp & 3,
                                           lane, base, kSlots);
     }

@@ -51,6 +51,9 @@ namespace {
 #endif
 constexpr int kConsumerWarps = BYBYCU_GEMV_WARPS;   // 8 or 16
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
+// With 8 consumer warps two CTAs of the M >= 2 kernel fit an SM (registers), so that a
+// one-pass launch's CTAs stream beside the previous launch's, as the M = 1 kernel's do.
+constexpr int kMinCtas = kConsumerWarps <= 8 ? 2 : 1;
 constexpr int kTileRows = 16;
 constexpr int kRedSlots = 4;                        // partial-sum slots of the cross-warp reduction
 constexpr uint32_t kMagicA = 0x43084308u;           // bf16 128 | (nibble ^ 8) via lop3
@@ -307,7 +310,7 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
 }
 
 template <int TP, int NT, bool XF32, bool STMA>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kMinCtas)
 gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
     constexpr int H = XF32 ? 2 : 1;   // bf16 terms per activation
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1255,12 +1258,11 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     // flight (1 x 32000 x 4096: 16.1 us against 17.9).
     // A tuned plan's depth (a.stages), then BYBY_CUDA_GEMV_STAGES, override.
     const int fit = stages;   // the most that fit in shared memory (and are useful)
-    if (m1) {
-        const size_t half_sm = static_cast<size_t>(dev.smem_per_sm) / 2 - 1024;   // per CTA, two per SM
-        const size_t fixed = 1024 + 16 + red_bytes + x_all;
-        const int two_cta = half_sm > fixed ? static_cast<int>((half_sm - fixed) / (stage_bytes + 16)) : 0;
-        stages = std::min(fit, tiles_max > tp ? 3 : std::max(2, two_cta));
-    }
+    const size_t half_sm = static_cast<size_t>(dev.smem_per_sm) / 2 - 1024;   // per CTA, two per SM
+    const size_t fixed = 1024 + 16 + red_bytes + x_all;
+    const int two_cta = half_sm > fixed ? static_cast<int>((half_sm - fixed) / (stage_bytes + 16)) : 0;
+    if (m1) stages = std::min(fit, tiles_max > tp ? 3 : std::max(2, two_cta));
+    else if (kMinCtas == 2 && tiles_max <= tp) stages = std::min(fit, std::max(2, two_cta));
     if (a.stages >= 1) stages = std::min(fit, a.stages);
     if (const char* e = getenv("BYBY_CUDA_GEMV_STAGES")) {
         const int want_stages = atoi(e);

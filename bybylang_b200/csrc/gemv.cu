@@ -46,14 +46,11 @@ namespace bybycu {
 
 namespace {
 
-#ifndef BYBYCU_GEMV_WARPS
-#define BYBYCU_GEMV_WARPS 16
-#endif
-constexpr int kConsumerWarps = BYBYCU_GEMV_WARPS;   // 8 or 16
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-// With 8 consumer warps two CTAs of the M >= 2 kernel fit an SM (registers), so that a
-// one-pass launch's CTAs stream beside the previous launch's, as the M = 1 kernel's do.
-constexpr int kMinCtas = kConsumerWarps <= 8 ? 2 : 1;
+// Consumer warps of the M >= 2 kernel: 16, one CTA per SM, where a CTA makes several passes
+// over its rows; 8 where it makes one, so that two CTAs fit an SM (registers) and a launch's
+// CTAs stream beside the previous launch's, as the M = 1 kernel's do (4096 x 4096 at M = 2:
+// 7.0 against 9.3 us; the 128256-row head at M = 4, several passes: 93 against 105 us).
+constexpr int kWarpsMany = 16, kWarpsOnePass = 8;
 constexpr int kTileRows = 16;
 constexpr int kRedSlots = 4;                        // partial-sum slots of the cross-warp reduction
 constexpr uint32_t kMagicA = 0x43084308u;           // bf16 128 | (nibble ^ 8) via lop3
@@ -309,8 +306,8 @@ __device__ __forceinline__ void gemv_producer(const GemvMaps& maps, const GemvPa
     }
 }
 
-template <int TP, int NT, bool XF32, bool STMA>
-__global__ void __launch_bounds__(kThreads, kMinCtas)
+template <int TP, int NT, bool XF32, bool STMA, int W>
+__global__ void __launch_bounds__((W + 1) * 32, W <= 8 ? 2 : 1)
 gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
     constexpr int H = XF32 ? 2 : 1;   // bf16 terms per activation
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -336,14 +333,14 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], kConsumerWarps);
+            mbar_init(&empty_bar[s], W);
         }
         *s_abort = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == kConsumerWarps) {
+    if (warp == W) {
         gemv_producer(maps, p, smem, full_bar, empty_bar, s_abort, lane, tile_begin, my_tiles, total_it);
         return;
     }
@@ -360,7 +357,7 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
             for (int v = 0; v < 4; ++v) acc[i][j][v] = 0.0f;
     const uint32_t ones[4] = {kOnesBf16x2, kOnesBf16x2, kOnesBf16x2, kOnesBf16x2};
     const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
-    const int qblocks = p.kc / (32 * kConsumerWarps);   // blocks of this warp per chunk: warp, warp + W, ...
+    const int qblocks = p.kc / (32 * W);   // blocks of this warp per chunk: warp, warp + W, ...
 
     int s = 0, round = 0, chunk = 0, t0 = tile_begin;
     for (int it = 0; it < total_it; ++it) {
@@ -372,7 +369,7 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
         }
         const uint32_t st = base + static_cast<uint32_t>(s) * p.stage_bytes;
         for (int qb = 0; qb < qblocks; ++qb) {
-            const int cb = warp + kConsumerWarps * qb;   // block within the chunk
+            const int cb = warp + W * qb;   // block within the chunk
             const int c = chunk * (p.kc / 32) + cb;  // block within the row
             if (!ok || c >= p.G) break;
             // ---- activation fragments of block c (B operands); the offset term 136 * sum(x)
@@ -472,14 +469,14 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
             constexpr int E = TP * NT * 128;
             const uint32_t slot = red + static_cast<uint32_t>((warp & 3) * E * 4);
 #pragma unroll
-            for (int phase = kConsumerWarps / 4 - 1; phase >= 0; --phase) {
+            for (int phase = W / 4 - 1; phase >= 0; --phase) {
                 if ((warp >> 2) == phase) {
 #pragma unroll
                     for (int i = 0; i < TP; ++i)
 #pragma unroll
                         for (int j = 0; j < NT; ++j) {
                             const uint32_t a = slot + ((i * NT + j) * 32 + lane) * 16;
-                            if (phase == kConsumerWarps / 4 - 1) {
+                            if (phase == W / 4 - 1) {
                                 sts_v4(a, acc[i][j][0], acc[i][j][1], acc[i][j][2], acc[i][j][3]);
                             } else {
                                 const float4 o = lds_v4f(a);
@@ -488,7 +485,7 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
                             }
                         }
                 }
-                named_barrier(1, kConsumerWarps * 32);
+                named_barrier(1, W * 32);
             }
 #pragma unroll
             for (int i = 0; i < TP; ++i)
@@ -497,7 +494,7 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
 #pragma unroll
                     for (int v = 0; v < 4; ++v) acc[i][j][v] = 0.0f;
             const int entries = nt * NT * 128;
-            for (int e = threadIdx.x; e < entries; e += kConsumerWarps * 32) {
+            for (int e = threadIdx.x; e < entries; e += W * 32) {
                 float sum = 0.0f;
 #pragma unroll
                 for (int w = 0; w < kRedSlots; ++w) sum += lds_f32(red + static_cast<uint32_t>((w * E + e) * 4));
@@ -513,11 +510,11 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
                     if (p.pg.world > 1) store_to_peers(p.pg, oi, sum);
                 }
             }
-            named_barrier(1, kConsumerWarps * 32);
+            named_barrier(1, W * 32);
         }
         if (++chunk == p.n_chunks) { chunk = 0; t0 += p.tp; }
     }
-    gemv_gather_end(p.pg, kConsumerWarps * 32);
+    gemv_gather_end(p.pg, W * 32);
 }
 
 
@@ -1017,9 +1014,9 @@ bool pdl_enabled() {
     return on != 0;
 }
 
-template <int TP, int NT, bool XF32, bool STMA>
+template <int TP, int NT, bool XF32, bool STMA, int W>
 int launch_t(const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, cudaStream_t stream) {
-    auto kern = gemv_q4b32_kernel<TP, NT, XF32, STMA>;
+    auto kern = gemv_q4b32_kernel<TP, NT, XF32, STMA, W>;
     static uint64_t configured = 0;   // per device: the opt-in smem limit is a function attribute
     int dev = 0;
     BYBYCU_CUDA_TRY(cudaGetDevice(&dev));
@@ -1029,7 +1026,7 @@ int launch_t(const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, c
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3((W + 1) * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -1082,11 +1079,19 @@ int launch_m1(int mode, bool xf32, const GemvMaps& maps, const GemvParams& p, in
     return BYBYCU_OK;
 }
 
-template <int TP, int NT>
-int dispatch_x(bool xf32, const GemvMaps& m, const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
+template <int TP, int NT, int W>
+int dispatch_xw(bool xf32, const GemvMaps& m, const GemvParams& p, int grid, size_t smem, cudaStream_t st) {
     if (p.scale_tma)
-        return xf32 ? launch_t<TP, NT, true, true>(m, p, grid, smem, st) : launch_t<TP, NT, false, true>(m, p, grid, smem, st);
-    return xf32 ? launch_t<TP, NT, true, false>(m, p, grid, smem, st) : launch_t<TP, NT, false, false>(m, p, grid, smem, st);
+        return xf32 ? launch_t<TP, NT, true, true, W>(m, p, grid, smem, st)
+                    : launch_t<TP, NT, false, true, W>(m, p, grid, smem, st);
+    return xf32 ? launch_t<TP, NT, true, false, W>(m, p, grid, smem, st)
+                : launch_t<TP, NT, false, false, W>(m, p, grid, smem, st);
+}
+template <int TP, int NT>
+int dispatch_x(bool xf32, bool one_pass, const GemvMaps& m, const GemvParams& p, int grid, size_t smem,
+               cudaStream_t st) {
+    return one_pass ? dispatch_xw<TP, NT, kWarpsOnePass>(xf32, m, p, grid, smem, st)
+                    : dispatch_xw<TP, NT, kWarpsMany>(xf32, m, p, grid, smem, st);
 }
 
 size_t round1k(size_t v) { return (v + 1023) / 1024 * 1024; }
@@ -1262,7 +1267,9 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     const size_t fixed = 1024 + 16 + red_bytes + x_all;
     const int two_cta = half_sm > fixed ? static_cast<int>((half_sm - fixed) / (stage_bytes + 16)) : 0;
     if (m1) stages = std::min(fit, tiles_max > tp ? 3 : std::max(2, two_cta));
-    else if (kMinCtas == 2 && tiles_max <= tp) stages = std::min(fit, std::max(2, two_cta));
+    // M >= 2, one pass per CTA: the 8-warp kernel, two CTAs per SM (as many stages as fit)
+    const bool one_pass = !m1 && tiles_max <= tp;
+    if (one_pass) stages = std::min(fit, std::max(2, two_cta));
     if (a.stages >= 1) stages = std::min(fit, a.stages);
     if (const char* e = getenv("BYBY_CUDA_GEMV_STAGES")) {
         const int want_stages = atoi(e);
@@ -1322,12 +1329,13 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
                         : launch_m1<7, false>(mode, xf32, maps, p, grid, smem, st);
     }
     if (ntn == 2) {
-        return tpl == 2 ? dispatch_x<2, 2>(xf32, maps, p, grid, smem, st) : dispatch_x<5, 2>(xf32, maps, p, grid, smem, st);
+        return tpl == 2 ? dispatch_x<2, 2>(xf32, one_pass, maps, p, grid, smem, st)
+                        : dispatch_x<5, 2>(xf32, one_pass, maps, p, grid, smem, st);
     }
     switch (tpl) {
-        case 2: return dispatch_x<2, 1>(xf32, maps, p, grid, smem, st);
-        case 5: return dispatch_x<5, 1>(xf32, maps, p, grid, smem, st);
-        default: return dispatch_x<8, 1>(xf32, maps, p, grid, smem, st);
+        case 2: return dispatch_x<2, 1>(xf32, one_pass, maps, p, grid, smem, st);
+        case 5: return dispatch_x<5, 1>(xf32, one_pass, maps, p, grid, smem, st);
+        default: return dispatch_x<8, 1>(xf32, one_pass, maps, p, grid, smem, st);
     }
 }
 

@@ -136,6 +136,8 @@ int launch_tc_f16(const GemmArgs& a);
 int launch_tc_static_scratch(const GemmArgs& a);
 // Loads that route's module array and kernels on the current device (bybycu_init).
 int tc_static_scratch_load();
+// Whether a sharded tensor-core call (route TC, Q4B32) stores to the peers from its epilogue.
+bool tc_fuse_gather(const GemmArgs& a);
 // The asymmetric-Q4 form of the tensor-core route (matmul_q4 prefill): fp32 x [M, K],
 // interleaved nibbles [N, K/2], fp32 scales and zero points [N, K/32], fp32 out [M, N].
 bool tc_asym_supports(int M, int K, int N, int group, int n_groups, const void* x, const void* wq, const void* scales,

@@ -249,7 +249,7 @@ static int tile_gemm_allgather(int fmt, int M, int K, int N, int n0, int n1, con
             // (in split phase its producer first waits for the ranks' previous launch)
             if (int rc = launch_gemv(a, &pg)) return rc;
             fused = true;
-        } else if (route == BYBYCU_ROUTE_TC && fmt == BYBYCU_FMT_Q4B32) {
+        } else if (route == BYBYCU_ROUTE_TC && fmt == BYBYCU_FMT_Q4B32 && tc_fuse_gather(a)) {
             // the tensor-core GEMM's epilogue does the same, tile by tile, so the transfer
             // overlaps the MMAs of the pair's next tiles
             a.pg = &pg;

@@ -22,9 +22,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-# GEMV (fused gather) at M = 1, 4, 16; tensor-core GEMM (gather fused into its epilogue) at
-# M = 64 over ragged 256-row tiles and at M = 300 over three token tiles
-CASES = [(1, 4096, 11008), (4, 4096, 1000), (16, 2048, 4160), (64, 4096, 4160), (300, 1024, 512)]
+# GEMV (fused gather) at M = 1, 4, 16; tensor-core GEMM with one round of tiles (the copy
+# kernel gathers) at M = 64 over ragged 256-row tiles and at M = 300 over three token tiles;
+# tensor-core GEMM with more tiles than CTA pairs (the gather fused into its epilogue)
+CASES = [(1, 4096, 11008), (4, 4096, 1000), (16, 2048, 4160), (64, 4096, 4160), (300, 1024, 512),
+         (128, 1024, 40960)]
 
 
 def _worker(rank, world, port, q):

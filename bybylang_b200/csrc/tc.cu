@@ -1337,12 +1337,15 @@ static int static_scratch(void** ptr) {
 
 // Loads, on the current device, the module's array and every kernel the static-scratch route
 // launches, and sets the GEMM's attributes: the allocations of lazy loading happen here.
-// Whether the sharded call stores to the peers from the GEMM's own epilogue: only when some
-// CTA pair has a second tile, so that the peer stores of one tile overlap the MMAs of the
-// next.  With one round of tiles every peer store sits in the launch's tail on the few SMs
-// that finish tiles (2048 x 4096 at M = 128 over two GPUs: 48.5 us fused against 29.1 us
-// for the GEMM alone); the copy kernel spreads them over every SM instead.
+// Whether the sharded call stores to the peers from the GEMM's own epilogue: when some CTA
+// pair has a second tile, so that the peer stores of one tile overlap the MMAs of the next,
+// or when tiles are small (at most 32 tokens: 32 KB per tile to each peer).  With one round
+// of large tiles every peer store sits in the launch's tail on the few SMs that finish tiles
+// (2048 x 4096 at M = 128 over two GPUs: 48.5 us fused, 32.9 us with the copy kernel, which
+// spreads the stores over every SM); at M = 16 the fused form wins (2048 x 11008: 22.9
+// against 26.2 us).
 bool tc_fuse_gather(const GemmArgs& a) {
+    if (a.M <= 32) return true;
     DeviceInfo info;
     int max_pairs = 0;
     int rc = 0;

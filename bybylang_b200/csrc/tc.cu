@@ -582,20 +582,6 @@ __device__ __forceinline__ bool convert_x_stage(uint32_t stage, int et) {
     return range_ok;
 }
 
-// Non-blocking test of a phase (mbarrier.try_wait may suspend the thread for a while first,
-// which a poll that has other work to do cannot afford).
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
 // The epilogue's wait for an accumulator buffer: a bounded wait, or (WaitD) a callable that
 // does other work while it waits.
 struct PlainWait {
@@ -1078,14 +1064,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             auto wait_d = [&](uint64_t* bar, uint32_t parity) -> bool {
                 uint64_t t0 = globaltimer_ns();
                 for (;;) {
-                    if (__all_sync(0xffffffffu, mbar_test_wait(bar, parity))) return true;
+                    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
                     if (*s_abort) return false;
-                    // nothing left to convert: the plain wait, which leaves the issue slots to
-                    // the dequantisers
-                    if (conv >= total) return PlainWait()(bar, parity);
-                    // the next stage: a short sleep in the barrier unit rather than a spin
-                    if (__all_sync(0xffffffffu,
-                                   mbar_try_wait_hint(&raw_full[conv % kStages], (conv / kStages) & 1, 256u))) {
+                    if (conv < total &&
+                        __all_sync(0xffffffffu, mbar_try_wait(&raw_full[conv % kStages], (conv / kStages) & 1))) {
                         const uint32_t st = base + L::kOffX + static_cast<uint32_t>(conv % kStages) * T::kXStageBytes;
                         if (!convert_x_stage<BN>(st, et)) record_device_error(kDevErrActRange);
                         // the MMAs read the stage through the async proxy

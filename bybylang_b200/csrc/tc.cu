@@ -107,8 +107,8 @@ struct Cfg {
     static constexpr uint32_t kOffW = kOffX + kStages * T::kXStageBytes;
     static constexpr uint32_t kOffS = kOffW + kWStages * kWStageBytes;
     // barriers: full, x_empty [kStages]; a_empty [kAStages]; w_full, w_empty [kWStages];
-    // d_full, d_empty [2]; done; raw_full [kStages] (bf16 activations converted in the kernel)
-    static constexpr uint32_t kNumBars = 3 * kStages + kAStages + 2 * kWStages + 5;
+    // d_full, d_empty [2]; done
+    static constexpr uint32_t kNumBars = 2 * kStages + kAStages + 2 * kWStages + 5;
     static constexpr uint32_t kOffBar = kOffS + kWStages * kSBytes;
     static constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
@@ -535,67 +535,11 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x
 // tiles of BN tokens back from tensor memory (tcgen05.ld, 32 or 16 columns at a time) and out
 // to out[token][feature]; each warp owns the TMEM lane quarter `quarter` (32 features) and
 // frees the buffer on rank 0 when done.
-__device__ __forceinline__ void sts_u128(uint32_t addr, uint4 v) {
-    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                 : "memory");
-}
-
-// The staging pass's work for bf16 activations, done inside the GEMM: one activation stage
-// of this CTA (two 64-value sub-boxes of kTokCta token rows, as TMA loaded them from x with
-// the 128-byte swizzle) converted in place to fp16 in the dequantisers' K order.  Each
-// 32-value block keeps its four 16-byte chunks (their swizzled positions), so the permutation
-// stays inside a thread.  Thread et of the four epilogue warps takes blocks et, et + 128, ...
-// Returns false when a value has no fp16 image (|x| >= 65520).
-template <int BN>
-__device__ __forceinline__ bool convert_x_stage(uint32_t stage, int et) {
-    using T = TokTile<BN>;
-    constexpr int kRowsSub = T::kTokCta;
-    constexpr int kBlocks = 2 * kRowsSub * 2;   // two sub-boxes, two blocks per 128-byte row
-    bool range_ok = true;
-    for (int b = et; b < kBlocks; b += 128) {
-        const int sub = b / (2 * kRowsSub), rem = b % (2 * kRowsSub);
-        const int tok = rem >> 1, hb = rem & 1;
-        const uint32_t row = stage + static_cast<uint32_t>(sub) * T::kXSubBytes + static_cast<uint32_t>(tok) * 128u;
-        uint32_t addr[4];
-        float v[32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            addr[c] = row + ((static_cast<uint32_t>(4 * hb + c) ^ static_cast<uint32_t>(tok & 7)) << 4);
-            const uint4 q = lds_u128(addr[c]);
-            const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                v[8 * c + 2 * e] = __uint_as_float(wv[e] << 16);
-                v[8 * c + 2 * e + 1] = __uint_as_float(wv[e] & 0xFFFF0000u);
-            }
-        }
-        uint32_t o[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-            const float a = v[perm_of(kPermQ4B32, 2 * c)], bb = v[perm_of(kPermQ4B32, 2 * c + 1)];
-            range_ok &= fabsf(a) < 65520.0f && fabsf(bb) < 65520.0f;
-            o[c] = h2_bits(__floats2half2_rn(a, bb));
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) sts_u128(addr[c], make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
-    }
-    return range_ok;
-}
-
-// The epilogue's wait for an accumulator buffer: a bounded wait, or (WaitD) a callable that
-// does other work while it waits.
-struct PlainWait {
-    __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity) const {
-        return __all_sync(0xffffffffu, wait_bar(bar, parity, kDevErrMmaWait));
-    }
-};
-
-template <int BN, int ACCB, class WaitD = PlainWait>
+template <int BN, int ACCB>
 __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem, uint64_t* d_full,
                                                  uint64_t* d_empty, volatile int* s_abort, int my_tiles, int pair,
                                                  int pairs, uint32_t rank, int quarter, int lane,
-                                                 uint32_t stage_smem = 0, int max_slots = 0,
-                                                 WaitD wait_d = WaitD()) {
+                                                 uint32_t stage_smem = 0, int max_slots = 0) {
     constexpr int kChunk = BN < 32 ? BN : 32;
     constexpr int kBlock = BN * 32;   // floats of one warp's partial sums (BN tokens x 32 features)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
@@ -615,7 +559,7 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
             return p.partial + ((static_cast<int64_t>(tix * (p.split - 1) + q) * 2 + rank) * 4 + quarter) * kBlock;
         };
         uint32_t* flag = tail ? p.flags + (tix * 2 + rank) * 4 + quarter : nullptr;
-        bool ok = wait_d(&d_full[b], static_cast<uint32_t>(u & 1));
+        bool ok = __all_sync(0xffffffffu, wait_bar(&d_full[b], u & 1, kDevErrMmaWait));
         if (ok && tail && last)   // the other parts of this tile stored their sums
             ok = __all_sync(0xffffffffu, wait_flag(flag, static_cast<uint32_t>(p.split - 1)));
         if (!ok) {
@@ -726,12 +670,9 @@ __device__ __forceinline__ void epilogue_tiles(const Params& p, uint32_t tmem, u
 // ---------------------------------------------------------------------------------------
 // EXACT (Q4B32 only): the weights enter as the two exact fp16 terms of dequant_word_exact, in
 // a pair of A slots per stage, sixteen MMAs per stage.  BN: tokens per pair tile (Cfg).
-// FX: x is bf16 and TMA-loaded as it is; the epilogue warps convert each activation stage to
-// fp16 in place (convert_x_stage) while they wait for accumulators, instead of a staging pass.
-template <bool ASYM, bool EXACT, int BN, bool FX>
+template <bool ASYM, bool EXACT, int BN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
     static_assert(!(ASYM && EXACT), "the exact weight split is for Q4B32");
-    static_assert(!(ASYM && FX), "in-kernel conversion is for Q4B32 (bf16 activations)");
     using L = Cfg<ASYM, EXACT, BN>;
     using T = TokTile<BN>;
     constexpr int kAStages = L::kAStages;   // A stages in flight (a slot, or a slot pair when EXACT)
@@ -751,7 +692,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     uint64_t* d_full = w_empty + kWSt;           // [2] accumulator buffer complete
     uint64_t* d_empty = d_full + 2;              // [2] (rank 0) both epilogues read it
     uint64_t* done_bar = d_full + 4;
-    uint64_t* raw_full = done_bar + 1;           // FX: [kStages] the stage's bf16 landed (TMA)
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::kOffTmemSlot);
     volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
 
@@ -760,10 +700,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
-            // FX: the four epilogue warps' conversions stand in for the TMA arrival
-            mbar_init(&full[i], FX ? (leader ? kFullArrivals - 1 + 4 : 4) : (leader ? kFullArrivals : 1));
+            mbar_init(&full[i], leader ? kFullArrivals : 1);
             mbar_init(&x_empty[i], 1);
-            if (FX) mbar_init(&raw_full[i], 1);
         }
         for (int i = 0; i < kAStages; ++i) mbar_init(&a_empty[i], 1);
         for (int i = 0; i < kWSt; ++i) {
@@ -808,11 +746,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         break;
                     }
                     if (*s_abort) break;
-                    uint64_t* landed = FX ? &raw_full[s] : &full[s];
-                    mbar_arrive_expect_tx(landed, T::kXStageBytes);
+                    mbar_arrive_expect_tx(&full[s], T::kXStageBytes);
                     uint8_t* dst = smem + L::kOffX + s * T::kXStageBytes;
-                    tma_load_2d(dst, &maps.x, landed, ks * kXK, tok);
-                    tma_load_2d(dst + T::kXSubBytes, &maps.x, landed, ks * kXK + kXSub, tok);
+                    tma_load_2d(dst, &maps.x, &full[s], ks * kXK, tok);
+                    tma_load_2d(dst + T::kXSubBytes, &maps.x, &full[s], ks * kXK + kXSub, tok);
                     ++issued;
                 }
             }
@@ -1050,46 +987,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // 4096 x 4096) than two slots and a fold between batches.
         constexpr int kSlots = 2;
         static_assert(4 * kSlots * BN * 32 * 4 <= L::kOffBar, "split-K sums: two blocks per warp");
-        if constexpr (FX) {
-            // convert activation stages, in order, whenever one has landed while waiting for an
-            // accumulator buffer; every stage a unit's MMAs need is converted before that
-            // unit's buffer can complete
-            int total = 0;
-            for (int t = 0; t < my_units; ++t) {
-                const WorkUnit w = work_unit(p, pair + t * pairs, n_kw);
-                total += (w.kw1 - w.kw0) * kSubs;
-            }
-            int conv = 0;
-            const int et = threadIdx.x - kEpilogueWarp0 * 32;
-            auto wait_d = [&](uint64_t* bar, uint32_t parity) -> bool {
-                uint64_t t0 = globaltimer_ns();
-                for (;;) {
-                    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-                    if (*s_abort) return false;
-                    if (conv < total &&
-                        __all_sync(0xffffffffu, mbar_try_wait(&raw_full[conv % kStages], (conv / kStages) & 1))) {
-                        const uint32_t st = base + L::kOffX + static_cast<uint32_t>(conv % kStages) * T::kXStageBytes;
-                        if (!convert_x_stage<BN>(st, et)) record_device_error(kDevErrActRange);
-                        // the MMAs read the stage through the async proxy
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&full[conv % kStages]);
-                        ++conv;
-                        t0 = globaltimer_ns();
-                        continue;
-                    }
-                    if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                        record_device_error(kDevErrMmaWait);
-                        return false;
-                    }
-                }
-            };
-            epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_units, pair, pairs, rank,
-                                              warp & 3, lane, base, kSlots, wait_d);
-        } else {
-            epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_units, pair, pairs, rank,
-                                              warp & 3, lane, base, kSlots);
-        }
+        epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_units, pair, pairs, rank, warp & 3,
+                                          lane, base, kSlots);
     }
     tc_fence_before();
     __syncthreads();
@@ -1153,7 +1052,7 @@ static int tc_token_tile(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ?
 
 // Device info, the kernel attribute and the number of CTA pairs that fit at once, per kernel
 // instantiation and device.
-template <bool ASYM, bool EXACT, int BN, bool FX = false>
+template <bool ASYM, bool EXACT, int BN>
 static int tc_setup(DeviceInfo* info, int* max_pairs) {
     if (int rc = current_device_info(info)) return rc;
     static std::once_flag once[64];
@@ -1163,7 +1062,7 @@ static int tc_setup(DeviceInfo* info, int* max_pairs) {
     if (dev < 0 || dev >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", dev);
     constexpr uint32_t smem = tc::Cfg<ASYM, EXACT, BN>::kSmemBytes;
     std::call_once(once[dev], [&] {
-        prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel<ASYM, EXACT, BN, FX>,
+        prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_kernel<ASYM, EXACT, BN>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (prep_rc[dev] != cudaSuccess) return;
         cudaLaunchConfig_t cfg = {};
@@ -1177,7 +1076,7 @@ static int tc_setup(DeviceInfo* info, int* max_pairs) {
         cfg.dynamicSmemBytes = smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        prep_rc[dev] = cudaOccupancyMaxActiveClusters(&pairs[dev], tc::gemm_kernel<ASYM, EXACT, BN, FX>, &cfg);
+        prep_rc[dev] = cudaOccupancyMaxActiveClusters(&pairs[dev], tc::gemm_kernel<ASYM, EXACT, BN>, &cfg);
     });
     if (prep_rc[dev] != cudaSuccess) return cuda_fail(prep_rc[dev], "tensor-core GEMM set-up");
     if (pairs[dev] < 1) return set_error(BYBYCU_ERR_DEVICE, "no CTA pair of the tensor-core GEMM fits on the device");
@@ -1231,9 +1130,7 @@ static SplitPlan tc_split_plan(int64_t tiles, int max_pairs, int n_kw, int bn) {
 
 // The staging pass and the GEMM with BN-token tiles over the work units of `sp`, with `xp`
 // (M * K fp16) as the staging buffer and `partial` / `flags` as the split-K scratch.
-// FX: the GEMM reads bf16 x itself and converts it (no staging pass; xp is unused and the
-// split-K counters are cleared by a memset instead).
-template <bool ASYM, bool EXACT, int BN, bool FX>
+template <bool ASYM, bool EXACT, int BN>
 static int tc_launch(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitPlan& sp, float* partial,
                      uint32_t* flags, int max_pairs, int tiles_n, int64_t tiles) {
     const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
@@ -1241,27 +1138,20 @@ static int tc_launch(const GemmArgs& a, const TcWeights& wt, void* xp, const Spl
     constexpr int perm = ASYM ? tc::kPermAsym : tc::kPermQ4B32;
     const PeerGather pg = a.pg ? *a.pg : PeerGather();
     const int n_flags = static_cast<int>(sp.flags);
-    if (FX) {
-        if (n_flags) BYBYCU_CUDA_TRY(cudaMemsetAsync(flags, 0, static_cast<size_t>(n_flags) * 4, a.stream));
-    } else {
-        if (a.x_dtype == BYBYCU_DT_F32)
-            tc::stage_x_kernel<true, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg,
-                                                                         flags, n_flags);
-        else
-            tc::stage_x_kernel<false, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg,
-                                                                          flags, n_flags);
-        BYBYCU_LAUNCH_CHECK("stage_x_kernel");
-    }
+    if (a.x_dtype == BYBYCU_DT_F32)
+        tc::stage_x_kernel<true, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg, flags,
+                                                                     n_flags);
+    else
+        tc::stage_x_kernel<false, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg,
+                                                                      flags, n_flags);
+    BYBYCU_LAUNCH_CHECK("stage_x_kernel");
 
     tc::Maps maps;
     memset(&maps, 0, sizeof maps);
     const uint64_t G = static_cast<uint64_t>(a.K / 32);
-    int rc = FX ? encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, a.K, a.M,
-                                       static_cast<uint64_t>(a.K) * 2, tc::kXSub, tc::TokTile<BN>::kTokCta,
-                                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B)
-                : encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xp, a.K, a.M,
-                                       static_cast<uint64_t>(a.K) * 2, tc::kXSub, tc::TokTile<BN>::kTokCta,
-                                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xp, a.K, a.M,
+                                  static_cast<uint64_t>(a.K) * 2, tc::kXSub, tc::TokTile<BN>::kTokCta,
+                                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (!rc)
         rc = encode_tensor_map_2d(&maps.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wt.nibbles, a.K / 2, a.N, a.K / 2,
                                   tc::kWK / 2, tc::kRowsCta, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1310,7 +1200,7 @@ static int tc_launch(const GemmArgs& a, const TcWeights& wt, void* xp, const Spl
     cfg.stream = a.stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel<ASYM, EXACT, BN, FX>, maps, p));
+    BYBYCU_CUDA_TRY(cudaLaunchKernelEx(&cfg, tc::gemm_kernel<ASYM, EXACT, BN>, maps, p));
     return BYBYCU_OK;
 }
 
@@ -1324,11 +1214,11 @@ struct SplitScratch {
 
 // tc_launch with a split-K plan: a tail that leaves pairs idle is split when `ss` offers
 // room for its partial sums and counters.
-template <bool ASYM, bool EXACT, int BN, bool FX>
+template <bool ASYM, bool EXACT, int BN>
 static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitScratch& ss) {
     DeviceInfo info;
     int max_pairs = 0;
-    if (int rc = tc_setup<ASYM, EXACT, BN, FX>(&info, &max_pairs)) return rc;
+    if (int rc = tc_setup<ASYM, EXACT, BN>(&info, &max_pairs)) return rc;
     const int tiles_n = static_cast<int>(ceil_div(a.N, tc::kRowsPair));
     const int64_t tiles = static_cast<int64_t>(tiles_n) * ceil_div(a.M, BN);
     if (tiles > (1 << 30)) return set_error(BYBYCU_ERR_SHAPE, "tensor-core route: too many tiles (M=%d N=%d)", a.M, a.N);
@@ -1336,63 +1226,48 @@ static int tc_run(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitS
     SplitPlan sp = tc_split_plan(tiles, max_pairs, a.K / tc::kWK, BN);
     const size_t sp_bytes = static_cast<size_t>(sp.partial_floats + sp.flags) * 4;
     if (sp.split > 1 && !ss.pool && sp_bytes > ss.bytes) sp = whole;
-    if (sp.split == 1) return tc_launch<ASYM, EXACT, BN, FX>(a, wt, xp, sp, nullptr, nullptr, max_pairs, tiles_n, tiles);
+    if (sp.split == 1) return tc_launch<ASYM, EXACT, BN>(a, wt, xp, sp, nullptr, nullptr, max_pairs, tiles_n, tiles);
     if (!ss.pool) {
         float* partial = static_cast<float*>(ss.ptr);
-        return tc_launch<ASYM, EXACT, BN, FX>(a, wt, xp, sp, partial,
-                                              reinterpret_cast<uint32_t*>(partial + sp.partial_floats), max_pairs,
-                                              tiles_n, tiles);
+        return tc_launch<ASYM, EXACT, BN>(a, wt, xp, sp, partial, reinterpret_cast<uint32_t*>(partial + sp.partial_floats),
+                                          max_pairs, tiles_n, tiles);
     }
     cudaMemPool_t pool = nullptr;
     if (int rc = scratch_pool(info.device, &pool)) return rc;
     void* part = nullptr;
     BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&part, sp_bytes, pool, a.stream));
     float* partial = static_cast<float*>(part);
-    const int rc = tc_launch<ASYM, EXACT, BN, FX>(a, wt, xp, sp, partial,
-                                                  reinterpret_cast<uint32_t*>(partial + sp.partial_floats), max_pairs,
-                                                  tiles_n, tiles);
+    const int rc = tc_launch<ASYM, EXACT, BN>(a, wt, xp, sp, partial,
+                                              reinterpret_cast<uint32_t*>(partial + sp.partial_floats), max_pairs,
+                                              tiles_n, tiles);
     const cudaError_t fe = cudaFreeAsync(part, a.stream);
     if (rc) return rc;
     if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync(tc split-K scratch)");
     return BYBYCU_OK;
 }
 
-// bf16 activations of the Q4B32 kernels are converted inside the GEMM; fp32 activations and
-// the asymmetric kernel's go through the staging pass.
-template <bool ASYM>
-static bool tc_in_kernel_x(const GemmArgs& a) { return !ASYM && a.x_dtype == BYBYCU_DT_BF16; }
-
-template <bool ASYM, bool EXACT, bool FX>
-static int tc_run_rows_t(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitScratch& ss) {
+template <bool ASYM, bool EXACT>
+static int tc_run_rows(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitScratch& ss) {
     switch (tc_token_tile(a.M)) {
-        case 16: return tc_run<ASYM, EXACT, 16, FX>(a, wt, xp, ss);
-        case 32: return tc_run<ASYM, EXACT, 32, FX>(a, wt, xp, ss);
-        case 64: return tc_run<ASYM, EXACT, 64, FX>(a, wt, xp, ss);
-        default: return tc_run<ASYM, EXACT, 128, FX>(a, wt, xp, ss);
+        case 16: return tc_run<ASYM, EXACT, 16>(a, wt, xp, ss);
+        case 32: return tc_run<ASYM, EXACT, 32>(a, wt, xp, ss);
+        case 64: return tc_run<ASYM, EXACT, 64>(a, wt, xp, ss);
+        default: return tc_run<ASYM, EXACT, 128>(a, wt, xp, ss);
     }
 }
 
-template <bool ASYM, bool EXACT>
-static int tc_run_rows(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitScratch& ss) {
-    if constexpr (!ASYM)
-        if (tc_in_kernel_x<ASYM>(a)) return tc_run_rows_t<ASYM, EXACT, true>(a, wt, xp, ss);
-    return tc_run_rows_t<ASYM, EXACT, false>(a, wt, xp, ss);
-}
-
-// Runs the GEMM with its scratch (the staged activations when the staging pass runs, split-K
-// sums) from stream-ordered pool memory.
+// Stages through stream-ordered pool scratch and runs the GEMM.
 template <bool ASYM, bool EXACT>
 static int tc_pooled(const GemmArgs& a, const TcWeights& wt) {
     DeviceInfo info;
     if (int rc = current_device_info(&info)) return rc;
-    SplitScratch ss;
-    ss.pool = true;
-    if (tc_in_kernel_x<ASYM>(a)) return tc_run_rows<ASYM, EXACT>(a, wt, nullptr, ss);
     const size_t xp_bytes = static_cast<size_t>(a.M) * a.K * 2;
     void* xp = nullptr;
     cudaMemPool_t pool = nullptr;
     if (int rc = scratch_pool(info.device, &pool)) return rc;
     BYBYCU_CUDA_TRY(cudaMallocFromPoolAsync(&xp, xp_bytes, pool, a.stream));
+    SplitScratch ss;
+    ss.pool = true;
     const int rc = tc_run_rows<ASYM, EXACT>(a, wt, xp, ss);
     const cudaError_t fe = cudaFreeAsync(xp, a.stream);
     if (rc) return rc;
@@ -1509,14 +1384,6 @@ int tc_static_scratch_load() {
     if (int rc = tc_setup<true, false, 32>(&d, &max_pairs)) return rc;
     if (int rc = tc_setup<true, false, 64>(&d, &max_pairs)) return rc;
     if (int rc = tc_setup<true, false, 128>(&d, &max_pairs)) return rc;
-    if (int rc = tc_setup<false, true, 16, true>(&d, &max_pairs)) return rc;
-    if (int rc = tc_setup<false, true, 32, true>(&d, &max_pairs)) return rc;
-    if (int rc = tc_setup<false, true, 64, true>(&d, &max_pairs)) return rc;
-    if (int rc = tc_setup<false, true, 128, true>(&d, &max_pairs)) return rc;
-    if (int rc = tc_setup<false, false, 16, true>(&d, &max_pairs)) return rc;
-    if (int rc = tc_setup<false, false, 32, true>(&d, &max_pairs)) return rc;
-    if (int rc = tc_setup<false, false, 64, true>(&d, &max_pairs)) return rc;
-    if (int rc = tc_setup<false, false, 128, true>(&d, &max_pairs)) return rc;
     cudaFuncAttributes fa;
     BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<false, tc::kPermQ4B32>));
     BYBYCU_CUDA_TRY(cudaFuncGetAttributes(&fa, tc::stage_x_kernel<true, tc::kPermQ4B32>));

@@ -144,14 +144,14 @@ BYBYCU_API int bybycu_tile_gemm_host(int fmt, int M, int K, int N,
  * nearly all HBM for its own caches at start-up, where a call-time allocation can fail or
  * stall on the allocator.  This entry point has no reference counterpart: the reference
  * never stages activations, so it never needs scratch.
- *   Scratch: the fp16 staging copy of fp32 x (M*K*2 bytes; bf16 x is converted inside the
- *   GEMM and needs none) lives in one fixed 32 MiB array of the library's device memory.  CUDA loads a module lazily, so bybycu_init(device) loads
+ *   Scratch: the fp16 staging copy of x (M*K*2 bytes) lives in one fixed 32 MiB array of
+ *   the library's device memory.  CUDA loads a module lazily, so bybycu_init(device) loads
  *   this array and the route's kernels on that device; call it once per device before the
  *   first call here (and before any stream capture).  Each call then looks the array's
  *   address up (cudaGetSymbolAddress) in the current context; nothing is allocated or freed
  *   per call.  No part of it needs to start at zero: every byte the GEMM reads is written
  *   by the same call first.  When the route splits its last wave's tiles along K, the
- *   partial sums use the array's room past M*K*2 bytes; without room the tiles
+ *   partial sums use the array's room past the staged activations; without room the tiles
  *   run whole (the same result within the route's tolerance, summed in another order).
  *   Limit: M*K <= 16,777,216 (e.g. M=4096 at K=4096); larger shapes fail with
  *   BYBYCU_ERR_RANGE before anything is launched.  Shapes the TC route cannot tile

@@ -27,6 +27,10 @@ struct GemmArgs {
     // stages: the ring depth of the streamed weights (GEMV routes).
     int variant = -1;
     int stages = 0;
+    // Tensor-core route, fp32 x: each activation row is staged as two fp16 rows, x_hi =
+    // RNE16(x) and x_lo = RNE16(x - x_hi), and the GEMM runs over 2 * M token rows (M here
+    // counts those), adding each row pair in its epilogue.
+    bool x_split = false;
     // Set by the sharded entry points: the kernel also stores its slice into every rank's
     // output (the tensor-core route; the GEMV takes it as launch_gemv's argument).
     const struct PeerGather* pg = nullptr;

@@ -142,6 +142,9 @@ struct Params {
     int64_t out_ld, out_col0;
     int out_bf16;
     PeerGather pg;    // world > 1: the epilogue also stores every value to the other ranks (fp32)
+    // x_split: token rows come in pairs (x_hi, x_lo of one fp32 activation row, M counting
+    // both); the epilogue stores row pair r as output row r / 2, the sum of the two
+    int x_split = 0;
     // Work units (the Q4 kernels): tiles [0, full_tiles) whole, every later tile as `split`
     // K-parts (one unit each, weight-stage aligned) so that the last wave fills the pairs.
     // Parts 0 .. split-2 leave fp32 partial sums in `partial` ([tail tile][part][CTA][warp]
@@ -483,10 +486,14 @@ constexpr int kPermQ4B32 = 0, kPermAsym = 1, kPermNone = 2;
 __host__ __device__ constexpr int perm_of(int mode, int kk) {
     return mode == kPermAsym ? perm_src_asym(kk) : mode == kPermNone ? kk : perm_src(kk);
 }
-template <bool XF32, int PERM = kPermQ4B32>
+// SPLIT (fp32 x): two fp16 rows per activation row, x_hi = RNE16(x) in row 2m and the exact
+// remainder x_lo = RNE16(x - x_hi) in row 2m + 1 (g: 32-blocks per row); together they keep
+// about 22 of fp32's 24 significant bits.
+template <bool XF32, int PERM = kPermQ4B32, bool SPLIT = false>
 __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x, uint4* __restrict__ xp,
                                                       int64_t nblocks, PeerGather pg, uint32_t* flags = nullptr,
-                                                      int n_flags = 0) {
+                                                      int n_flags = 0, int64_t g = 0) {
+    static_assert(!SPLIT || XF32, "the two-term form is for fp32 activations");
     pdl_launch_dependents();   // the GEMM may start its prologue; it waits before reading xp
     if (blockIdx.x == 0)       // the GEMM's split-K counters (its griddepcontrol.wait sees these)
         for (int f = threadIdx.x; f < n_flags; f += blockDim.x) flags[f] = 0u;
@@ -526,8 +533,26 @@ __global__ void __launch_bounds__(256) stage_x_kernel(const void* __restrict__ x
         o[c] = h2_bits(__floats2half2_rn(a, b));
     }
     if (!range_ok) record_device_error(kDevErrActRange);
+    if constexpr (SPLIT) {
+        const int64_t m = i / g, c = i % g;
+        uint4* hi = xp + ((2 * m) * g + c) * 4;
+        uint4* lo = xp + ((2 * m + 1) * g + c) * 4;
+        uint32_t r[16];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) xp[i * 4 + q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        for (int k = 0; k < 16; ++k) {
+            const __half2 h = bits_h2(o[k]);
+            const float a = v[perm_of(PERM, 2 * k)] - __low2float(h), b = v[perm_of(PERM, 2 * k + 1)] - __high2float(h);
+            r[k] = h2_bits(__floats2half2_rn(a, b));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            hi[q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            lo[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) xp[i * 4 + q] = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+    }
 }
 
 
@@ -627,7 +652,19 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
                     for (int k = 1; k < active; ++k) sum += lds_f32(slot0 + k * (kBlock * 4) + o);
                     v[j] = __float_as_uint(sum + __uint_as_float(v[j]));
                 }
-            if (feat_ok) {
+            if (feat_ok && p.x_split) {   // row pairs (x_hi, x_lo): one output row each
+                const int nt = min(kChunk, p.M - (tok0 + c0));
+                const int64_t o0 = p.out_col0 + feat + static_cast<int64_t>((tok0 + c0) >> 1) * p.out_ld;
+#pragma unroll
+                for (int j = 0; j < kChunk; j += 2) {
+                    if (j >= nt) continue;
+                    const float val = __uint_as_float(v[j]) + __uint_as_float(v[j + 1]);
+                    const int64_t oi = o0 + (j >> 1) * p.out_ld;
+                    if (p.out_bf16) reinterpret_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(val);
+                    else reinterpret_cast<float*>(p.out)[oi] = val;
+                    if (p.pg.world > 1) store_to_peers(p.pg, oi, val);
+                }
+            } else if (feat_ok) {
                 const int nt = min(kChunk, p.M - (tok0 + c0));
                 if (p.out_bf16) {
                     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + p.out_col0 + feat +
@@ -1133,12 +1170,16 @@ static SplitPlan tc_split_plan(int64_t tiles, int max_pairs, int n_kw, int bn) {
 template <bool ASYM, bool EXACT, int BN>
 static int tc_launch(const GemmArgs& a, const TcWeights& wt, void* xp, const SplitPlan& sp, float* partial,
                      uint32_t* flags, int max_pairs, int tiles_n, int64_t tiles) {
-    const int64_t nblocks = static_cast<int64_t>(a.M) * (a.K / 32);
+    const int64_t G = static_cast<int64_t>(a.K / 32);
+    const int64_t nblocks = static_cast<int64_t>(a.x_split ? a.M / 2 : a.M) * G;   // 32-blocks of x
     const unsigned grid_x = static_cast<unsigned>(ceil_div(nblocks, 256));
     constexpr int perm = ASYM ? tc::kPermAsym : tc::kPermQ4B32;
     const PeerGather pg = a.pg ? *a.pg : PeerGather();
     const int n_flags = static_cast<int>(sp.flags);
-    if (a.x_dtype == BYBYCU_DT_F32)
+    if (a.x_split)
+        tc::stage_x_kernel<true, perm, true><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg,
+                                                                           flags, n_flags, G);
+    else if (a.x_dtype == BYBYCU_DT_F32)
         tc::stage_x_kernel<true, perm><<<grid_x, 256, 0, a.stream>>>(a.x, static_cast<uint4*>(xp), nblocks, pg, flags,
                                                                      n_flags);
     else
@@ -1148,7 +1189,6 @@ static int tc_launch(const GemmArgs& a, const TcWeights& wt, void* xp, const Spl
 
     tc::Maps maps;
     memset(&maps, 0, sizeof maps);
-    const uint64_t G = static_cast<uint64_t>(a.K / 32);
     int rc = encode_tensor_map_2d(&maps.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xp, a.K, a.M,
                                   static_cast<uint64_t>(a.K) * 2, tc::kXSub, tc::TokTile<BN>::kTokCta,
                                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
@@ -1174,6 +1214,7 @@ static int tc_launch(const GemmArgs& a, const TcWeights& wt, void* xp, const Spl
     p.out_ld = a.out_ld;
     p.out_col0 = a.out_col0;
     p.out_bf16 = a.out_dtype == BYBYCU_DT_BF16;
+    p.x_split = a.x_split ? 1 : 0;
     if (a.pg) {
         if (p.out_bf16) return set_error(BYBYCU_ERR_ARGS, "tensor-core all-gather: the gathered output is fp32");
         p.pg = *a.pg;
@@ -1277,13 +1318,25 @@ static int tc_pooled(const GemmArgs& a, const TcWeights& wt) {
 
 // Q4B32 on the tensor cores: exact weight terms (route TC), or each weight rounded once to
 // fp16 (route TC_FP16W, the reference's cooperative-matrix lowering).
+// fp32 activations enter the tensor cores as two fp16 rows each (x_split), so that they keep
+// ~22 significant bits instead of fp16's 11.
+static GemmArgs tc_split_rows(const GemmArgs& a) {
+    GemmArgs b = a;
+    if (a.x_dtype == BYBYCU_DT_F32 && a.M <= (1 << 29)) {
+        b.M = 2 * a.M;
+        b.x_split = true;
+    }
+    return b;
+}
+
 int launch_tc(const GemmArgs& a, bool fp16_weights) {
     if (a.fmt == BYBYCU_FMT_F16) return launch_tc_f16(a);
     if (int rc = tc_check(a)) return rc;
     TcWeights wt;
     wt.nibbles = a.packed;
     wt.scales = a.packed + a.scale_base;
-    return fp16_weights ? tc_pooled<false, false>(a, wt) : tc_pooled<false, true>(a, wt);
+    const GemmArgs b = tc_split_rows(a);
+    return fp16_weights ? tc_pooled<false, false>(b, wt) : tc_pooled<false, true>(b, wt);
 }
 
 bool tc_asym_supports(int M, int K, int N, int group, int n_groups, const void* x, const void* wq, const void* scales,
@@ -1390,14 +1443,16 @@ int tc_static_scratch_load() {
     return BYBYCU_OK;
 }
 
-int launch_tc_static_scratch(const GemmArgs& a) {
-    const size_t need = static_cast<size_t>(a.M) * a.K * 2;
+int launch_tc_static_scratch(const GemmArgs& a_in) {
+    const int terms = a_in.x_dtype == BYBYCU_DT_F32 ? 2 : 1;   // fp32 rows stage as two fp16 rows
+    const size_t need = static_cast<size_t>(a_in.M) * a_in.K * 2 * terms;
     if (need > kStaticScratchBytes)
         return set_error(BYBYCU_ERR_RANGE,
-                         "static-scratch tensor-core GEMM stages M*K fp16 activations in a fixed %zu MiB array: "
-                         "M=%d K=%d needs %zu bytes (at most M*K = %zu)",
-                         kStaticScratchBytes >> 20, a.M, a.K, need, kStaticScratchBytes / 2);
-    if (int rc = tc_check(a)) return rc;
+                         "static-scratch tensor-core GEMM stages M*K fp16 activations (two terms each for fp32 x) "
+                         "in a fixed %zu MiB array: M=%d K=%d needs %zu bytes (at most M*K = %zu)",
+                         kStaticScratchBytes >> 20, a_in.M, a_in.K, need, kStaticScratchBytes / 2 / terms);
+    if (int rc = tc_check(a_in)) return rc;
+    const GemmArgs a = tc_split_rows(a_in);
     void* xp = nullptr;
     if (int rc = static_scratch(&xp)) return rc;
     TcWeights wt;

@@ -7,11 +7,11 @@ accumulation.  Its outputs are held to the reference gate's per-element metric,
 |got - want| / max(1, |want|) <= 1e-3 (backends/vulkan/vulkan_driver.nim:2752-2754), and to the
 reference test's max|diff| <= tol * max(1, max|ref|) (tests/t_fp4_tile_gemm.nim:54-67).
 
-fp32 activations on this route are rounded to fp16 (the GEMV route keeps them exact up to 32
-rows, and AUTO sends fp32 rows there); with them only the reference test's peak-normalised
-metric at the path's 1e-3 applies.  Route TC_FP16W rounds each weight once to fp16, as the
-reference's cooperative lowering does (micro_kernel/tile_gemm.nim:322-325, 414): peak-normalised
-1e-3 as well.
+fp32 activations enter this route as two fp16 rows each, x_hi = RNE16(x) and the remainder
+x_lo = RNE16(x - x_hi) (about 22 of fp32's 24 significant bits), whose two products the
+epilogue adds: per-element 1e-3 as well (test_tc_fp32_activations_per_element).  Route
+TC_FP16W rounds each weight once to fp16, as the reference's cooperative lowering does
+(micro_kernel/tile_gemm.nim:322-325, 414): the reference test's peak-normalised 1e-3.
 """
 import numpy as np
 import pytest
@@ -57,7 +57,7 @@ def test_tc_golden_cases(golden, oracle_mod):
         assert_close(g[f"q4_{i}_vm"], out.cpu().numpy(), TC_TOL, ELEM_TOL, what=f"case {i} bf16")
         xf = dev(oracle_mod.bf16_to_f32(g[f"q4_{i}_x_bf16"]))
         out = run(2, M, K, N, xf, slot, scale_base=sb, route=_lib.ROUTE_TC)
-        assert_close(g[f"q4_{i}_vm"], out.cpu().numpy(), TC_TOL, what=f"case {i} f32")
+        assert_close(g[f"q4_{i}_vm"], out.cpu().numpy(), TC_TOL, ELEM_TOL, what=f"case {i} f32")
         ran += 1
     assert ran == 3
 
@@ -109,6 +109,22 @@ def test_tc_prefill_rows_against_oracle(oracle_mod):
     rows = np.r_[0:8, 255:259, 1023:1027, 2040:2048]
     want = O.tile_gemm_q4b32(O.bf16_to_f32(xb[rows]), p, s, len(rows), K, N, threads=8)
     assert_close(want, out[rows], TC_TOL, ELEM_TOL, what="C3 sampled rows")
+
+
+@pytest.mark.parametrize("M,K,N", [(32, 4096, 4096), (300, 1024, 384), (1000, 2048, 77)])
+def test_tc_fp32_activations_per_element(M, K, N, oracle_mod, parity_log):
+    """fp32 activations with their full mantissa (not bf16 values) on route TC, against the
+    oracle's fp32 arithmetic, per element; the first shape is config C1."""
+    O = oracle_mod
+    p, s = O.gen_q4b32(N, K, seed=O.Xorshift32.SEED + M)
+    xf = O.gen_x_f32(M, K, seed=O.Xorshift32.SEED + 7 + M)
+    slot, sb = q4_slot(p, s)
+    want = O.tile_gemm_q4b32(xf, p, s, M, K, N, threads=8)
+    got = run(2, M, K, N, dev(xf), slot, scale_base=sb, route=_lib.ROUTE_TC).cpu().numpy()
+    parity_log.append((f"{M}x{K}x{N} fp32 x, route TC (two fp16 terms per activation)", elem_err(want, got), ELEM_TOL))
+    assert_close(want, got, TC_TOL, ELEM_TOL, what=f"fp32 x M={M} K={K} N={N}")
+    b16 = run(2, M, K, N, dev(xf), slot, scale_base=sb, route=_lib.ROUTE_TC, out_dtype=torch.bfloat16)
+    assert torch.equal(torch.from_numpy(got).to(torch.bfloat16), b16.cpu())
 
 
 def test_tc_bf16_output_is_rounded_f32_output(oracle_mod):

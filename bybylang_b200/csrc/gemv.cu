@@ -1227,31 +1227,36 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     size_t stage_bytes = 0, red_bytes = 0;
     uint32_t s_pitch = 0, w_box = 0, s_off = 0, x_off = 0;
     int x_pitch = 0;
-    for (int kc_try : {512, 1024, 2048}) {
-        if (m1 && kc_try != kM1KC) continue;   // the M = 1 kernel: one 256-value box per warp
-        // M = 1: passes of 5 or 7 tiles, whichever needs fewer passes over a CTA's rows (each
-        // pass is a whole sweep of K and ends in a cross-warp reduction); 5 on a tie, whose
-        // smaller stages let two CTAs share an SM when one pass does
-        const int tp_m1 = ceil_div(tiles_max, 7) < ceil_div(tiles_max, 5) ? 7 : 5;
-        const int tp_try = std::min(tiles_max, m1 ? tp_m1 : ntn == 2 ? 5 : 8);
-        const int tpl_try = tp_try <= 2 ? 2 : tp_try <= 5 ? 5 : (m1 ? 7 : 8);
-        const uint32_t rows = 16 * tpl_try;
-        const uint32_t sp = static_cast<uint32_t>(kc_try / 32 * 2);
-        const uint32_t wb = rows * 128;
-        const uint32_t so = (kc_try / 256) * wb;
-        const uint32_t xo = static_cast<uint32_t>(so + round1k(scale_tma ? rows * sp : 0));
-        const int xp = kc_try * xe + 32;
-        const size_t sb = round1k(xo + (x_whole ? 0 : static_cast<size_t>(a.M) * xp));
-        const size_t rb = m1 ? static_cast<size_t>(kM1Warps) * tpl_try * 16 * sizeof(float)
-                             : static_cast<size_t>(kRedSlots) * tpl_try * ntn * 128 * sizeof(float);
-        const int nch = static_cast<int>(ceil_div(a.K, kc_try));
-        const int want = static_cast<int>(ceil_div(tiles_max, tp_try)) * nch;
-        if (budget < rb + x_all + sb + 16) continue;
-        const int st = static_cast<int>((budget - rb - x_all) / (sb + 16));
-        if (st >= std::min(m1 ? 2 : 4, want) && st >= 1) {
-            kc = kc_try; tp = tp_try; tpl = tpl_try; stages = std::min(st, want);
-            stage_bytes = sb; red_bytes = rb; s_pitch = sp; w_box = wb; s_off = so; x_off = xo; x_pitch = xp;
-            break;
+    // at least four stages in flight where they fit (two for the M = 1 kernel), else two:
+    // 16 fp32 rows beside 80-row tiles leave room for three (M = 16, N = 11008)
+    for (int need_st : {m1 ? 2 : 4, 2}) {
+        if (kc) break;
+        for (int kc_try : {512, 1024, 2048}) {
+            if (m1 && kc_try != kM1KC) continue;   // the M = 1 kernel: one 256-value box per warp
+            // M = 1: passes of 5 or 7 tiles, whichever needs fewer passes over a CTA's rows (each
+            // pass is a whole sweep of K and ends in a cross-warp reduction); 5 on a tie, whose
+            // smaller stages let two CTAs share an SM when one pass does
+            const int tp_m1 = ceil_div(tiles_max, 7) < ceil_div(tiles_max, 5) ? 7 : 5;
+            const int tp_try = std::min(tiles_max, m1 ? tp_m1 : ntn == 2 ? 5 : 8);
+            const int tpl_try = tp_try <= 2 ? 2 : tp_try <= 5 ? 5 : (m1 ? 7 : 8);
+            const uint32_t rows = 16 * tpl_try;
+            const uint32_t sp = static_cast<uint32_t>(kc_try / 32 * 2);
+            const uint32_t wb = rows * 128;
+            const uint32_t so = (kc_try / 256) * wb;
+            const uint32_t xo = static_cast<uint32_t>(so + round1k(scale_tma ? rows * sp : 0));
+            const int xp = kc_try * xe + 32;
+            const size_t sb = round1k(xo + (x_whole ? 0 : static_cast<size_t>(a.M) * xp));
+            const size_t rb = m1 ? static_cast<size_t>(kM1Warps) * tpl_try * 16 * sizeof(float)
+                                 : static_cast<size_t>(kRedSlots) * tpl_try * ntn * 128 * sizeof(float);
+            const int nch = static_cast<int>(ceil_div(a.K, kc_try));
+            const int want = static_cast<int>(ceil_div(tiles_max, tp_try)) * nch;
+            if (budget < rb + x_all + sb + 16) continue;
+            const int st = static_cast<int>((budget - rb - x_all) / (sb + 16));
+            if (st >= std::min(need_st, want) && st >= 1) {
+                kc = kc_try; tp = tp_try; tpl = tpl_try; stages = std::min(st, want);
+                stage_bytes = sb; red_bytes = rb; s_pitch = sp; w_box = wb; s_off = so; x_off = xo; x_pitch = xp;
+                break;
+            }
         }
     }
     if (!kc) return set_error(BYBYCU_ERR_SHAPE, "GEMV: shared memory too small for M=%d", a.M);

@@ -60,7 +60,7 @@ extern "C" {
 #define BYBYCU_DT_BF16 1
 
 /* kernel routes */
-#define BYBYCU_ROUTE_AUTO 0   /* GEMV for M <= 16 (M <= 32 with fp32 x), tensor-core GEMM above;
+#define BYBYCU_ROUTE_AUTO 0   /* GEMV for M <= 16, tensor-core GEMM above;
                                  format 2 with bf16 x: tensor cores from M = 4 when K >= 8192
                                  and from M = 12 when N >= 65536 */
 #define BYBYCU_ROUTE_GEMV 1   /* decode GEMV: TMA-streamed weights, register dequant */

@@ -48,18 +48,18 @@ def _peak_tol(route):
 
 
 def test_c1_fp32_rows_per_element(oracle_mod, parity_log):
-    """C1 through AUTO: 32 fp32 rows take the GEMV route (two launches of 16 rows), whose
-    activations stay exact as two bf16 terms."""
+    """C1 through AUTO: 32 fp32 rows take the tensor-core route, each activation as two fp16
+    terms (x_hi and the remainder x_lo)."""
     O = oracle_mod
     M, K, N = 32, 4096, 4096
     p, s, slot, sb = _weights(O, N, K, 1)
     xf = O.gen_x_f32(M, K, seed=O.Xorshift32.SEED + 3)
     route = gb.route_for(2, M, K, N, _lib.DT_F32)
-    assert route == _lib.ROUTE_GEMV
+    assert route == _lib.ROUTE_TC
     want = O.tile_gemm_q4b32(xf, p, s, M, K, N, threads=THREADS)
     got = run(2, M, K, N, dev(xf), slot, scale_base=sb).cpu().numpy()
     worst = elem_err(want, got)
-    parity_log.append(("C1 32x4096x4096 fp32 x, AUTO (GEMV)", worst, ELEM_TOL))
+    parity_log.append(("C1 32x4096x4096 fp32 x, AUTO (TC, two fp16 terms per activation)", worst, ELEM_TOL))
     assert_close(want, got, _peak_tol(route), ELEM_TOL, what="C1")
 
 

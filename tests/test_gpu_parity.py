@@ -126,6 +126,20 @@ def test_gemv_lm_head_columns_against_oracle(oracle_mod):
     assert_close(want, out[:, cols], what="lm head")
 
 
+@pytest.mark.parametrize("M,N", [(9, 11008), (16, 11008)])
+def test_gemv_fp32_rows_beside_wide_tiles(M, N, oracle_mod):
+    """fp32 rows of 9-16 activations beside 80-row weight tiles: four ring stages do not fit in
+    shared memory, so the GEMV plans two or three."""
+    O = oracle_mod
+    K = 4096
+    p, s = O.gen_q4b32(N, K, seed=77 + M)
+    xf = O.gen_x_f32(M, K, seed=78 + M)
+    want = O.tile_gemm_q4b32(xf, p, s, M, K, N, threads=8)
+    slot, sb = q4_slot(p, s)
+    out = run(2, M, K, N, dev(xf), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert_close(want, out.cpu().numpy(), 1e-4, 1e-3, what=f"fp32 M={M} N={N}")
+
+
 @pytest.mark.parametrize("M,K,N", [(1, 32, 1), (2, 96, 15), (3, 288, 17), (7, 4128, 130), (8, 256, 16),
                                    (12, 800, 33), (16, 64, 1000), (5, 4096, 1)])
 def test_gemv_ragged_shapes(M, K, N, oracle_mod):

@@ -1051,6 +1051,16 @@ int m1_mode() {
     return mode;
 }
 
+// BYBY_CUDA_GEMV_M1=i8f32: fp32 decode rows in the integer mode too (faster, 15-bit
+// activations relative to each block's largest value).
+bool m1_fp32_digits() {
+    static const bool on = [] {
+        const char* e = getenv("BYBY_CUDA_GEMV_M1");
+        return e && !strcmp(e, "i8f32");
+    }();
+    return on;
+}
+
 template <int TP, bool STMA>
 int launch_m1(int mode, bool xf32, const GemvMaps& maps, const GemvParams& p, int grid, size_t smem,
               cudaStream_t stream) {
@@ -1198,11 +1208,14 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     const int xe = xf32 ? 4 : 2;
     const int n_tiles = static_cast<int>(ceil_div(a.N, kTileRows));
     const int grid = std::min(n_tiles, dev.sm_count);
-    // the M = 1 kernel: bf16 rows in every operand mode, fp32 rows in the integer mode (the
-    // other modes take fp32 rows through the general kernel's two-term split)
+    // the M = 1 kernel takes bf16 rows.  fp32 rows take the general kernel's two bf16 terms
+    // (16 significant bits per value): the integer mode's 15-bit fixed point, relative to each
+    // block's largest value, left up to 2.1e-3 per element on N(0, 1) fp32 rows at K = 11008,
+    // against 1.0e-4 with the two terms (C2 with fp32 x: 14.2 against 7.3 us).  The integer
+    // mode still takes fp32 rows when BYBY_CUDA_GEMV_M1=i8f32 asks for the faster form.
     const int want_mode = a.variant >= kM1Bf16 && a.variant <= kM1I8 ? a.variant : m1_mode();
     const int mode = want_mode == kM1I8 && a.K > 32768 ? kM1F16 : want_mode;
-    const bool m1 = a.M == 1 && (!xf32 || mode == kM1I8);
+    const bool m1 = a.M == 1 && (!xf32 || (mode == kM1I8 && m1_fp32_digits()));
     // M = 1 splits rows, not tiles: 11008 rows over 148 CTAs is 74 or 75 rows each instead of 4
     // or 5 tiles (64 or 80 rows), so no CTA streams 6% more than its share and all end together
     const int rows_base = a.N / grid, rows_extra = a.N % grid;

@@ -197,21 +197,22 @@ def test_gemv_m1_activation_dynamic_range(K, N, xdt, oracle_mod):
     assert _lib.device_error() == 0
 
 
-@pytest.mark.parametrize("K,N", [(4096, 11008), (4192, 300), (1024, 64)])
-def test_gemv_m1_f32_rows_match_bf16_rows(K, N, oracle_mod):
-    """fp32 rows take the decode kernel's integer mode directly: a row of bf16 values gives
-    bit-identical outputs as fp32 and as bf16 (same exponents, same fixed-point digits)."""
+@pytest.mark.parametrize("K,N", [(4096, 11008), (11008, 4096), (4192, 300), (1024, 64)])
+def test_gemv_m1_f32_rows_per_element(K, N, oracle_mod):
+    """fp32 decode rows with their full mantissa take the general kernel's two bf16 terms:
+    per element within 1e-3 of the oracle's fp32 arithmetic (the integer mode's 15-bit fixed
+    point, relative to each block's largest value, is not)."""
     O = oracle_mod
     p, s = O.gen_q4b32(N, K, seed=K + 3)
-    xb = O.gen_x_bf16(1, K, seed=N)
+    xf = O.gen_x_f32(1, K, seed=N)
     slot, sb = q4_slot(p, s)
-    a = run(2, 1, K, N, dev(xb).view(torch.bfloat16), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
-    b = run(2, 1, K, N, dev(O.bf16_to_f32(xb)), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
-    assert torch.equal(a, b)
-    assert_close(O.tile_gemm_q4b32(O.bf16_to_f32(xb), p, s, 1, K, N), b.cpu().numpy(), what=f"K={K} N={N}")
+    got = run(2, 1, K, N, dev(xf), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert_close(O.tile_gemm_q4b32(xf, p, s, 1, K, N, threads=8), got.cpu().numpy(), what=f"K={K} N={N}")
 
 
-def test_gemv_m1_nonfinite_f32_activation_is_reported(oracle_mod):
+def test_gemv_m1_nonfinite_f32_activation_propagates(oracle_mod):
+    """An fp32 NaN activation reaches every output as NaN, as in the reference's fp32
+    arithmetic, without a device error; the next call is clean."""
     O = oracle_mod
     K, N = 2048, 256
     p, s = O.gen_q4b32(N, K)
@@ -219,8 +220,9 @@ def test_gemv_m1_nonfinite_f32_activation_is_reported(oracle_mod):
     slot, sb = q4_slot(p, s)
     x = dev(xf).clone()
     x[0, 1500] = float("nan")
-    run(2, 1, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_GEMV)
-    assert _lib.device_error() == 7
+    bad = run(2, 1, K, N, x, slot, scale_base=sb, route=_lib.ROUTE_GEMV)
+    assert torch.isnan(bad).all()
+    assert _lib.device_error() == 0
     out = run(2, 1, K, N, dev(xf), slot, scale_base=sb, route=_lib.ROUTE_GEMV)
     assert_close(O.tile_gemm_q4b32(xf, p, s, 1, K, N), out.cpu().numpy())
 

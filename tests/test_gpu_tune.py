@@ -70,12 +70,11 @@ def test_q4b32_decode_plan_is_used_and_correct():
     # preparing again is a table hit, not a second tune
     assert w.prepare(1)
     assert gb.q4TuningStats()[0] == 1
-    # fp32 rows have their own plan: the integer-mode kernel reads them directly and beats
-    # the general kernel's two-term split
+    # fp32 rows have their own plan (the GEMV's two-term form for fp32 activations)
     assert gb.tunedPlan(_lib.OP_TILE_GEMM, fmt=_lib.FMT_Q4B32, x_dtype=_lib.DT_F32, M=1, K=K, N=N) is None
     assert w.prepare(1, _lib.DT_F32)
     plan32 = gb.tunedPlan(_lib.OP_TILE_GEMM, fmt=_lib.FMT_Q4B32, x_dtype=_lib.DT_F32, M=1, K=K, N=N)
-    assert plan32 is not None and plan32.name.startswith(b"gemv-s8"), plan32
+    assert plan32 is not None and plan32.route == _lib.ROUTE_GEMV, plan32
     xf = O.bf16_to_f32(xb)
     got = w.matmul(torch.from_numpy(xf).to(DEV))
     torch.cuda.synchronize()

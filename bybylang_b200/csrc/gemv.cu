@@ -536,7 +536,8 @@ gemv_q4b32_kernel(const __grid_constant__ GemvMaps maps, const GemvParams p) {
 // of each 32-block become a fixed-point image X = rint(x * 2^(140 - E)) (E = the block's
 // largest bf16 exponent, so |X| <= 2^14: exact for every element within 7 binades of the
 // block's largest, 2^-15 of it otherwise) split into two signed byte digits,
-// X = 256 h + sext8(X).  The four blocks of a warp share one accumulator: block j's low and
+// X = 256 h + sext8(X); an fp32 row adds a second image of the remainder (fp32's 24 bits are
+// more than one image holds).  The four blocks of a warp share one accumulator: block j's low and
 // high digits occupy B columns 2j and 2j+1, so four s8 MMAs (K = 32 each) fill all eight
 // columns and lane (g, t) ends with block t's two digit sums for rows g and g + 8, exact in
 // int32.  The epilogue is one integer combine, one conversion and one FMA with
@@ -570,8 +571,11 @@ constexpr int kM1I8 = 2;     // s8 MMAs on 16 q and two-digit fixed-point activa
 // (X + 128) >> 8.  The factor 2^(E - 144) of each block (it undoes the scaling and the 16 of
 // the 16 q operands) goes to the factor table.  All loads come before all stores, so the four
 // blocks' dependency chains overlap.  An fp32 row keeps 128 bytes per block; its digits take
-// the first 64 of them (lane t's loads at bytes 16t.. and 64+16t.. feed the block's exponent,
-// which the quad shuffles before any lane stores, so no store lands on bytes still unread).
+// the first 64 of them, and the last 64 hold a second image of what the first leaves out:
+// R = x * 2^(140 - E) - X (exact, |R| <= 1/2) as X2 = rint(R * 2^15) in the same two-digit
+// form, so the pair carries x to 2^-30 of the block's largest value (fp32 keeps 2^-24 of
+// each value).  Lane t's loads at bytes 16t.. and 64+16t.. feed the block's exponent, which
+// the quad shuffles before any lane stores, so no store lands on bytes still unread.
 template <bool XF32>
 __device__ __forceinline__ float m1_x_elem(const uint2& lo, const uint2& hi, const uint4& lo4, const uint4& hi4, int i) {
     if constexpr (XF32) {
@@ -627,29 +631,44 @@ __device__ __forceinline__ void m1_digits_chunk(const GemvParams& p, uint8_t* sm
     for (int j = 0; j < J; ++j) e[j] = max(e[j], __shfl_xor_sync(0xffffffffu, e[j], 1));
 #pragma unroll
     for (int j = 0; j < J; ++j) e[j] = max(e[j], __shfl_xor_sync(0xffffffffu, e[j], 2));
-    uint32_t out[J][4];
+    uint32_t out[J][4], out2[J][4];   // out2: fp32 rows' second image
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         if (live[j] && e[j] == 255 && t == 0) record_device_error(kDevErrActRange);   // inf or NaN
         e[j] = max(e[j], 18);                                  // blocks below 2^-109: normal factors
         const float up = __int_as_float((267 - e[j]) << 23);   // 2^(140 - E)
-        uint32_t r[8], h[8];
+        uint32_t r[8], h[8], r2[8], h2[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float f = m1_x_elem<XF32>(lo[j], hi[j], lo4[j], hi4[j], i);
             r[i] = __float_as_uint(fmaf(f, up, 12582912.0f));   // 0x4B400000 + X
             h[i] = __float_as_uint(fmaf(f, up, 12583040.0f));   // 0x4B400000 + X + 128
+            if constexpr (XF32) {
+                const float rem = fmaf(f, up, -(__uint_as_float(r[i]) - 12582912.0f));   // R, exact
+                r2[i] = __float_as_uint(fmaf(rem, 32768.0f, 12582912.0f));
+                h2[i] = __float_as_uint(fmaf(rem, 32768.0f, 12583040.0f));
+            }
         }
         out[j][0] = prmt(prmt(r[0], r[1], 0x0040), prmt(r[2], r[3], 0x0040), 0x5410);
         out[j][1] = prmt(prmt(r[4], r[5], 0x0040), prmt(r[6], r[7], 0x0040), 0x5410);
         out[j][2] = prmt(prmt(h[0], h[1], 0x0051), prmt(h[2], h[3], 0x0051), 0x5410);
         out[j][3] = prmt(prmt(h[4], h[5], 0x0051), prmt(h[6], h[7], 0x0051), 0x5410);
+        if constexpr (XF32) {
+            out2[j][0] = prmt(prmt(r2[0], r2[1], 0x0040), prmt(r2[2], r2[3], 0x0040), 0x5410);
+            out2[j][1] = prmt(prmt(r2[4], r2[5], 0x0040), prmt(r2[6], r2[7], 0x0040), 0x5410);
+            out2[j][2] = prmt(prmt(h2[0], h2[1], 0x0051), prmt(h2[2], h2[3], 0x0051), 0x5410);
+            out2[j][3] = prmt(prmt(h2[4], h2[5], 0x0051), prmt(h2[6], h2[7], 0x0051), 0x5410);
+        }
     }
 #pragma unroll
     for (int j = 0; j < J; ++j) {
         if (!live[j]) continue;
         *reinterpret_cast<uint2*>(smem + xr[j] + 8 * t) = make_uint2(out[j][0], out[j][1]);
         *reinterpret_cast<uint2*>(smem + xr[j] + 32 + 8 * t) = make_uint2(out[j][2], out[j][3]);
+        if constexpr (XF32) {
+            *reinterpret_cast<uint2*>(smem + xr[j] + 64 + 8 * t) = make_uint2(out2[j][0], out2[j][1]);
+            *reinterpret_cast<uint2*>(smem + xr[j] + 96 + 8 * t) = make_uint2(out2[j][2], out2[j][3]);
+        }
         if (t == 0)
             *reinterpret_cast<float*>(smem + p.x_all_off + static_cast<uint32_t>(p.K) * kElem +
                                       (chunk * (kM1KC / 32) + 8 * j + g) * 4) = __int_as_float((e[j] - 17) << 23);
@@ -689,11 +708,25 @@ __device__ __forceinline__ uint32_t digit4f(uint4 v, float up, float magic, uint
     const uint32_t r3 = __float_as_uint(fmaf(__uint_as_float(v.w), up, magic));
     return prmt(prmt(r0, r1, sel), prmt(r2, r3, sel), 0x5410);
 }
+// The second image's digit of one raw fp32 activation: R = x * 2^(140 - E) - X, exact, then
+// rint(R * 2^15) through the same magic-number form.
+__device__ __forceinline__ uint32_t residual_digit(uint32_t v, float up, float magic) {
+    const float f = __uint_as_float(v);
+    const float x1 = __uint_as_float(__float_as_uint(fmaf(f, up, 12582912.0f))) - 12582912.0f;   // X
+    return __float_as_uint(fmaf(fmaf(f, up, -x1), 32768.0f, magic));
+}
+// The same, for four raw fp32 activations.
+__device__ __forceinline__ uint32_t residual4f(uint4 v, float up, float magic, uint32_t sel) {
+    const uint32_t r0 = residual_digit(v.x, up, magic), r1 = residual_digit(v.y, up, magic);
+    const uint32_t r2 = residual_digit(v.z, up, magic), r3 = residual_digit(v.w, up, magic);
+    return prmt(prmt(r0, r1, sel), prmt(r2, r3, sel), 0x5410);
+}
 
 // The weight side of one chunk in the integer mode for one warp: blocks blk0 .. blk0 + 3 of
 // box `box` (c0 = the box's first block of K) for the pass's nt tiles, accumulated into acc.
 // Lane (g, t) feeds B column g (digit g % 2 of block g / 2) and combines block t's two digit
-// sums for rows g and g + 8.
+// sums for rows g and g + 8.  fp32 rows run a second chain of the same A operands over the
+// second image's digits and add its sums with weight 2^-15.
 template <int TP, bool STMA, bool XF32>
 __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* smem, uint32_t st, int box, int blk0,
                                             int c0, int g, int t, int64_t row0, int64_t row_end,
@@ -702,7 +735,7 @@ __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* 
     constexpr uint32_t kElem = XF32 ? 4u : 2u;
     const int q = g >> 1;
     const int bb = c0 + blk0 + q, bt = c0 + blk0 + t;
-    uint2 dw;
+    uint2 dw, dw2 = make_uint2(0u, 0u);
     float ft;
     if (raw) {   // chunk 0: the digits from the raw row, here (the same arithmetic as m1_digits_chunk)
         const uint32_t xr = p.x_all_off + bb * kPitch + 4 * t * kElem;
@@ -725,26 +758,37 @@ __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* 
         const float up = __int_as_float((267 - e) << 23);
         const float magic = (g & 1) ? 12583040.0f : 12582912.0f;
         const uint32_t sel = (g & 1) ? 0x0051u : 0x0040u;
-        if constexpr (XF32) dw = make_uint2(digit4f(lo4, up, magic, sel), digit4f(hi4, up, magic, sel));
-        else dw = make_uint2(digit4(lo.x, lo.y, up, magic, sel), digit4(hi.x, hi.y, up, magic, sel));
+        if constexpr (XF32) {
+            dw = make_uint2(digit4f(lo4, up, magic, sel), digit4f(hi4, up, magic, sel));
+            dw2 = make_uint2(residual4f(lo4, up, magic, sel), residual4f(hi4, up, magic, sel));
+        } else {
+            dw = make_uint2(digit4(lo.x, lo.y, up, magic, sel), digit4(hi.x, hi.y, up, magic, sel));
+        }
         const int et = __shfl_sync(0xffffffffu, e, 8 * t);   // lane 8t built block t
         ft = bt < p.G ? __int_as_float((et - 17) << 23) : 0.0f;
     } else {
         dw = bb < p.G ? sh_u64(smem, p.x_all_off + bb * kPitch + (g & 1) * 32 + 8 * t) : make_uint2(0u, 0u);
+        if constexpr (XF32)
+            dw2 = bb < p.G ? sh_u64(smem, p.x_all_off + bb * kPitch + 64 + (g & 1) * 32 + 8 * t) : make_uint2(0u, 0u);
         ft = bt < p.G ? *reinterpret_cast<const float*>(smem + p.x_all_off + static_cast<uint32_t>(p.K) * kElem + bt * 4)
                       : 0.0f;
     }
-    uint32_t bq[4][2];
+    uint32_t bq[4][2], bq2[4][2];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         bq[j][0] = q == j ? dw.x : 0u;
         bq[j][1] = q == j ? dw.y : 0u;
         asm volatile("" : "+r"(bq[j][0]), "+r"(bq[j][1]));   // keep them in registers
+        if constexpr (XF32) {
+            bq2[j][0] = q == j ? dw2.x : 0u;
+            bq2[j][1] = q == j ? dw2.y : 0u;
+            asm volatile("" : "+r"(bq2[j][0]), "+r"(bq2[j][1]));
+        }
     }
     const uint32_t wbox = st + box * p.w_box_bytes;
 #pragma unroll
     for (int i = 0; i < TP; ++i) {
-        int d[4] = {0, 0, 0, 0};
+        int d[4] = {0, 0, 0, 0}, d2[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint32_t wt = wbox + i * (kTileRows * 128) + woff[j];
@@ -753,8 +797,13 @@ __device__ __forceinline__ void m1_i8_stage(const GemvParams& p, const uint8_t* 
             const uint32_t a[4] = {(w0 << 4) & 0xF0F0F0F0u, (w8 << 4) & 0xF0F0F0F0u, w0 & 0xF0F0F0F0u,
                                    w8 & 0xF0F0F0F0u};
             mma_s8(d, a, bq[j][0], bq[j][1]);
+            if constexpr (XF32) mma_s8(d2, a, bq2[j][0], bq2[j][1]);
         }
-        const float v0 = static_cast<float>(d[0] + d[1] * 256), v8 = static_cast<float>(d[2] + d[3] * 256);
+        float v0 = static_cast<float>(d[0] + d[1] * 256), v8 = static_cast<float>(d[2] + d[3] * 256);
+        if constexpr (XF32) {   // the second image: |sum| <= 2^26, exact in int32
+            v0 = fmaf(static_cast<float>(d2[0] + d2[1] * 256), 1.0f / 32768.0f, v0);
+            v8 = fmaf(static_cast<float>(d2[2] + d2[3] * 256), 1.0f / 32768.0f, v8);
+        }
         float sg, sg8;
         if constexpr (STMA) {
             const uint32_t sa = st + p.s_off + (i * kTileRows + g) * p.s_pitch + (box * 8 + blk0 + t) * 2;
@@ -1051,16 +1100,6 @@ int m1_mode() {
     return mode;
 }
 
-// BYBY_CUDA_GEMV_M1=i8f32: fp32 decode rows in the integer mode too (faster, 15-bit
-// activations relative to each block's largest value).
-bool m1_fp32_digits() {
-    static const bool on = [] {
-        const char* e = getenv("BYBY_CUDA_GEMV_M1");
-        return e && !strcmp(e, "i8f32");
-    }();
-    return on;
-}
-
 template <int TP, bool STMA>
 int launch_m1(int mode, bool xf32, const GemvMaps& maps, const GemvParams& p, int grid, size_t smem,
               cudaStream_t stream) {
@@ -1208,14 +1247,12 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     const int xe = xf32 ? 4 : 2;
     const int n_tiles = static_cast<int>(ceil_div(a.N, kTileRows));
     const int grid = std::min(n_tiles, dev.sm_count);
-    // the M = 1 kernel takes bf16 rows.  fp32 rows take the general kernel's two bf16 terms
-    // (16 significant bits per value): the integer mode's 15-bit fixed point, relative to each
-    // block's largest value, left up to 2.1e-3 per element on N(0, 1) fp32 rows at K = 11008,
-    // against 1.0e-4 with the two terms (C2 with fp32 x: 14.2 against 7.3 us).  The integer
-    // mode still takes fp32 rows when BYBY_CUDA_GEMV_M1=i8f32 asks for the faster form.
+    // The M = 1 kernel takes bf16 rows in every operand mode and fp32 rows in the integer mode
+    // (two fixed-point images, 2^-30 of each block's largest value).  The fp16 / bf16 modes
+    // have no fp32 form: there fp32 rows take the general kernel's two bf16 terms.
     const int want_mode = a.variant >= kM1Bf16 && a.variant <= kM1I8 ? a.variant : m1_mode();
     const int mode = want_mode == kM1I8 && a.K > 32768 ? kM1F16 : want_mode;
-    const bool m1 = a.M == 1 && (!xf32 || (mode == kM1I8 && m1_fp32_digits()));
+    const bool m1 = a.M == 1 && (!xf32 || mode == kM1I8);
     // M = 1 splits rows, not tiles: 11008 rows over 148 CTAs is 74 or 75 rows each instead of 4
     // or 5 tiles (64 or 80 rows), so no CTA streams 6% more than its share and all end together
     const int rows_base = a.N / grid, rows_extra = a.N % grid;

@@ -573,10 +573,12 @@ int bybycu_prepare_tile_gemm_tuned(int fmt, int x_dtype, int M, int K, int N, co
                 for (int st : {2, 3})
                     cands.push_back({make_plan(BYBYCU_ROUTE_GEMV, f.mode, st, "gemv-%s-st%d", f.tag, st), kTolNarrow});
             }
-        } else if (mc == 1) {   // fp32 rows: the general kernel's two-term split at a few ring depths
-            cands.push_back({make_plan(BYBYCU_ROUTE_GEMV, -1, 0, "gemv-split"), kTolNarrow});
-            for (int st : {2, 3})
-                cands.push_back({make_plan(BYBYCU_ROUTE_GEMV, -1, st, "gemv-split-st%d", st), kTolNarrow});
+        } else if (mc == 1) {   // fp32 rows: the integer mode's two images, or the general kernel's
+                                // two bf16 terms (the bf16 operand mode has no fp32 form)
+            if (K <= 32768)
+                for (int st : {2, 3})
+                    cands.push_back({make_plan(BYBYCU_ROUTE_GEMV, kM1I8, st, "gemv-s8x2-st%d", st), kTolNarrow});
+            cands.push_back({make_plan(BYBYCU_ROUTE_GEMV, kM1Bf16, 0, "gemv-split"), kTolNarrow});
         } else {
             cands.push_back({make_plan(BYBYCU_ROUTE_GEMV, -1, 0, "gemv-stmax"), kTolNarrow});
             for (int st : {2, 3})

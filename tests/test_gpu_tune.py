@@ -70,7 +70,8 @@ def test_q4b32_decode_plan_is_used_and_correct():
     # preparing again is a table hit, not a second tune
     assert w.prepare(1)
     assert gb.q4TuningStats()[0] == 1
-    # fp32 rows have their own plan (the GEMV's two-term form for fp32 activations)
+    # fp32 rows have their own plan (the integer mode's two images, or the general kernel's
+    # two bf16 terms)
     assert gb.tunedPlan(_lib.OP_TILE_GEMM, fmt=_lib.FMT_Q4B32, x_dtype=_lib.DT_F32, M=1, K=K, N=N) is None
     assert w.prepare(1, _lib.DT_F32)
     plan32 = gb.tunedPlan(_lib.OP_TILE_GEMM, fmt=_lib.FMT_Q4B32, x_dtype=_lib.DT_F32, M=1, K=K, N=N)
@@ -164,6 +165,25 @@ def test_hand_installed_plan_and_removal():
     _lib.call("bybycu_plan_set", _lib.OP_TILE_GEMM, _lib.FMT_Q4B32, _lib.DT_BF16, M, K, N, 0, 0, None)
     assert gb.tunedPlan(_lib.OP_TILE_GEMM, fmt=_lib.FMT_Q4B32, M=M, K=K, N=N) is None
     assert gb.route_for(_lib.FMT_Q4B32, M, K, N) == _lib.ROUTE_GEMV
+
+
+def test_fp32_decode_general_kernel_plan():
+    """A plan with variant 0 (the bf16 operand mode, which has no fp32 form) sends fp32 decode
+    rows to the general kernel's two bf16 terms; within 1e-3 per element of the oracle too."""
+    K, N = 4096, 2048
+    p, s, w = q4b32_weights(N, K, seed=5)
+    xf = O.gen_x_f32(1, K, seed=6)
+    want = O.tile_gemm_q4b32(xf, p, s, 1, K, N)
+    x = torch.from_numpy(xf).to(DEV)
+    plan = _lib.Plan(route=_lib.ROUTE_GEMV, variant=0, stages=0, ms=0.0, name=b"gemv-split")
+    _lib.call("bybycu_plan_set", _lib.OP_TILE_GEMM, _lib.FMT_Q4B32, _lib.DT_F32, 1, K, N, 0, 0, plan)
+    got = w.matmul(x).cpu().numpy().astype(np.float64)
+    _lib.call("bybycu_plan_set", _lib.OP_TILE_GEMM, _lib.FMT_Q4B32, _lib.DT_F32, 1, K, N, 0, 0, None)
+    d = np.abs(got - want) / np.maximum(1.0, np.abs(want))
+    assert d.max() <= 1e-3, d.max()
+    # the default (integer mode, two images) agrees with it to within both errors
+    dflt = w.matmul(x).cpu().numpy().astype(np.float64)
+    assert (np.abs(dflt - want) / np.maximum(1.0, np.abs(want))).max() <= 1e-4
 
 
 def test_switches_and_untunable_format(monkeypatch):

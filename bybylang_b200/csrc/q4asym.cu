@@ -12,10 +12,13 @@
 //     an m16n8k32 s8 MMA in the K order (slot s < 16 -> k = 2s, slot 16 + s -> k = 2s + 1);
 //   * x becomes X = rint(x * 2^(140 - E)) per 32-block (E its largest fp32 exponent, |X| <=
 //     2^14) in two signed byte digits laid out in the same K order, four blocks x two digits
-//     filling the MMA's eight columns;
-//   * per row and block the epilogue adds s * 2^(E-140) * (sum u X - z * sum X): the zero point
-//     enters through the block's sum of X (the s (dot(a, u) - z sum(a)) factorisation of the
-//     reference's GPU kernels).
+//     filling the MMA's eight columns; the remainder R = x * 2^(140 - E) - X (exact, |R| <= 1/2)
+//     becomes a second image X2 = rint(R * 2^15) in the same form, fed to a second chain of
+//     MMAs on the same A registers, so x is carried to 2^-29 of its block's largest value
+//     (one image, 15 bits, left fp32 rows outside 1e-3 per element near zero outputs);
+//   * per row and block the epilogue adds s * 2^(E-140) * ((sum u X - z * sum X) + 2^-15 *
+//     (sum u X2 - z * sum X2)): the zero point enters through the block's sums of X and X2 (the
+//     s (dot(a, u) - z sum(a)) factorisation of the reference's GPU kernels).
 // Everything else (any M, any group size, odd K, unaligned slots) runs q4a_exact_kernel: one
 // thread per output, fmaf(x, (u - z) * s, sum) in k order (the CPU VM's OP_Q4_GEMV arithmetic).
 //
@@ -261,33 +264,44 @@ __global__ void __launch_bounds__(kM1Threads, 1) q4a_kernel(const __grid_constan
             if (live && e == 255 && t == 0 && !(g & 1)) record_device_error(kDevErrActRange);
             const int ec = max(e, 14);                               // normal factors 2^(ec - 140)
             const float up = __int_as_float((267 - ec) << 23);       // 2^(140 - ec)
-            uint32_t r[8];
-            int sx = 0;
+            uint32_t r[8], r2[8];
+            int sx = 0, sx2 = 0;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                r[i] = __float_as_uint(fmaf(__uint_as_float(xv[i]), up, magic));   // bits + X
+                const float f = __uint_as_float(xv[i]);
+                r[i] = __float_as_uint(fmaf(f, up, magic));   // bits + X
                 sx += static_cast<int>(r[i]) - x_off_bits;
+                const float rem = fmaf(f, up, -(__uint_as_float(r[i]) - magic));   // R, exact
+                r2[i] = __float_as_uint(fmaf(rem, 32768.0f, magic));              // bits + X2
+                sx2 += static_cast<int>(r2[i]) - x_off_bits;
             }
             const uint32_t b0 = prmt(prmt(r[0], r[2], sel), prmt(r[4], r[6], sel), 0x5410);   // k = 8t + 2i
             const uint32_t b1 = prmt(prmt(r[1], r[3], sel), prmt(r[5], r[7], sel), 0x5410);   // k = 8t + 2i + 1
+            const uint32_t c0r = prmt(prmt(r2[0], r2[2], sel), prmt(r2[4], r2[6], sel), 0x5410);
+            const uint32_t c1r = prmt(prmt(r2[1], r2[3], sel), prmt(r2[5], r2[7], sel), 0x5410);
             sx += __shfl_xor_sync(0xffffffffu, sx, 1);
             sx += __shfl_xor_sync(0xffffffffu, sx, 2);   // sum of X over block q
-            uint32_t bq[4][2];
+            sx2 += __shfl_xor_sync(0xffffffffu, sx2, 1);
+            sx2 += __shfl_xor_sync(0xffffffffu, sx2, 2);   // sum of X2 over block q
+            uint32_t bq[4][2], bq2[4][2];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 bq[j][0] = q == j ? b0 : 0u;
                 bq[j][1] = q == j ? b1 : 0u;
-                asm volatile("" : "+r"(bq[j][0]), "+r"(bq[j][1]));   // keep them in registers
+                bq2[j][0] = q == j ? c0r : 0u;
+                bq2[j][1] = q == j ? c1r : 0u;
+                asm volatile("" : "+r"(bq[j][0]), "+r"(bq[j][1]), "+r"(bq2[j][0]), "+r"(bq2[j][1]));   // keep them in registers
             }
-            // lane (g, t) combines block t (built by lane 8t): its factor and its sum of X
+            // lane (g, t) combines block t (built by lane 8t): its factor and its sums of X, X2
             const int et = __shfl_sync(0xffffffffu, ec, 8 * t);
             const float ft = __int_as_float((et - 13) << 23);   // 2^(et - 140)
             const float sxt = static_cast<float>(__shfl_sync(0xffffffffu, sx, 8 * t));
+            const float sxt2 = static_cast<float>(__shfl_sync(0xffffffffu, sx2, 8 * t));
             const uint32_t wbox = st + box * p.w_box_bytes;
-            // ---- weights: four s8 MMAs per tile fill the eight columns
+            // ---- weights: four s8 MMAs per tile and image fill the eight columns
 #pragma unroll
             for (int i = 0; i < TP; ++i) {
-                int d[4] = {0, 0, 0, 0};
+                int d[4] = {0, 0, 0, 0}, d2[4] = {0, 0, 0, 0};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const uint32_t wt = wbox + i * (kTileRows * 128) + woff[j];
@@ -296,8 +310,11 @@ __global__ void __launch_bounds__(kM1Threads, 1) q4a_kernel(const __grid_constan
                     const uint32_t a[4] = {w0 & 0x0F0F0F0Fu, w8 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
                                            (w8 >> 4) & 0x0F0F0F0Fu};
                     mma_s8(d, a, bq[j][0], bq[j][1]);
+                    mma_s8(d2, a, bq2[j][0], bq2[j][1]);
                 }
+                // sum u X and sum u X2 are below 2^23 in magnitude: exact as floats
                 const float v0 = static_cast<float>(d[0] + d[1] * 256), v8 = static_cast<float>(d[2] + d[3] * 256);
+                const float u0 = static_cast<float>(d2[0] + d2[1] * 256), u8 = static_cast<float>(d2[2] + d2[3] * 256);
                 // scale and zero point of block t for rows g and g + 8 (128-byte swizzled boxes)
                 const int cb = box * 8 + blk0 + t;   // block inside the chunk: 16-byte column cb / 4
                 const uint32_t r0 = i * kTileRows + g, r8 = r0 + 8;
@@ -307,8 +324,10 @@ __global__ void __launch_bounds__(kM1Threads, 1) q4a_kernel(const __grid_constan
                 const float z0 = *reinterpret_cast<const float*>(smem + st + p.z_off + o0);
                 const float s8 = *reinterpret_cast<const float*>(smem + st + p.s_off + o8);
                 const float z8 = *reinterpret_cast<const float*>(smem + st + p.z_off + o8);
-                acc[i][0] = fmaf(s0 * ft, fmaf(-z0, sxt, v0), acc[i][0]);
-                acc[i][1] = fmaf(s8 * ft, fmaf(-z8, sxt, v8), acc[i][1]);
+                const float y0 = fmaf(fmaf(-z0, sxt2, u0), 1.0f / 32768.0f, fmaf(-z0, sxt, v0));
+                const float y8 = fmaf(fmaf(-z8, sxt2, u8), 1.0f / 32768.0f, fmaf(-z8, sxt, v8));
+                acc[i][0] = fmaf(s0 * ft, y0, acc[i][0]);
+                acc[i][1] = fmaf(s8 * ft, y8, acc[i][1]);
             }
         }
         __syncwarp();

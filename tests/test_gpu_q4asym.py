@@ -6,10 +6,10 @@ into oracle/_ref, and its restatement in the oracle port.  Data: interleaved nib
 
 Tolerances (written here):
 * decode kernel (route AUTO at M = 1, group 32): the reference test's max|diff| <= 1e-4 *
-  max(1, max|ref|), and per element its fixed-point bound against float64,
-  |diff| <= 2^-14 * sum_b max|x_b| * sum_{k in b} |w[n, k]| plus fp32 slack, on inputs of any
-  dynamic range.  (fp32 activations are rounded to 15-bit fixed point per 32-block, so the
-  1e-3 per-element bound of the bf16 decode path does not hold near zero outputs.)
+  max(1, max|ref|), the north star's 1e-3 per element (|diff| / max(1, |ref|)), and per
+  element its fixed-point bound against float64,
+  |diff| <= 2^-29 * sum_b max|x_b| * sum_{k in b} |w[n, k]| plus fp32 slack, on inputs of any
+  dynamic range (fp32 activations travel as two fixed-point images per 32-block).
 * exact kernel (route SIMT, and AUTO for every other shape): the same bounds against the
   reference (its k-order fmaf differs from nimf_cpu_matmul_q4's evaluation order only by
   fp32 rounding).
@@ -26,7 +26,7 @@ torch = pytest.importorskip("torch")
 from bybylang_b200 import _lib  # noqa: E402
 from bybylang_b200 import gpubackend as gb  # noqa: E402
 
-from gpu_helpers import DEV, assert_close  # noqa: E402
+from gpu_helpers import DEV, assert_close, elem_err  # noqa: E402
 
 PEAK_TOL, ELEM_TOL = 1e-4, 1e-3
 
@@ -71,13 +71,13 @@ def dequant_np(wq, scales, zeros, K, group):
 
 
 def assert_fixed_point_bound(x, wq, scales, zeros, K, got):
-    """Per element against float64: |diff| <= 2^-14 sum_b max|x_b| sum_{k in b} |w| + slack."""
+    """Per element against float64: |diff| <= 2^-29 sum_b max|x_b| sum_{k in b} |w| + slack."""
     N = wq.shape[0]
     w = dequant_np(wq, scales, zeros, K, 32)
     xd = x.astype(np.float64)
     want = w @ xd
     blk_max = np.abs(xd).reshape(-1, 32).max(axis=1)
-    quant = 2.0 ** -14 * (np.abs(w).reshape(N, -1, 32).sum(axis=2) * blk_max).sum(axis=1)
+    quant = 2.0 ** -29 * (np.abs(w).reshape(N, -1, 32).sum(axis=2) * blk_max).sum(axis=1)
     slack = 1e-5 * (np.abs(w) * np.abs(xd)).sum(axis=1) + 1e-30
     err = np.abs(np.asarray(got, np.float64) - want)
     assert np.isfinite(got).all()
@@ -85,13 +85,15 @@ def assert_fixed_point_bound(x, wq, scales, zeros, K, got):
 
 
 @pytest.mark.parametrize("K,N", [(4096, 11008), (4096, 4096), (11008, 4096), (128, 1), (1152, 17), (2048, 300)])
-def test_decode_kernel_against_reference(K, N, oracle_mod):
+def test_decode_kernel_against_reference(K, N, oracle_mod, parity_log):
     O = oracle_mod
     a, wq, scales, zeros = gen_q4(1, K, N, seed=K + N)
     want = O.ref_matmul_q4(a, wq, scales, zeros, 1, K, N, 32, threads=8)
     got = run_q4(a, wq, scales, zeros, 1, K, N, 32, route=_lib.ROUTE_GEMV)
-    assert_close(want, got, PEAK_TOL, None, f"K={K} N={N}")
-    assert_close(O.matmul_q4_asym(a, wq, scales, zeros, 1, K, N, 32), got, PEAK_TOL, None, "port")
+    assert_close(want, got, PEAK_TOL, ELEM_TOL, f"K={K} N={N}")
+    if N >= 1024:
+        parity_log.append((f"asym Q4 1x{K}x{N} fp32 x, decode kernel (two images)", elem_err(want, got), ELEM_TOL))
+    assert_close(O.matmul_q4_asym(a, wq, scales, zeros, 1, K, N, 32), got, PEAK_TOL, ELEM_TOL, "port")
     assert_fixed_point_bound(a[0], wq, scales, zeros, K, got[0])
 
 
@@ -100,7 +102,7 @@ def test_decode_kernel_integer_zero_points(oracle_mod):
     K, N = 4096, 2048
     a, wq, scales, zeros = gen_q4(1, K, N, seed=3, integer_zeros=True)
     got = run_q4(a, wq, scales, zeros, 1, K, N, 32)
-    assert_close(O.ref_matmul_q4(a, wq, scales, zeros, 1, K, N, 32, threads=8), got, PEAK_TOL, None)
+    assert_close(O.ref_matmul_q4(a, wq, scales, zeros, 1, K, N, 32, threads=8), got, PEAK_TOL, ELEM_TOL)
     assert_fixed_point_bound(a[0], wq, scales, zeros, K, got[0])
 
 
@@ -137,15 +139,18 @@ TC_TOL = 1e-3   # the tensor-core route: weights and activations rounded once to
 
 
 @pytest.mark.parametrize("M,K,N", [(64, 4096, 2048), (200, 1024, 300), (2, 256, 40), (129, 2048, 513)])
-def test_tensor_core_prefill_against_reference(M, K, N, oracle_mod):
+def test_tensor_core_prefill_against_reference(M, K, N, oracle_mod, parity_log):
     """M > 1, group 32, K % 256 == 0: AUTO takes the tcgen05 GEMM (the same kernel as the
     Q4B32 prefill, dequantising w = RNE16(u s - z s)); checked with the reference test's metric
-    at the tensor-core tolerance, and explicit route TC gives the same bits."""
+    at the tensor-core tolerance (the reference's own gate for its matrix-unit Q4 plans is
+    3e-3 of the peak, backends/vulkan/q4_autotune.nim:506), and explicit route TC gives the
+    same bits.  The per-element error is logged, not bounded: fp16 rounding of s, z s and x."""
     O = oracle_mod
     a, wq, scales, zeros = gen_q4(M, K, N, seed=M + K + N)
     want = O.ref_matmul_q4(a, wq, scales, zeros, M, K, N, 32, threads=8)
     got = run_q4(a, wq, scales, zeros, M, K, N, 32)
     assert_close(want, got, TC_TOL, None, f"M={M} K={K} N={N}")
+    parity_log.append((f"asym Q4 {M}x{K}x{N} fp32 x, route TC (one fp16 rounding)", elem_err(want, got), 0.0))
     assert np.array_equal(got, run_q4(a, wq, scales, zeros, M, K, N, 32, route=_lib.ROUTE_TC))
     assert _lib.device_error() == 0
 
@@ -234,7 +239,7 @@ def _bound(w, x):
     """The decode kernel's per-element fixed-point bound for W . x (float64 arrays)."""
     N = w.shape[0]
     blk_max = np.abs(x).reshape(-1, 32).max(axis=1)
-    quant = 2.0 ** -14 * (np.abs(w).reshape(N, -1, 32).sum(axis=2) * blk_max).sum(axis=1)
+    quant = 2.0 ** -29 * (np.abs(w).reshape(N, -1, 32).sum(axis=2) * blk_max).sum(axis=1)
     return quant + 1e-5 * (np.abs(w) * np.abs(x)).sum(axis=1) + 1e-30
 
 

@@ -40,6 +40,7 @@
 
 #include "kernels.h"
 
+#include <atomic>
 #include <mutex>
 
 namespace bybycu {
@@ -1066,12 +1067,13 @@ bool pdl_enabled() {
 template <int TP, int NT, bool XF32, bool STMA, int W>
 int launch_t(const GemvMaps& maps, const GemvParams& p, int grid, size_t smem, cudaStream_t stream) {
     auto kern = gemv_q4b32_kernel<TP, NT, XF32, STMA, W>;
-    static uint64_t configured = 0;   // per device: the opt-in smem limit is a function attribute
+    static std::atomic<uint64_t> configured{0};   // per device: the opt-in smem limit is a function attribute
     int dev = 0;
     BYBYCU_CUDA_TRY(cudaGetDevice(&dev));
-    if (!(configured >> (dev & 63) & 1)) {
+    if (dev < 0 || dev >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", dev);
+    if (!(configured.load(std::memory_order_acquire) >> dev & 1)) {
         BYBYCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
-        configured |= uint64_t(1) << (dev & 63);
+        configured.fetch_or(uint64_t(1) << dev, std::memory_order_release);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -1105,13 +1107,14 @@ int launch_m1(int mode, bool xf32, const GemvMaps& maps, const GemvParams& p, in
               cudaStream_t stream) {
     auto kern = mode == kM1I8 ? (xf32 ? gemv_m1_kernel<TP, STMA, kM1I8, true> : gemv_m1_kernel<TP, STMA, kM1I8>)
               : mode == kM1F16 ? gemv_m1_kernel<TP, STMA, kM1F16> : gemv_m1_kernel<TP, STMA, kM1Bf16>;
-    static uint64_t configured[4] = {0, 0, 0, 0};
+    static std::atomic<uint64_t> configured[4];   // per operand form, per device (zero-initialised)
     int dev = 0;
     BYBYCU_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", dev);
     const int fi = xf32 ? 3 : mode;
-    if (!(configured[fi] >> (dev & 63) & 1)) {
+    if (!(configured[fi].load(std::memory_order_acquire) >> dev & 1)) {
         BYBYCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
-        configured[fi] |= uint64_t(1) << (dev & 63);
+        configured[fi].fetch_or(uint64_t(1) << dev, std::memory_order_release);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);

@@ -502,9 +502,10 @@ int launch_q4a_fused(const Q4aFused& f, cudaStream_t stream) {
                                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
                 return rc;
         }
-    static std::once_flag once[16];
-    static cudaError_t attr_rc[16];
-    const int di = dev.device & 15;
+    static std::once_flag once[64];
+    static cudaError_t attr_rc[64];
+    const int di = dev.device;
+    if (di < 0 || di >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", di);
     std::call_once(once[di], [&] {
         attr_rc[di] = cudaFuncSetAttribute(q4a_kernel<kQ4aTP, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
         if (attr_rc[di] == cudaSuccess)

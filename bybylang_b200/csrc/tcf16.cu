@@ -228,10 +228,11 @@ int launch_tc_f16(const GemmArgs& a) {
                                            "weights (M=%d K=%d N=%d)", a.M, a.K, a.N);
     DeviceInfo info;
     if (int rc = current_device_info(&info)) return rc;
-    static std::once_flag once[16];
-    static cudaError_t prep_rc[16];
-    static int max_pairs[16];
-    const int dev = info.device & 15;
+    static std::once_flag once[64];
+    static cudaError_t prep_rc[64];
+    static int max_pairs[64];
+    const int dev = info.device;
+    if (dev < 0 || dev >= 64) return set_error(BYBYCU_ERR_ARGS, "device %d out of range", dev);
     std::call_once(once[dev], [&] {
         prep_rc[dev] = cudaFuncSetAttribute(tc::gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             static_cast<int>(tc::kF16SmemBytes));

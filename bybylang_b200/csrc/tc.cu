@@ -112,7 +112,11 @@ struct Cfg {
     static constexpr uint32_t kOffBar = kOffS + kWStages * kSBytes;
     static constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
     static constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
-    static constexpr uint32_t kUsed = kOffAbort + 4 + 1024;   // + alignment slack
+    // the epilogue's output staging: one chunk (up to 32 tokens x 32 fp32 features) per
+    // epilogue warp, written back to the output rows with 16-byte stores
+    static constexpr uint32_t kEpiWarpBytes = (BN < 32 ? BN : 32) * 32 * 4;
+    static constexpr uint32_t kOffEpi = (kOffAbort + 4 + 15) / 16 * 16;
+    static constexpr uint32_t kUsed = kOffEpi + 4 * kEpiWarpBytes + 1024;   // + alignment slack
     // more than half an SM's shared memory: one CTA per SM, so that no second CTA waits for
     // the tensor memory this one allocates
     static constexpr uint32_t kSmemBytes = kUsed > 117 * 1024 ? kUsed : 117 * 1024;
@@ -564,11 +568,21 @@ template <int BN, int ACCB>
 __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem, uint64_t* d_full,
                                                  uint64_t* d_empty, volatile int* s_abort, int my_tiles, int pair,
                                                  int pairs, uint32_t rank, int quarter, int lane,
-                                                 uint32_t stage_smem = 0, int max_slots = 0) {
+                                                 uint32_t stage_smem = 0, int max_slots = 0,
+                                                 uint8_t* stage_gen = nullptr, uint8_t* epi_gen = nullptr) {
     constexpr int kChunk = BN < 32 ? BN : 32;
     constexpr int kBlock = BN * 32;   // floats of one warp's partial sums (BN tokens x 32 features)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t lead_d_empty = map_to_rank(d_empty, 0);
+    // Output chunks go through this warp's staging block when every 16-byte store is aligned:
+    // a store instruction then writes 4 (fp32) or 8 (bf16) output rows of 128 / 64 contiguous
+    // bytes instead of one strided value per lane (the strided form took ~1.2 us per chunk of
+    // 32 tokens at 4096 columns, 4x the same stores into a contiguous block).
+    const int esz = p.out_bf16 ? 2 : 4;
+    const bool staged = epi_gen != nullptr && !p.x_split && p.pg.world <= 1 &&
+                        reinterpret_cast<uintptr_t>(p.out) % 16 == 0 && (p.out_ld * esz) % 16 == 0 &&
+                        (p.out_col0 * esz) % 16 == 0;
+    uint8_t* const epi = staged ? epi_gen + quarter * (kChunk * 32 * 4) : nullptr;
     for (int t = 0; t < my_tiles; ++t) {
         const int b = t % ACCB, u = t / ACCB;
         const int unit = pair + t * pairs;
@@ -596,7 +610,12 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
         // this unit's MMAs completed (a tail unit is its pair's last), `max_slots` blocks per
         // warp.  Every block of a batch is fetched at once (one round trip per batch; one batch
         // when the parts fit); a later batch first folds the slots into slot 0, in part order.
-        const uint32_t slot0 = stage_smem + static_cast<uint32_t>(quarter * max_slots) * (kBlock * 4);
+        // The sums read the slots with plain loads (stage_gen is stage_smem's generic address),
+        // so the compiler keeps many in flight: asm loads with a memory clobber issued one
+        // dependent chain per token and left a 4-part finisher ~9 us behind the other CTAs.
+        const uint32_t slot_off = static_cast<uint32_t>(quarter * max_slots) * (kBlock * 4);
+        const uint32_t slot0 = stage_smem + slot_off;
+        float* const slots = reinterpret_cast<float*>(stage_gen + slot_off);   // [max_slots][kBlock]
         int active = 0;   // slots holding parts still to add, slot 0 first
         if (tail && last) {
             auto fetch = [&](int q, int slot) {
@@ -614,12 +633,12 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
             while (done < parts) {
                 cp_async_wait<0>();
                 __syncwarp();
-#pragma unroll 4
+#pragma unroll 8
                 for (int tk = 0; tk < BN; ++tk) {
-                    const uint32_t o = static_cast<uint32_t>(tk * 32 + lane) * 4;
-                    float sum = lds_f32(slot0 + o);
-                    for (int k = 1; k < active; ++k) sum += lds_f32(slot0 + k * (kBlock * 4) + o);
-                    sts_f32(slot0 + o, sum);
+                    const int o = tk * 32 + lane;
+                    float sum = slots[o];
+                    for (int k = 1; k < active; ++k) sum += slots[k * kBlock + o];
+                    slots[o] = sum;
                 }
                 __syncwarp();
                 const int nb = min(max_slots - 1, parts - done);
@@ -647,12 +666,42 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
             if (tail)   // the other parts in part order, then this part's
 #pragma unroll
                 for (int j = 0; j < kChunk; ++j) {
-                    const uint32_t o = static_cast<uint32_t>((c0 + j) * 32 + lane) * 4;
-                    float sum = lds_f32(slot0 + o);
-                    for (int k = 1; k < active; ++k) sum += lds_f32(slot0 + k * (kBlock * 4) + o);
+                    const int o = (c0 + j) * 32 + lane;
+                    float sum = slots[o];
+                    for (int k = 1; k < active; ++k) sum += slots[k * kBlock + o];
                     v[j] = __float_as_uint(sum + __uint_as_float(v[j]));
                 }
-            if (feat_ok && p.x_split) {   // row pairs (x_hi, x_lo): one output row each
+            const int f0 = feat - lane;   // this warp's first feature
+            if (staged && f0 + 32 <= p.N) {
+                const int nt = min(kChunk, p.M - (tok0 + c0));
+                const int64_t row0 = static_cast<int64_t>(tok0 + c0) * p.out_ld + p.out_col0 + f0;
+                if (p.out_bf16) {   // [kChunk][32] bf16, then 8 rows of 64 bytes per store
+                    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(epi);
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j) st[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[j]));
+                    __syncwarp();
+#pragma unroll
+                    for (int r = 0; r < kChunk / 8; ++r) {
+                        const int j = r * 8 + (lane >> 2), f = (lane & 3) * 8;
+                        if (j < nt)
+                            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + row0 + j * p.out_ld + f) =
+                                *reinterpret_cast<const uint4*>(st + j * 32 + f);
+                    }
+                } else {            // [kChunk][32] fp32, then 4 rows of 128 bytes per store
+                    float* st = reinterpret_cast<float*>(epi);
+#pragma unroll
+                    for (int j = 0; j < kChunk; ++j) st[j * 32 + lane] = __uint_as_float(v[j]);
+                    __syncwarp();
+#pragma unroll
+                    for (int r = 0; r < kChunk / 4; ++r) {
+                        const int j = r * 4 + (lane >> 3), f = (lane & 7) * 4;
+                        if (j < nt)
+                            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + row0 + j * p.out_ld + f) =
+                                *reinterpret_cast<const float4*>(st + j * 32 + f);
+                    }
+                }
+                __syncwarp();   // the block is read before the next chunk overwrites it
+            } else if (feat_ok && p.x_split) {   // row pairs (x_hi, x_lo): one output row each
                 const int nt = min(kChunk, p.M - (tok0 + c0));
                 const int64_t o0 = p.out_col0 + feat + static_cast<int64_t>((tok0 + c0) >> 1) * p.out_ld;
 #pragma unroll
@@ -1025,7 +1074,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         constexpr int kSlots = 2;
         static_assert(4 * kSlots * BN * 32 * 4 <= L::kOffBar, "split-K sums: two blocks per warp");
         epilogue_tiles_t<BN, L::kAccBufs>(p, tmem, d_full, d_empty, s_abort, my_units, pair, pairs, rank, warp & 3,
-                                          lane, base, kSlots);
+                                          lane, base, kSlots, smem, smem + L::kOffEpi);
     }
     tc_fence_before();
     __syncthreads();

@@ -4,8 +4,8 @@
 ## after the `SessionHandle` and `ResidentWeightHandle` type sections, so it sees their fields
 ## (`cudaHandle: CudaResidentTensor`, `cudaWq/cudaScales/cudaZeros`), `GpuBackend`,
 ## `gForbidCpuFallback` and `handleGpuFailure`.  It defines `cuda*` procs only; each public
-## session proc of gpubackend.nim gains a one-line branch that calls its twin here (the list is
-## in INTEGRATION.md).  It holds no state of its own: device pointers live in the handles,
+## session proc of gpubackend.nim gains a one-line branch that calls its twin here (cudaXxx for
+## each public proc Xxx).  It holds no state of its own: device pointers live in the handles,
 ## and every failure raises through handleGpuFailure (the cuda path never falls back to the
 ## CPU; gForbidCpuFallback is forced on at init).
 ##

@@ -135,11 +135,12 @@ int choose_route(const GemmArgs& a, int requested, int* route) {
     if (requested != BYBYCU_ROUTE_AUTO) return set_error(BYBYCU_ERR_ARGS, "unknown route %d", requested);
     // GEMV up to 16 rows, the tensor cores above (fp32 rows enter them as two fp16 terms: C1,
     // 32 fp32 rows of 4096 x 4096, 19.3 us against 28.3 on the GEMV, measured on one B200).
-    // Except where the GEMV's cost per row is highest: bf16 rows from 8 on with K >= 8192
-    // (4096 x 11008 at M = 16: 21.9 us on the tensor cores against 31.9, at M = 8 21.8
-    // against 22.6, at M = 4 21.7 against 18.5), and from 12 on with N >= 65536
-    // (128256 x 4096 at M = 16: 120 against 158 us).
-    const bool tc_rows = a.fmt == BYBYCU_FMT_Q4B32 && a.x_dtype == BYBYCU_DT_BF16 && a.M >= 8 && a.M <= 16 &&
+    // Except where the GEMV's cost per row is highest: rows from 8 on with K >= 8192
+    // (4096 x 11008 at M = 16: 21.9 us on the tensor cores against 31.9 for bf16 rows, 24.1
+    // against 35.7 for fp32 rows; at M = 8 21.8 against 22.6 and 22.4 against 24.5; at M = 4
+    // the GEMV wins), and from 12 on with N >= 65536 (128256 x 4096 at M = 16: 120 against
+    // 158 us for bf16 rows, 129 against 182 for fp32 rows; fp32 rows at M = 8: 124 against 112).
+    const bool tc_rows = a.fmt == BYBYCU_FMT_Q4B32 && a.M >= 8 && a.M <= 16 &&
                          (a.K >= 8192 || (a.M >= 12 && a.N >= 65536));
     const bool gemv_rows = !tc_rows && a.M <= 16;
     if (gemv_rows && gemv_supports(a)) *route = BYBYCU_ROUTE_GEMV;

@@ -61,7 +61,7 @@ extern "C" {
 
 /* kernel routes */
 #define BYBYCU_ROUTE_AUTO 0   /* GEMV for M <= 16, tensor-core GEMM above;
-                                 format 2 with bf16 x: tensor cores from M = 8 when K >= 8192
+                                 format 2: tensor cores from M = 8 when K >= 8192
                                  and from M = 12 when N >= 65536 */
 #define BYBYCU_ROUTE_GEMV 1   /* decode GEMV: TMA-streamed weights, register dequant */
 #define BYBYCU_ROUTE_TC 2     /* prefill GEMM: tcgen05 MMAs, fp32 accumulators in TMEM */

@@ -155,7 +155,9 @@ def test_auto_route_prefill_is_tc(oracle_mod):
     assert gb.route_for(2, 8, 11008, 4096) == _lib.ROUTE_TC                   # long rows
     assert gb.route_for(2, 11, 4096, 128256) == _lib.ROUTE_GEMV
     assert gb.route_for(2, 12, 4096, 128256) == _lib.ROUTE_TC                 # very wide output
-    assert gb.route_for(2, 16, 11008, 4096, _lib.DT_F32) == _lib.ROUTE_GEMV
+    assert gb.route_for(2, 7, 11008, 4096, _lib.DT_F32) == _lib.ROUTE_GEMV
+    assert gb.route_for(2, 8, 11008, 4096, _lib.DT_F32) == _lib.ROUTE_TC     # long fp32 rows too
+    assert gb.route_for(2, 12, 4096, 128256, _lib.DT_F32) == _lib.ROUTE_TC
     assert gb.route_for(2, 32, 4096, 4096) == _lib.ROUTE_TC                  # bf16 rows
     assert gb.route_for(2, 32, 4096, 4096, _lib.DT_F32) == _lib.ROUTE_TC     # two fp16 terms per fp32 value
     assert gb.route_for(2, 33, 4096, 4096, _lib.DT_F32) == _lib.ROUTE_TC

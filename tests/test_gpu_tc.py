@@ -127,6 +127,23 @@ def test_tc_fp32_activations_per_element(M, K, N, oracle_mod, parity_log):
     assert torch.equal(torch.from_numpy(got).to(torch.bfloat16), b16.cpu())
 
 
+@pytest.mark.parametrize("M,N", [(8, 300), (13, 96), (16, 520)])
+def test_auto_fp32_rows_long_k_per_element(M, N, oracle_mod, parity_log):
+    """8 to 16 fp32 rows with K >= 8192: AUTO takes the tensor cores, whose split rows (16 to
+    32 fp16 rows) run the 16- and 32-token tiles; per element against the oracle."""
+    O = oracle_mod
+    K = 8192
+    p, s = O.gen_q4b32(N, K, seed=O.Xorshift32.SEED + 3 * M)
+    xf = O.gen_x_f32(M, K, seed=O.Xorshift32.SEED + 11 + M)
+    slot, sb = q4_slot(p, s)
+    assert gb.route_for(2, M, K, N, _lib.DT_F32) == _lib.ROUTE_TC
+    want = O.tile_gemm_q4b32(xf, p, s, M, K, N, threads=8)
+    got = run(2, M, K, N, dev(xf), slot, scale_base=sb).cpu().numpy()
+    parity_log.append((f"{M}x{K}x{N} fp32 x, AUTO (TC, two fp16 terms per activation)", elem_err(want, got), ELEM_TOL))
+    assert_close(want, got, TC_TOL, ELEM_TOL, what=f"fp32 x M={M} K={K} N={N}")
+    assert _lib.device_error() == 0
+
+
 def test_tc_bf16_output_is_rounded_f32_output(oracle_mod):
     O = oracle_mod
     M, K, N = 300, 1024, 256

@@ -578,8 +578,13 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
     // a store instruction then writes 4 (fp32) or 8 (bf16) output rows of 128 / 64 contiguous
     // bytes instead of one strided value per lane (the strided form took ~1.2 us per chunk of
     // 32 tokens at 4096 columns, 4x the same stores into a contiguous block).
+    // With a gather the same 16-byte segments go to every peer's buffer (fp32 outputs).
     const int esz = p.out_bf16 ? 2 : 4;
-    const bool staged = epi_gen != nullptr && !p.x_split && p.pg.world <= 1 &&
+    bool peers_aligned = !p.out_bf16;
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+        if (r < p.pg.world && reinterpret_cast<uintptr_t>(p.pg.out[r]) % 16 != 0) peers_aligned = false;
+    const bool staged = epi_gen != nullptr && !p.x_split && (p.pg.world <= 1 || peers_aligned) &&
                         reinterpret_cast<uintptr_t>(p.out) % 16 == 0 && (p.out_ld * esz) % 16 == 0 &&
                         (p.out_col0 * esz) % 16 == 0;
     uint8_t* const epi = staged ? epi_gen + quarter * (kChunk * 32 * 4) : nullptr;
@@ -695,9 +700,16 @@ __device__ __forceinline__ void epilogue_tiles_t(const Params& p, uint32_t tmem,
 #pragma unroll
                     for (int r = 0; r < kChunk / 4; ++r) {
                         const int j = r * 4 + (lane >> 3), f = (lane & 7) * 4;
-                        if (j < nt)
-                            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + row0 + j * p.out_ld + f) =
-                                *reinterpret_cast<const float4*>(st + j * 32 + f);
+                        if (j < nt) {
+                            const float4 val = *reinterpret_cast<const float4*>(st + j * 32 + f);
+                            const int64_t oi = row0 + j * p.out_ld + f;
+                            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + oi) = val;
+                            if (p.pg.world > 1)   // the fused all-gather: every peer's buffer
+#pragma unroll
+                                for (int q = 0; q < kMaxRanks; ++q)
+                                    if (q < p.pg.world && q != p.pg.rank)
+                                        *reinterpret_cast<float4*>(p.pg.out[q] + oi) = val;
+                        }
                     }
                 }
                 __syncwarp();   // the block is read before the next chunk overwrites it

@@ -574,7 +574,7 @@ constexpr int kM1I8 = 2;     // s8 MMAs on 16 q and two-digit fixed-point activa
 // blocks' dependency chains overlap.  An fp32 row keeps 128 bytes per block; its digits take
 // the first 64 of them, and the last 64 hold a second image of what the first leaves out:
 // R = x * 2^(140 - E) - X (exact, |R| <= 1/2) as X2 = rint(R * 2^15) in the same two-digit
-// form, so the pair carries x to 2^-30 of the block's largest value (fp32 keeps 2^-24 of
+// form, so the pair carries x to 2^-29 of the block's largest value (fp32 keeps 2^-24 of
 // each value).  Lane t's loads at bytes 16t.. and 64+16t.. feed the block's exponent, which
 // the quad shuffles before any lane stores, so no store lands on bytes still unread.
 template <bool XF32>

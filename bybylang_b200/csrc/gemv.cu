@@ -1251,7 +1251,7 @@ int launch_gemv(const GemmArgs& a, const PeerGather* pg) {
     const int n_tiles = static_cast<int>(ceil_div(a.N, kTileRows));
     const int grid = std::min(n_tiles, dev.sm_count);
     // The M = 1 kernel takes bf16 rows in every operand mode and fp32 rows in the integer mode
-    // (two fixed-point images, 2^-30 of each block's largest value).  The fp16 / bf16 modes
+    // (two fixed-point images, 2^-29 of each block's largest value).  The fp16 / bf16 modes
     // have no fp32 form: there fp32 rows take the general kernel's two bf16 terms.
     const int want_mode = a.variant >= kM1Bf16 && a.variant <= kM1I8 ? a.variant : m1_mode();
     const int mode = want_mode == kM1I8 && a.K > 32768 ? kM1F16 : want_mode;
